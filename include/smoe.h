@@ -1,0 +1,162 @@
+/* smoe.h - C ABI of the B200-native StrataMetal MoE block (sm_100a).
+ *
+ * Every entry point takes device pointers, plain sizes and an explicit, non-null CUDA stream
+ * (cudaStream_t passed as void*), enqueues work on that stream, never synchronises and never
+ * allocates.  Scratch comes from a caller-owned arena sized by the matching *_scratch_bytes().
+ *
+ * Each declaration names the reference interface it replaces (file:line inside the StrataMetal tree).
+ * Argument meaning and error behaviour follow those interfaces:
+ *   - negative counts, k > 64, n_expert > 1024, k > n_expert, an unsupported type or a bad multiple
+ *     return SMOE_INVALID_ARG / SMOE_UNSUPPORTED (the reference throws MetalError: router.mm:33-37,
+ *     iq.mm:148-158, moe_combine.mm:31-38);
+ *   - a zero count returns SMOE_OK before any launch and leaves every output untouched
+ *     (router_parity.cpp:220-225, moe_combine_parity.cpp:168-176, iq_parity.cpp:560-569);
+ *   - outputs are never written past their extent.
+ * A kernel that gives up on a bounded wait, or meets a routed id outside the pool, records a code in the
+ * per-device status word read by smoe_device_status(). */
+#ifndef SMOE_H
+#define SMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    SMOE_OK = 0,
+    SMOE_INVALID_ARG = 1,
+    SMOE_UNSUPPORTED = 2,
+    SMOE_CUDA_ERROR = 3,
+    SMOE_DEVICE_TIMEOUT = 4
+} smoe_status;
+
+enum { SMOE_Q2_0 = 42, SMOE_IQ2_S = 22 };
+
+/* Message of the last non-OK status returned on this thread ("" after an OK call). */
+const char* smoe_last_error(void);
+
+/* Reads (and with clear != 0 resets) the device status word of the current device after a sync:
+ * 0 ok, 1 a bounded wait ran out, 2 a routed id outside the pool was met.
+ * Replaces the reference's std::exit on CUDA errors (src/kernels/cuda/bf16_gemv.cu:68-80). */
+unsigned smoe_device_status(int clear);
+
+/* ---- geometry ------------------------------------------------------------------------------------ */
+
+/* iq_row_bytes (metal/include/strata/metal/iq.hpp:41, iq.mm:124-129): bytes of one row of n values; 0 for an
+ * unsupported type or a bad multiple.  Q2_0: 18 B / 64 values; IQ2_S: 82 B / 256. */
+size_t smoe_row_bytes(int ggml_type, int64_t n);
+/* iq_q8_1_bytes (iq.hpp:43, iq.mm:131-134): 36 B per 32 values; 0 unless n is a positive multiple of 32. */
+size_t smoe_q8_1_bytes(int64_t n);
+
+/* ---- stage entry points (one reference kernel each) ---------------------------------------------- */
+
+/* f32_to_bf16_bulk (metal/include/strata/metal/elementwise.hpp:27; layer_exec.cpp:470):
+ * round-to-nearest-even bf16 bits of n floats (bf16_bits.hpp:37-47). */
+smoe_status smoe_f32_to_bf16_bulk(const float* x, uint16_t* y, int64_t n, void* stream);
+
+/* bf16_gemv (metal/include/strata/metal/bf16_gemv.hpp:83-89, bf16_gemv.mm:195-203), n_col columns:
+ * y[c][o] = sum_i f32(x[c][i]) * f32(w[o][i]).  The sum is accumulated in fp64 and rounded once, which is
+ * the host oracle's bf16_dot (pack_parity.cpp:3795-3799); w is [n_out][n_in] row-major; n_in % 8 == 0. */
+smoe_status smoe_bf16_gemv(const uint16_t* x, const uint16_t* w, float* y, int64_t n_in, int64_t n_out,
+                           int64_t n_col, void* stream);
+
+/* router_top10 (metal/include/strata/metal/router.hpp:14-16, router.mm:32-49; CUDA contract
+ * include/strata/kernels/router_top10.hpp:20-21, native_router.hpp:17-18): per token softmax over all
+ * n_expert logits (fp64), top-k by probability with the lower index on a tie, weights divided by
+ * max(sum of the k, 2^-14).  logits [n_tokens][n_expert] f32; ids, weights [n_tokens][k]. */
+smoe_status smoe_router_top10(const float* logits, int n_tokens, int n_expert, int k, int32_t* ids, float* weights,
+                              void* stream);
+
+/* The router as one call (a1 + a2 + a3 of the block, layer_exec.cpp:470-472): bf16 rounding of x, the
+ * fp64-accumulated bf16 GEMV against w_router [n_expert][n_embd] into logits [n_tokens][n_expert], and
+ * router_top10 on them.  n_embd % 8 == 0. */
+smoe_status smoe_router(const float* x, const uint16_t* w_router, int n_tokens, int n_embd, int n_expert, int k,
+                        float* logits, int32_t* ids, float* weights, void* stream);
+
+/* iq_quantize_q8_1 (iq.hpp:46, iq.mm:138-146; kernel iq.metal:597-627): n floats (a multiple of 32) into
+ * n/32 q8_1 blocks. */
+smoe_status smoe_iq_quantize_q8_1(const float* x, int64_t n, uint8_t* y, void* stream);
+
+/* iq_mmvq (iq.hpp:50-51, iq.mm:148-169; CUDA contract include/strata/kernels/iq_kernels.hpp:30):
+ * y[c * n_out + r] = W[r] . x[c] for n_col q8_1 columns, W n_out rows of ggml_type over n_in values.
+ * The sum of a row follows the reference's 32-lane order (iq.metal:459-514) and is bitwise its host
+ * reference (iq_parity.cpp:275-292). */
+smoe_status smoe_iq_mmvq(int ggml_type, const uint8_t* w, const uint8_t* x_q8, int64_t n_in, int64_t n_out,
+                         int64_t n_col, float* y, void* stream);
+
+/* iq_swiglu_q8 (iq.hpp:54, iq.mm:201-210; kernel iq.metal:630-663): silu(gate) * up, stored as q8_1. */
+smoe_status smoe_iq_swiglu_q8(const float* gate, const float* up, int64_t n, uint8_t* y, void* stream);
+
+/* moe_combine (metal/include/strata/metal/moe_combine.hpp:14-15, moe_combine.mm:31-48; CUDA contract
+ * native_moe.hpp:15-20, shared_expert.hpp:97-101) for n_tok tokens:
+ * y[t][j] = sum_e w[t][e] * parts[t][e][j] + shared[t][j], summed in fp64 in router order and rounded once
+ * (pack_parity.cpp:8607-8616).  shared may be NULL; it is added plain, not router weighted. */
+smoe_status smoe_moe_combine(const float* parts, const float* weights, const float* shared, float* y,
+                             int64_t n_embd, int k, int n_tok, void* stream);
+
+/* fused::group (include/strata/prefill/moe_fused.hpp:46-50): routing ids [n_tok][k] -> expert groups.
+ * Writes, inside `scratch` (smoe_moe_group_scratch_bytes), counts[n_expert], offsets[n_expert + 1] and the
+ * active-expert list; slot[i] = the grouped row of pair i (i = t * k + j); src[row] = its token.  Rows of
+ * one expert are in token order (the reference leaves that order free; this build fixes it). */
+size_t smoe_moe_group_scratch_bytes(int n_tok, int k, int n_expert);
+smoe_status smoe_moe_group(const int32_t* ids, int n_tok, int k, int n_expert, void* scratch, int32_t* slot,
+                           int32_t* src, void* stream);
+
+/* ---- the block ----------------------------------------------------------------------------------- */
+
+/* One MoE layer's weights on the device, named as the GGUF names them (layer_exec.cpp:369-452,
+ * expert_spans :109-123).  Routed planes hold n_expert experts back to back; expert e's gate rows start
+ * at gate + e * n_ff * smoe_row_bytes(gu_type, n_embd). */
+typedef struct smoe_layer {
+    int n_embd, n_ff, n_expert, k;
+    int gu_type, d_type;              /* routed gate/up type (Q2_0 or IQ2_S), down type (Q2_0) */
+    const uint16_t* router;           /* ffn_gate_inp.weight       [n_expert][n_embd] bf16 */
+    const uint8_t* gate;              /* ffn_gate_exps.weight      [n_expert][n_ff rows] */
+    const uint8_t* up;                /* ffn_up_exps.weight        [n_expert][n_ff rows] */
+    const uint8_t* down;              /* ffn_down_exps.weight      [n_expert][n_embd rows] */
+    int has_shared;
+    int sg_type, su_type, sd_type;
+    const uint8_t* sgate;             /* ffn_gate_shexp.weight     [n_ff rows over n_embd] */
+    const uint8_t* sup;               /* ffn_up_shexp.weight       [n_ff rows over n_embd] */
+    const uint8_t* sdown;             /* ffn_down_shexp.weight     [n_embd rows over n_ff] */
+    const uint16_t* gate_inp_shexp;   /* ffn_gate_inp_shexp.weight [n_embd] bf16 */
+} smoe_layer;
+
+/* Optional stage outputs, the device-side FfnTrace (metal/include/strata/metal/layer_exec.hpp:100-109).
+ * Any pointer may be NULL.  Shapes for n_tokens tokens. */
+typedef struct smoe_trace {
+    float* logits;     /* [T][n_expert] router logits (FfnTrace::route) */
+    int32_t* ids;      /* [T][k] */
+    float* weights;    /* [T][k] (FfnTrace::route_w) */
+    uint8_t* xq;       /* [T][n_embd / 32 * 36] q8_1 image of x (FfnTrace::exq) */
+    float* parts;      /* [T][k][n_embd] routed expert outputs in router order (FfnTrace::edown) */
+    float* shared;     /* [T][n_embd] gated shared-expert output (FfnTrace::shared) */
+} smoe_trace;
+
+/* Stage timing, the device-side counterpart of the reference's per-(layer, stage) event pairs
+ * (include/strata/core/layer.hpp:317-337).  While set (n >= SMOE_STAGES, events are cudaEvent_t),
+ * smoe_moe_forward records events[i] on its stream when stage i has been enqueued:
+ * 0 router GEMV, 1 top-k + q8_1 of x, 2 dispatch, 3 gate/up + SwiGLU, 4 down, 5 combine.
+ * The setting is per host thread; NULL or n = 0 turns it off. */
+enum { SMOE_STAGES = 6 };
+void smoe_set_stage_events(void** events, int n);
+
+/* Validates the layer's geometry and types: SMOE_OK when smoe_moe_forward can run it. */
+smoe_status smoe_layer_check(const smoe_layer* L);
+
+/* Scratch the block needs for up to max_tokens tokens. */
+size_t smoe_moe_scratch_bytes(const smoe_layer* L, int max_tokens);
+
+/* FfnExec::run's MoE block (layer_exec.cpp:462-563 between gr_read and gr_write; upstream moe_route +
+ * moe_shared + moe_combine_parts, include/strata/core/layer.hpp:170-190): x [n_tokens][n_embd] f32 ->
+ * out [n_tokens][n_embd] f32 = router -> dispatch -> routed experts (gate/up, SwiGLU, q8_1, down) ->
+ * sigmoid-gated shared expert -> combine.  The shared expert is added only when the layer has one. */
+smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, float* out, void* scratch,
+                             size_t scratch_bytes, const smoe_trace* trace, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

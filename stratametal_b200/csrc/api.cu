@@ -1,0 +1,368 @@
+// api.cu - the C ABI (include/smoe.h): argument checks that mirror the reference's host API, scratch
+// layout, and the MoE block's launch sequence.
+#include "../../include/smoe.h"
+#include "common.cuh"
+#include "kernels.cuh"
+
+#include <string>
+
+namespace smoe {
+namespace {
+
+thread_local std::string g_err;
+thread_local cudaEvent_t* g_stage_events = nullptr;
+
+cudaError_t mark(int stage, cudaStream_t s) {
+    return g_stage_events ? cudaEventRecord(g_stage_events[stage], s) : cudaSuccess;
+}
+
+smoe_status fail(smoe_status s, const std::string& msg) {
+    g_err = msg;
+    return s;
+}
+smoe_status ok() {
+    g_err.clear();
+    return SMOE_OK;
+}
+smoe_status cuda_fail(cudaError_t e, const char* where) {
+    return fail(SMOE_CUDA_ERROR, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+int block_values(int t) { return t == kQ2_0 ? 64 : t == kIQ2_S ? 256 : 0; }
+size_t block_bytes(int t) { return t == kQ2_0 ? 18 : t == kIQ2_S ? 82 : 0; }
+
+size_t row_bytes(int t, int64_t n) {
+    const int v = block_values(t);
+    if (v == 0 || n <= 0 || n % v) return 0;
+    return (size_t) (n / v) * block_bytes(t);
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+size_t up256(size_t n) { return (n + 255) & ~(size_t) 255; }
+
+// Scratch regions of the block for T tokens.
+struct Layout {
+    size_t xq, logits, sh_logit, ids, w, slot, slot_token, tables, hq, parts, total;
+};
+
+Layout layout_of(const smoe_layer* L, int T) {
+    Layout o;
+    const size_t H = (size_t) L->n_embd, F = (size_t) L->n_ff, E = (size_t) L->n_expert, K = (size_t) L->k;
+    const size_t rows = (size_t) T * K + (L->has_shared ? (size_t) T : 0);
+    size_t at = 0;
+    o.xq = at; at += up256((size_t) T * (H / 32) * kQ8Block);
+    o.logits = at; at += up256((size_t) T * E * 4);
+    o.sh_logit = at; at += up256((size_t) T * 4);
+    o.ids = at; at += up256((size_t) T * K * 4);
+    o.w = at; at += up256((size_t) T * K * 4);
+    o.slot = at; at += up256((size_t) T * K * 4);
+    o.slot_token = at; at += up256((size_t) T * K * 4);
+    o.tables = at; at += group_tables_bytes((int) E);
+    o.hq = at; at += up256(rows * (F / 32) * kQ8Block);
+    o.parts = at; at += up256(rows * H * 4);
+    o.total = at;
+    return o;
+}
+
+smoe_status check_layer(const smoe_layer* L) {
+    if (!L) return fail(SMOE_INVALID_ARG, "layer is null");
+    if (L->n_embd <= 0 || L->n_ff <= 0 || L->n_expert <= 0 || L->k <= 0)
+        return fail(SMOE_INVALID_ARG, "layer: sizes must be positive");
+    if (L->k > kMaxK) return fail(SMOE_INVALID_ARG, "layer: k exceeds 64");
+    if (L->n_expert > kMaxExperts) return fail(SMOE_INVALID_ARG, "layer: n_expert exceeds 1024");
+    if (L->k > L->n_expert) return fail(SMOE_INVALID_ARG, "layer: k exceeds n_expert");
+    if (!row_bytes(L->gu_type, L->n_embd) || !row_bytes(L->d_type, L->n_ff))
+        return fail(SMOE_UNSUPPORTED, "layer: routed types must be Q2_0 or IQ2_S with whole blocks per row");
+    if (L->n_ff % 32 || L->n_embd % 64) return fail(SMOE_INVALID_ARG, "layer: n_ff % 32 and n_embd % 64 must be 0");
+    if (L->n_embd > 4096 || L->n_ff > 4096) return fail(SMOE_UNSUPPORTED, "layer: n_embd and n_ff are at most 4096");
+    if (!L->router || !L->gate || !L->up || !L->down) return fail(SMOE_INVALID_ARG, "layer: a routed plane is null");
+    if (!aligned(L->router, 16) || !aligned(L->gate, 16) || !aligned(L->up, 16) || !aligned(L->down, 16))
+        return fail(SMOE_INVALID_ARG, "layer: planes must be 16-byte aligned");
+    if (L->has_shared) {
+        if (!row_bytes(L->sg_type, L->n_embd) || !row_bytes(L->su_type, L->n_embd) || !row_bytes(L->sd_type, L->n_ff))
+            return fail(SMOE_UNSUPPORTED, "layer: shared types must be Q2_0 or IQ2_S with whole blocks per row");
+        if (L->sg_type != L->su_type) return fail(SMOE_UNSUPPORTED, "layer: shared gate and up types differ");
+        if (!L->sgate || !L->sup || !L->sdown || !L->gate_inp_shexp)
+            return fail(SMOE_INVALID_ARG, "layer: a shared plane is null");
+        if (!aligned(L->sgate, 16) || !aligned(L->sup, 16) || !aligned(L->sdown, 16) ||
+            !aligned(L->gate_inp_shexp, 16))
+            return fail(SMOE_INVALID_ARG, "layer: shared planes must be 16-byte aligned");
+    }
+    return SMOE_OK;
+}
+
+}  // namespace
+}  // namespace smoe
+
+using namespace smoe;
+
+extern "C" {
+
+const char* smoe_last_error(void) { return g_err.c_str(); }
+
+void smoe_set_stage_events(void** events, int n) {
+    g_stage_events = (events && n >= SMOE_STAGES) ? reinterpret_cast<cudaEvent_t*>(events) : nullptr;
+}
+
+unsigned smoe_device_status(int clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_smoe_status, sizeof v) != cudaSuccess) return 0xFFFFFFFFu;
+    if (clear) {
+        const unsigned z = 0;
+        cudaMemcpyToSymbol(g_smoe_status, &z, sizeof z);
+    }
+    return v;
+}
+
+size_t smoe_row_bytes(int ggml_type, int64_t n) { return row_bytes(ggml_type, n); }
+
+size_t smoe_q8_1_bytes(int64_t n) { return (n <= 0 || n % 32) ? 0 : (size_t) (n / 32) * kQ8Block; }
+
+smoe_status smoe_f32_to_bf16_bulk(const float* x, uint16_t* y, int64_t n, void* stream) {
+    if (n < 0) return fail(SMOE_INVALID_ARG, "f32_to_bf16_bulk: negative size");
+    if (n == 0) return ok();
+    if (!stream) return fail(SMOE_INVALID_ARG, "f32_to_bf16_bulk: a non-null stream is required");
+    if (!x || !y) return fail(SMOE_INVALID_ARG, "f32_to_bf16_bulk: null buffer");
+    const cudaError_t e = launch_f32_to_bf16(x, y, n, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "f32_to_bf16_bulk");
+}
+
+smoe_status smoe_bf16_gemv(const uint16_t* x, const uint16_t* w, float* y, int64_t n_in, int64_t n_out,
+                           int64_t n_col, void* stream) {
+    // bf16_gemv.mm:195-200: non-positive sizes return without a launch; sizes past int32 throw
+    if (n_in <= 0 || n_out <= 0 || n_col <= 0) return ok();
+    if (n_in > 0x7fffffff || n_out > 0x7fffffff || n_col > 0x7fffffff)
+        return fail(SMOE_INVALID_ARG, "bf16_gemv: dimension does not fit in int32");
+    if (n_in % 8) return fail(SMOE_INVALID_ARG, "bf16_gemv: n_in must be a multiple of 8");
+    if (n_in > 16384) return fail(SMOE_UNSUPPORTED, "bf16_gemv: n_in is at most 16384");
+    if (!stream) return fail(SMOE_INVALID_ARG, "bf16_gemv: a non-null stream is required");
+    if (!x || !w || !y || !aligned(x, 16) || !aligned(w, 16))
+        return fail(SMOE_INVALID_ARG, "bf16_gemv: x and w must be non-null and 16-byte aligned");
+    const cudaError_t e = launch_bf16_gemv(x, false, w, nullptr, y, nullptr, (int) n_col, (int) n_in, (int) n_out,
+                                           (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "bf16_gemv");
+}
+
+static smoe_status check_router_args(int n_tokens, int n_expert, int k, bool* noop) {
+    // router.mm:32-37
+    *noop = false;
+    if (n_tokens < 0 || n_expert < 0 || k < 0) return fail(SMOE_INVALID_ARG, "router_top10: negative size");
+    if (n_tokens == 0 || n_expert == 0 || k == 0) {
+        *noop = true;
+        return ok();
+    }
+    if (k > kMaxK) return fail(SMOE_INVALID_ARG, "router_top10: k exceeds 64");
+    if (n_expert > kMaxExperts) return fail(SMOE_INVALID_ARG, "router_top10: n_expert exceeds 1024");
+    if (k > n_expert) return fail(SMOE_INVALID_ARG, "router_top10: k exceeds n_expert");
+    return ok();
+}
+
+smoe_status smoe_router_top10(const float* logits, int n_tokens, int n_expert, int k, int32_t* ids, float* weights,
+                              void* stream) {
+    bool noop;
+    const smoe_status st = check_router_args(n_tokens, n_expert, k, &noop);
+    if (st != SMOE_OK || noop) return st;
+    if (!stream) return fail(SMOE_INVALID_ARG, "router_top10: a non-null stream is required");
+    if (!logits || !ids || !weights) return fail(SMOE_INVALID_ARG, "router_top10: null buffer");
+    const cudaError_t e = launch_router_topk(logits, n_tokens, n_expert, k, ids, weights, nullptr, nullptr, 0,
+                                             (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "router_top10");
+}
+
+smoe_status smoe_router(const float* x, const uint16_t* w_router, int n_tokens, int n_embd, int n_expert, int k,
+                        float* logits, int32_t* ids, float* weights, void* stream) {
+    bool noop;
+    smoe_status st = check_router_args(n_tokens, n_expert, k, &noop);
+    if (st != SMOE_OK || noop) return st;
+    if (n_embd <= 0 || n_embd % 8 || n_embd > 16384)
+        return fail(SMOE_INVALID_ARG, "router: n_embd must be a positive multiple of 8, at most 16384");
+    if (!stream) return fail(SMOE_INVALID_ARG, "router: a non-null stream is required");
+    if (!x || !w_router || !logits || !ids || !weights || !aligned(w_router, 16))
+        return fail(SMOE_INVALID_ARG, "router: null or misaligned buffer");
+    cudaError_t e = launch_bf16_gemv(x, true, w_router, nullptr, logits, nullptr, n_tokens, n_embd, n_expert,
+                                     (cudaStream_t) stream);
+    if (e != cudaSuccess) return cuda_fail(e, "router");
+    e = launch_router_topk(logits, n_tokens, n_expert, k, ids, weights, nullptr, nullptr, 0, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "router");
+}
+
+smoe_status smoe_iq_quantize_q8_1(const float* x, int64_t n, uint8_t* y, void* stream) {
+    // iq.mm:138-141: n <= 0 returns; a partial block throws
+    if (n <= 0) return ok();
+    if (n % 32) return fail(SMOE_INVALID_ARG, "iq_quantize_q8_1: length must be a multiple of 32");
+    if (!stream) return fail(SMOE_INVALID_ARG, "iq_quantize_q8_1: a non-null stream is required");
+    if (!x || !y) return fail(SMOE_INVALID_ARG, "iq_quantize_q8_1: null buffer");
+    const cudaError_t e = launch_quant_q8_1(x, n, y, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "iq_quantize_q8_1");
+}
+
+smoe_status smoe_iq_mmvq(int ggml_type, const uint8_t* w, const uint8_t* x_q8, int64_t n_in, int64_t n_out,
+                         int64_t n_col, float* y, void* stream) {
+    // iq.mm:150-158
+    if (n_in == 0 || n_out == 0 || n_col == 0) return ok();
+    if (n_in < 0 || n_out < 0 || n_col < 0) return fail(SMOE_INVALID_ARG, "iq_mmvq: negative size");
+    if (!block_values(ggml_type)) return fail(SMOE_UNSUPPORTED, "iq_mmvq: type is not Q2_0 or IQ2_S");
+    if (!row_bytes(ggml_type, n_in)) return fail(SMOE_INVALID_ARG, "iq_mmvq: n_in is not a whole number of blocks");
+    if (n_in > 4096) return fail(SMOE_UNSUPPORTED, "iq_mmvq: n_in is at most 4096");
+    if (n_out > 0x7fffffff || n_col > 0x7fffffff) return fail(SMOE_INVALID_ARG, "iq_mmvq: size does not fit in int");
+    if (!stream) return fail(SMOE_INVALID_ARG, "iq_mmvq: a non-null stream is required");
+    if (!w || !x_q8 || !y || !aligned(w, 16) || !aligned(x_q8, 4))
+        return fail(SMOE_INVALID_ARG, "iq_mmvq: w must be 16-byte and x 4-byte aligned");
+    GroupView g{};
+    g.single_cols = (int) n_col;
+    const Matrix m{w, 0, ggml_type};
+    const cudaError_t e = launch_expert_down(m, m, g, x_q8, 0, y, n_out, (int) n_in, (int) n_out,
+                                             (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "iq_mmvq");
+}
+
+smoe_status smoe_iq_swiglu_q8(const float* gate, const float* up, int64_t n, uint8_t* y, void* stream) {
+    // iq.mm:201-203
+    if (n == 0) return ok();
+    if (n < 0 || n % 32) return fail(SMOE_INVALID_ARG, "iq_swiglu_q8: length must be a positive multiple of 32");
+    if (!stream) return fail(SMOE_INVALID_ARG, "iq_swiglu_q8: a non-null stream is required");
+    if (!gate || !up || !y) return fail(SMOE_INVALID_ARG, "iq_swiglu_q8: null buffer");
+    const cudaError_t e = launch_swiglu_q8(gate, up, n, y, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "iq_swiglu_q8");
+}
+
+smoe_status smoe_moe_combine(const float* parts, const float* weights, const float* shared, float* y,
+                             int64_t n_embd, int k, int n_tok, void* stream) {
+    // moe_combine.mm:31-34
+    if (n_embd < 0 || k < 0 || n_tok < 0) return fail(SMOE_INVALID_ARG, "moe_combine: negative size");
+    if (n_embd == 0 || k == 0 || n_tok == 0) return ok();
+    if (k > kMaxK) return fail(SMOE_INVALID_ARG, "moe_combine: k exceeds 64");
+    if (!stream) return fail(SMOE_INVALID_ARG, "moe_combine: a non-null stream is required");
+    if (!parts || !weights || !y) return fail(SMOE_INVALID_ARG, "moe_combine: null buffer");
+    const cudaError_t e = launch_combine(parts, nullptr, weights, shared, nullptr, y, nullptr, n_embd, k, n_tok,
+                                         n_embd, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "moe_combine");
+}
+
+size_t smoe_moe_group_scratch_bytes(int n_tok, int k, int n_expert) {
+    (void) n_tok;
+    (void) k;
+    return (n_expert > 0 && n_expert <= kMaxExperts) ? group_tables_bytes(n_expert) : 0;
+}
+
+smoe_status smoe_moe_group(const int32_t* ids, int n_tok, int k, int n_expert, void* scratch, int32_t* slot,
+                           int32_t* src, void* stream) {
+    if (n_tok < 0 || k < 0 || n_expert < 0) return fail(SMOE_INVALID_ARG, "moe_group: negative size");
+    if (n_tok == 0 || k == 0 || n_expert == 0) return ok();
+    if (k > kMaxK || n_expert > kMaxExperts) return fail(SMOE_INVALID_ARG, "moe_group: k > 64 or n_expert > 1024");
+    if (!stream) return fail(SMOE_INVALID_ARG, "moe_group: a non-null stream is required");
+    if (!ids || !scratch || !slot || !aligned(scratch, 4)) return fail(SMOE_INVALID_ARG, "moe_group: null buffer");
+    const cudaError_t e = launch_group(ids, n_tok, k, n_expert, group_tables_at(scratch, n_expert), slot, src,
+                                       (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "moe_group");
+}
+
+smoe_status smoe_layer_check(const smoe_layer* L) {
+    const smoe_status st = check_layer(L);
+    return st == SMOE_OK ? ok() : st;
+}
+
+size_t smoe_moe_scratch_bytes(const smoe_layer* L, int max_tokens) {
+    if (check_layer(L) != SMOE_OK || max_tokens < 0) return 0;
+    return layout_of(L, max_tokens).total;
+}
+
+smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, float* out, void* scratch,
+                             size_t scratch_bytes, const smoe_trace* trace, void* stream) {
+    smoe_status st = check_layer(L);
+    if (st != SMOE_OK) return st;
+    if (n_tokens < 0) return fail(SMOE_INVALID_ARG, "moe_forward: negative token count");
+    if (n_tokens == 0) return ok();
+    if (!stream) return fail(SMOE_INVALID_ARG, "moe_forward: a non-null stream is required");
+    if (!x || !out || !scratch || !aligned(scratch, 256))
+        return fail(SMOE_INVALID_ARG, "moe_forward: null buffer or scratch not 256-byte aligned");
+    const Layout lo = layout_of(L, n_tokens);
+    if (scratch_bytes < lo.total) return fail(SMOE_INVALID_ARG, "moe_forward: scratch is too small");
+    cudaStream_t s = (cudaStream_t) stream;
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    const int T = n_tokens, H = L->n_embd, F = L->n_ff, E = L->n_expert, K = L->k;
+    uint8_t* xq = base + lo.xq;
+    float* logits = reinterpret_cast<float*>(base + lo.logits);
+    float* sh_logit = reinterpret_cast<float*>(base + lo.sh_logit);
+    int32_t* ids = reinterpret_cast<int32_t*>(base + lo.ids);
+    float* w = reinterpret_cast<float*>(base + lo.w);
+    int32_t* slot = reinterpret_cast<int32_t*>(base + lo.slot);
+    int32_t* slot_tok = reinterpret_cast<int32_t*>(base + lo.slot_token);
+    const GroupTables tabs = group_tables_at(base + lo.tables, E);
+    uint8_t* hq = base + lo.hq;
+    float* parts = reinterpret_cast<float*>(base + lo.parts);
+
+    cudaError_t e = launch_bf16_gemv(x, true, L->router, L->has_shared ? L->gate_inp_shexp : nullptr, logits,
+                                     sh_logit, T, H, E, s);
+    if (e == cudaSuccess) e = mark(0, s);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_forward: router");
+    e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s);
+    if (e == cudaSuccess) e = mark(1, s);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_forward: top-k");
+    e = launch_group(ids, T, K, E, tabs, slot, slot_tok, s);
+    if (e == cudaSuccess) e = mark(2, s);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_forward: dispatch");
+
+    GroupView g{};
+    g.offsets = tabs.offsets;
+    g.active = tabs.active;
+    g.n_active = tabs.n_active;
+    g.slot_token = slot_tok;
+    g.max_active = T * K < E ? T * K : E;
+    g.shared_base = T * K;
+    const int64_t gu_stride = (int64_t) F * (int64_t) row_bytes(L->gu_type, H);
+    const int64_t d_stride = (int64_t) H * (int64_t) row_bytes(L->d_type, F);
+    const Matrix mg{L->gate, gu_stride, L->gu_type}, mu{L->up, gu_stride, L->gu_type}, md{L->down, d_stride, L->d_type};
+    const Matrix sg{L->sgate, 0, L->sg_type}, su{L->sup, 0, L->su_type}, sd{L->sdown, 0, L->sd_type};
+
+    // gate/up: the shared expert rides in the routed launch when its type matches
+    const bool sh = L->has_shared != 0;
+    const bool gu_same = sh && L->sg_type == L->gu_type;
+    GroupView g1 = g;
+    g1.shared_slots = gu_same ? T : 0;
+    e = launch_expert_gate_up(mg, mu, sg, su, g1, xq, hq, H, F, s);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_forward: gate/up");
+    if (sh && !gu_same) {
+        GroupView g2 = g;
+        g2.no_routed = 1;
+        g2.shared_slots = T;
+        e = launch_expert_gate_up(sg, su, sg, su, g2, xq, hq, H, F, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: shared gate/up");
+    }
+    e = mark(3, s);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_forward: stage event");
+    const bool d_same = sh && L->sd_type == L->d_type;
+    GroupView g3 = g;
+    g3.shared_slots = d_same ? T : 0;
+    e = launch_expert_down(md, sd, g3, hq, 0, parts, H, F, H, s);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_forward: down");
+    if (sh && !d_same) {
+        GroupView g4 = g;
+        g4.no_routed = 1;
+        g4.shared_slots = T;
+        e = launch_expert_down(sd, sd, g4, hq, 0, parts, H, F, H, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: shared down");
+    }
+    e = mark(4, s);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_forward: stage event");
+    e = launch_combine(parts, slot, w, sh ? parts + (int64_t) T * K * H : nullptr, sh ? sh_logit : nullptr, out,
+                       trace ? trace->shared : nullptr, H, K, T, H, s);
+    if (e == cudaSuccess) e = mark(5, s);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_forward: combine");
+
+    if (trace) {
+        if (trace->logits) e = cudaMemcpyAsync(trace->logits, logits, (size_t) T * E * 4, cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess && trace->ids)
+            e = cudaMemcpyAsync(trace->ids, ids, (size_t) T * K * 4, cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess && trace->weights)
+            e = cudaMemcpyAsync(trace->weights, w, (size_t) T * K * 4, cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess && trace->xq)
+            e = cudaMemcpyAsync(trace->xq, xq, (size_t) T * (H / 32) * kQ8Block, cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess && trace->parts) e = launch_gather_parts(parts, slot, trace->parts, H, K, T, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: trace");
+    }
+    return ok();
+}
+
+}  // extern "C"

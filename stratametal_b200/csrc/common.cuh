@@ -1,0 +1,163 @@
+// common.cuh - formats, bit conversions and small device helpers shared by the sm_100a MoE kernels.
+//
+// Formats (ggml, as StrataMetal stores them):
+//   Q2_0  (type 42): 18 B / 64 values  = { fp16 d; u8 qs[16] }, 4 codes per byte LSB first, value (code-1)*d
+//                    (include/strata/artifact/dequant.hpp:8-13, 69-78)
+//   IQ2_S (type 22): 82 B / 256 values = { fp16 d; qs[32]; signs[32]; qh[8]; scales[8] }
+//                    (metal/shaders/iq.metal:152-180, gguf_reader.hpp:197-199)
+//   q8_1           : 36 B / 32 values  = { fp16 d; fp16 sum; int8 q[32] }  (iq.metal:597-627)
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#define SMOE_HD __host__ __device__ __forceinline__
+
+namespace smoe {
+
+constexpr int kQ2_0 = 42;
+constexpr int kIQ2_S = 22;
+constexpr int kQ8Block = 36;
+
+// Status word shared by all kernels of this library (one per device).  A kernel that gives up on a
+// bounded wait records its code here; the host reads and clears it with smoe_device_status().
+enum : unsigned { kDevOk = 0, kDevTimeout = 1, kDevBadId = 2 };
+// The library is one translation unit (smoe_lib.cu), so the word is defined here, once.
+__device__ unsigned g_smoe_status = 0;
+
+SMOE_HD uint32_t f2u(float f) {
+#ifdef __CUDA_ARCH__
+    return __float_as_uint(f);
+#else
+    uint32_t u;
+    __builtin_memcpy(&u, &f, 4);
+    return u;
+#endif
+}
+
+SMOE_HD float u2f(uint32_t u) {
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(u);
+#else
+    float f;
+    __builtin_memcpy(&f, &u, 4);
+    return f;
+#endif
+}
+
+// Round-to-nearest-even f32 -> bf16 bits; a NaN is passed through quieted (the rule of
+// include/strata/kernels/bf16_bits.hpp:37-47).
+SMOE_HD uint16_t bf16_bits(float f) {
+    uint32_t i = f2u(f);
+    if ((i & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t) ((i >> 16) | 64u);
+    i = (i + ((i >> 16) & 1u) + 0x7FFFu) & 0xFFFF0000u;
+    return (uint16_t) (i >> 16);
+}
+
+SMOE_HD float bf16_round(float f) { return u2f((uint32_t) bf16_bits(f) << 16); }
+
+// Round-to-nearest-even f32 -> fp16 bits, subnormals kept, finite overflow -> inf, NaN stays NaN
+// (IEEE binary16; the rounding rule include/strata/kernels/f16_bits.hpp:37-73 states).
+SMOE_HD uint16_t f16_bits(float f) {
+    const uint32_t x = f2u(f);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t rawexp = (x >> 23) & 0xFFu;
+    const int e = (int) rawexp - 127 + 15;
+    uint32_t man = x & 0x7FFFFFu;
+    if (rawexp == 0xFFu) return (uint16_t) (sign | 0x7C00u | (man ? 0x200u : 0u));
+    if (e >= 31) return (uint16_t) (sign | 0x7C00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t) sign;
+        man |= 0x800000u;
+        const uint32_t sh = (uint32_t) (14 - e);
+        uint32_t h = (man >> sh) & 0x3FFu;
+        const uint32_t rem = man & ((1u << sh) - 1u);
+        const uint32_t half = 1u << (sh - 1);
+        if (rem > half || (rem == half && (h & 1u))) ++h;
+        return (uint16_t) (sign | h);
+    }
+    uint32_t h = sign | ((uint32_t) e << 10) | (man >> 13);
+    const uint32_t rem = man & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+    return (uint16_t) h;
+}
+
+// Exact fp16 -> f32 (every fp16 value, subnormals included, is an f32 value).
+__device__ __forceinline__ float f16_to_f32(uint16_t h) {
+    float f;
+    asm("{ .reg .b16 t; mov.b16 t, %1; cvt.f32.f16 %0, t; }" : "=f"(f) : "h"(h));
+    return f;
+}
+
+__device__ __forceinline__ float f32_from_bf16_bits(uint16_t h) { return __uint_as_float((uint32_t) h << 16); }
+
+// dp4a with an UNSIGNED first operand (weight codes 0..255) and a signed second (q8 activations).
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ int dp4a_ss(int a, int b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ------------------------------------------------------------------------------------------------
+// mbarrier + 1D bulk copy (TMA without a tensor map).  Every wait is bounded.
+// ------------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t) __cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Bulk global -> shared copy; dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` for at most `limit_ns`; false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_timer_ns() - t0 > limit_ns) return false;
+    }
+    return true;
+}
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legal copy, far below a hang
+
+}  // namespace smoe

@@ -1,0 +1,133 @@
+// dispatch.cu - token -> expert grouping (row a11): per-expert counts, exclusive prefix sums, the list of
+// experts with rows, and a stable permutation of the (token, k) pairs into contiguous per-expert groups.
+//
+// Contract: fused::group (include/strata/prefill/moe_fused.hpp:46-50) - slot[i] is the grouped row of pair
+// i = t * k + j and src[row] its token.  The reference leaves the order inside an expert free; here it is
+// token order, so every replay groups identically (and combine reads rows in router order).
+//
+// One CTA of 1024 threads walks the tokens in chunks of 64: each chunk builds, per expert, a 64-bit mask of
+// the chunk's tokens that route to it; popcounts of those masks give the counts, and the popcount of the
+// mask below a token gives that token's rank inside its expert.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace smoe {
+
+size_t group_tables_bytes(int n_expert) {
+    const size_t n = (size_t) n_expert * 3 + 1 + 1 + 4;
+    return (n * 4 + 255) & ~(size_t) 255;
+}
+
+GroupTables group_tables_at(void* base, int n_expert) {
+    int32_t* p = static_cast<int32_t*>(base);
+    GroupTables g;
+    g.counts = p;
+    g.offsets = p + n_expert;
+    g.active = p + 2 * n_expert + 1;
+    g.n_active = p + 3 * n_expert + 1;
+    g.work = p + 3 * n_expert + 2;
+    return g;
+}
+
+__device__ __forceinline__ int block_excl_scan(int v, int* warp_sums, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < (int) (blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        warp_sums[lane] = w;  // inclusive
+    }
+    __syncthreads();
+    const int before = warp > 0 ? warp_sums[warp - 1] : 0;
+    if (total) *total = warp_sums[(blockDim.x >> 5) - 1];
+    __syncthreads();
+    return before + x - v;
+}
+
+__global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__ ids, int T, int k, int E,
+                                                     GroupTables g, int32_t* __restrict__ slot,
+                                                     int32_t* __restrict__ src) {
+    __shared__ unsigned long long mask[kMaxExperts];
+    __shared__ int run[kMaxExperts];
+    __shared__ int warp_sums[32];
+    const int tid = threadIdx.x;
+    const int nchunks = (T + 63) / 64;
+
+    for (int e = tid; e < E; e += blockDim.x) run[e] = 0;
+    for (int pass = 0; pass < 2; pass++) {
+        for (int c = 0; c < nchunks; c++) {
+            const int t0 = c * 64;
+            const int nt = min(64, T - t0);
+            for (int e = tid; e < E; e += blockDim.x) mask[e] = 0ull;
+            __syncthreads();
+            for (int p = tid; p < nt * k; p += blockDim.x) {
+                const int tl = p / k;
+                const int e = ids[(size_t) (t0 + tl) * k + (p % k)];
+                if (e >= 0 && e < E) atomicOr(&mask[e], 1ull << tl);
+            }
+            __syncthreads();
+            if (pass == 1) {
+                for (int p = tid; p < nt * k; p += blockDim.x) {
+                    const int tl = p / k;
+                    const size_t i = (size_t) (t0 + tl) * k + (p % k);
+                    const int e = ids[i];
+                    if (e < 0 || e >= E) {
+                        slot[i] = -1;
+                        atomicOr(&g_smoe_status, kDevBadId);
+                        continue;
+                    }
+                    const int pos = run[e] + __popcll(mask[e] & ((1ull << tl) - 1ull));
+                    slot[i] = pos;
+                    if (src) src[pos] = t0 + tl;
+                }
+                __syncthreads();
+            }
+            for (int e = tid; e < E; e += blockDim.x) run[e] += __popcll(mask[e]);
+            __syncthreads();
+        }
+        if (pass == 0) {
+            // counts -> exclusive offsets and the active list (experts with rows, ascending id)
+            int carry = 0, carry_act = 0;
+            for (int e0 = 0; e0 < E; e0 += blockDim.x) {
+                const int e = e0 + tid;
+                const int cnt = e < E ? run[e] : 0;
+                int tot, tot_act;
+                const int off = block_excl_scan(cnt, warp_sums, &tot);
+                const int act = block_excl_scan(cnt > 0 ? 1 : 0, warp_sums, &tot_act);
+                if (e < E) {
+                    g.counts[e] = cnt;
+                    g.offsets[e] = carry + off;
+                    run[e] = carry + off;
+                    if (cnt > 0) g.active[carry_act + act] = e;
+                }
+                carry += tot;
+                carry_act += tot_act;
+            }
+            if (tid == 0) {
+                g.offsets[E] = carry;
+                g.n_active[0] = carry_act;
+                g.work[0] = g.work[1] = g.work[2] = g.work[3] = 0;
+            }
+            __syncthreads();
+        }
+    }
+}
+
+cudaError_t launch_group(const int32_t* ids, int T, int k, int E, GroupTables g, int32_t* slot, int32_t* src,
+                         cudaStream_t s) {
+    group_kernel<<<1, 1024, 0, s>>>(ids, T, k, E, g, slot, src);
+    return cudaGetLastError();
+}
+
+}  // namespace smoe

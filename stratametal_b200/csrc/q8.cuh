@@ -1,0 +1,45 @@
+// q8.cuh - the q8_1 activation rule and SwiGLU, shared by the router and the expert kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace smoe {
+
+// ------------------------------------------------------------------------------------------------
+// q8_1 of one 32-value block by one warp (iq.metal:597-627; host quant_host_block iq_parity.cpp:350-382):
+// the amax and the float sum meet in an xor butterfly (offsets 16..1) in the host reference's order.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void quant_q8_1_warp(float xi, uint8_t* __restrict__ yb, int lane) {
+    float amax = fabsf(xi), sum = xi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    }
+    float d = __fdiv_rn(amax, 127.f);
+    if (fabsf(d) > 65504.f) d = copysignf(65504.f, d);
+    int q = 0;
+    if (amax != 0.f) {
+        float r = roundf(__fdiv_rn(xi, d));
+        r = fminf(fmaxf(r, -127.f), 127.f);
+        q = (int) r;
+    }
+    yb[4 + lane] = (uint8_t) (int8_t) q;
+    if (lane == 0) {
+        const float sc = fabsf(sum) > 65504.f ? copysignf(65504.f, sum) : sum;
+        const uint16_t dh = f16_bits(d), sh = f16_bits(sc);
+        yb[0] = (uint8_t) dh;
+        yb[1] = (uint8_t) (dh >> 8);
+        yb[2] = (uint8_t) sh;
+        yb[3] = (uint8_t) (sh >> 8);
+    }
+}
+
+// silu(g) * u (iq.metal:630-663).  exp is taken in fp64 and rounded to f32: that is the correctly rounded
+// expf, which the host reference's libm expf returns on all but a vanishing fraction of inputs.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float e = (float) exp(-(double) g);
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, e)), u);
+}
+
+}  // namespace smoe

@@ -1,0 +1,244 @@
+// router.cu - the MoE router on sm_100a: bf16 GEMV with fp64 accumulation, then softmax / top-k /
+// renormalise, fused with the q8_1 quantization of the token (rows a1-a4 of the block).
+//
+// Numerics (what makes the expert ids exact against the host reference):
+//   * the activation is rounded to bf16 with round-to-nearest-even (bf16_bits.hpp:37-47);
+//   * each product bf16 x bf16 is exact in fp64 and the 2048-term sum is accumulated in fp64, then rounded
+//     once to f32 - the host oracle's bf16_dot (pack_parity.cpp:3795-3799).  The sums of these products span
+//     far fewer than 53 bits on this data, so the order of the fp64 additions does not change the result;
+//   * the softmax is computed in fp64 (route_ref, pack_parity.cpp:5144-5165), ranked by probability with
+//     the lower index on a tie; the weights are (float) p, then (float)((double) w / max(sum, 2^-14)) with
+//     the sum taken in rank order.
+#include "common.cuh"
+#include "kernels.cuh"
+#include "q8.cuh"
+
+#include <cfloat>
+
+namespace smoe {
+
+// ------------------------------------------------------------------------------------------------
+// a1 + a2: logits.  One warp per output row, TT tokens per CTA staged in shared memory as bf16 bits.
+// Rows [0, n_out) come from `w`; when `extra` is set, row n_out is that vector (the shared-expert gate
+// ffn_gate_inp_shexp) and its result goes to y_extra[t].
+// ------------------------------------------------------------------------------------------------
+template <bool kF32In>
+__global__ void __launch_bounds__(128) bf16_gemv_kernel(const void* __restrict__ xin, const uint16_t* __restrict__ w,
+                                                        const uint16_t* __restrict__ extra, float* __restrict__ y,
+                                                        float* __restrict__ y_extra, int T, int H, int n_out) {
+    constexpr int TT = kRouterTokTile;
+    extern __shared__ __align__(16) uint16_t xs[];  // [TT][H]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int o = blockIdx.x * 4 + warp;
+    const int t0 = blockIdx.y * TT;
+    const int nt = min(TT, T - t0);
+    for (int i = threadIdx.x; i < nt * H; i += blockDim.x) {
+        const size_t g = (size_t) t0 * H + i;
+        if (kF32In) xs[i] = bf16_bits(static_cast<const float*>(xin)[g]);
+        else xs[i] = static_cast<const uint16_t*>(xin)[g];
+    }
+    __syncthreads();
+    const int n_rows = n_out + (extra ? 1 : 0);
+    if (o >= n_rows) return;
+    const uint16_t* row = o < n_out ? w + (size_t) o * H : extra;
+    double acc[TT];
+#pragma unroll
+    for (int t = 0; t < TT; t++) acc[t] = 0.0;
+    for (int c = lane * 8; c < H; c += 256) {
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(row + c));
+        double wd[8];
+        const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            wd[2 * q] = (double) __uint_as_float(wu[q] << 16);
+            wd[2 * q + 1] = (double) __uint_as_float(wu[q] & 0xFFFF0000u);
+        }
+#pragma unroll
+        for (int t = 0; t < TT; t++) {
+            if (t < nt) {
+                const uint4 xv = *reinterpret_cast<const uint4*>(xs + t * H + c);
+                const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    acc[t] = fma((double) __uint_as_float(xu[q] << 16), wd[2 * q], acc[t]);
+                    acc[t] = fma((double) __uint_as_float(xu[q] & 0xFFFF0000u), wd[2 * q + 1], acc[t]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < TT; t++) {
+        if (t < nt) {
+            double v = acc[t];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0) {
+                if (o < n_out) y[(size_t) (t0 + t) * n_out + o] = (float) v;
+                else y_extra[t0 + t] = (float) v;
+            }
+        }
+    }
+}
+
+__global__ void quant_q8_1_kernel(const float* __restrict__ x, uint8_t* __restrict__ y, int64_t n_blocks) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t b = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks; b += warps)
+        quant_q8_1_warp(x[b * 32 + lane], y + b * kQ8Block, lane);
+}
+
+__global__ void swiglu_q8_kernel(const float* __restrict__ g, const float* __restrict__ u, uint8_t* __restrict__ y,
+                                 int64_t n_blocks) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t b = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks; b += warps)
+        quant_q8_1_warp(silu_mul(g[b * 32 + lane], u[b * 32 + lane]), y + b * kQ8Block, lane);
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ x, uint16_t* __restrict__ y, int64_t n) {
+    for (int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t) gridDim.x * blockDim.x)
+        y[i] = bf16_bits(x[i]);
+}
+
+// ------------------------------------------------------------------------------------------------
+// a3 (+ a4): one CTA per token.  Softmax in fp64, top-k by (probability desc, index asc), renormalise.
+// When xq != nullptr the CTA also writes the q8_1 image of the token's activation x.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ bool better(double v, int i, double bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+__global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restrict__ logits, int E, int k,
+                                                           int32_t* __restrict__ ids, float* __restrict__ wout,
+                                                           const float* __restrict__ x, uint8_t* __restrict__ xq,
+                                                           int H) {
+    extern __shared__ double sp[];  // [E] probabilities
+    __shared__ double red[32];
+    __shared__ double sbv[64];
+    __shared__ int sbi[64];
+    const int t = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const float* l = logits + (size_t) t * E;
+
+    // block max of the logits
+    float mxf = -INFINITY;
+    for (int e = tid; e < E; e += blockDim.x) mxf = fmaxf(mxf, l[e]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mxf = fmaxf(mxf, __shfl_xor_sync(0xffffffffu, mxf, o));
+    if (lane == 0) red[warp] = (double) mxf;
+    __syncthreads();
+    double mx = red[0];
+    for (int i = 1; i < nw; i++) mx = fmax(mx, red[i]);
+    __syncthreads();
+
+    // p = exp(l - mx), fp64 sum
+    double part = 0;
+    for (int e = tid; e < E; e += blockDim.x) {
+        const double p = exp((double) l[e] - mx);
+        sp[e] = p;
+        part += p;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (lane == 0) red[warp] = part;
+    __syncthreads();
+    double sum = 0;
+    for (int i = 0; i < nw; i++) sum += red[i];
+    for (int e = tid; e < E; e += blockDim.x) sp[e] = sp[e] / sum;
+    __syncthreads();
+
+    // top-k by warp 0: every lane owns experts lane, lane + 32, ...
+    if (warp == 0) {
+        uint32_t taken = 0;  // bit j: expert lane + 32 j is taken (E <= 1024)
+        double bv = -1.0;
+        int bi = 0x7fffffff;
+        for (int j = 0, e = lane; e < E; j++, e += 32)
+            if (better(sp[e], e, bv, bi)) { bv = sp[e]; bi = e; }
+        for (int i = 0; i < k; i++) {
+            double v = bv;
+            int ix = bi;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const double ov = __shfl_xor_sync(0xffffffffu, v, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
+                if (better(ov, oi, v, ix)) { v = ov; ix = oi; }
+            }
+            if (lane == 0) { sbv[i] = v; sbi[i] = ix; }
+            if ((ix & 31) == lane) {
+                taken |= 1u << (ix >> 5);
+                bv = -1.0;
+                bi = 0x7fffffff;
+                for (int j = 0, e = lane; e < E; j++, e += 32)
+                    if (!((taken >> j) & 1u) && better(sp[e], e, bv, bi)) { bv = sp[e]; bi = e; }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            double chosen = 0;
+            for (int i = 0; i < k; i++) chosen += sbv[i];
+            chosen = fmax(chosen, 6.103515625e-05);
+            for (int i = 0; i < k; i++) {
+                ids[(size_t) t * k + i] = sbi[i];
+                wout[(size_t) t * k + i] = (float) ((double) (float) sbv[i] / chosen);
+            }
+        }
+    }
+
+    if (xq) {
+        const float* xt = x + (size_t) t * H;
+        uint8_t* yt = xq + (size_t) t * (H / 32) * kQ8Block;
+        for (int b = warp; b < H / 32; b += nw) quant_q8_1_warp(xt[b * 32 + lane], yt + b * kQ8Block, lane);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// launchers
+// ------------------------------------------------------------------------------------------------
+
+cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, const uint16_t* extra, float* y,
+                             float* y_extra, int T, int H, int n_out, cudaStream_t s) {
+    const int n_rows = n_out + (extra ? 1 : 0);
+    const dim3 grid((n_rows + 3) / 4, (T + kRouterTokTile - 1) / kRouterTokTile);
+    const size_t smem = (size_t) kRouterTokTile * H * 2;
+    cudaError_t err;
+    if (f32_in) {
+        err = cudaFuncSetAttribute(bf16_gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (err != cudaSuccess) return err;
+        bf16_gemv_kernel<true><<<grid, 128, smem, s>>>(x, w, extra, y, y_extra, T, H, n_out);
+    } else {
+        err = cudaFuncSetAttribute(bf16_gemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        if (err != cudaSuccess) return err;
+        bf16_gemv_kernel<false><<<grid, 128, smem, s>>>(x, w, extra, y, y_extra, T, H, n_out);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_router_topk(const float* logits, int T, int E, int k, int32_t* ids, float* w, const float* x,
+                               uint8_t* xq, int H, cudaStream_t s) {
+    int threads = ((E + 31) / 32) * 32;
+    if (threads < 64) threads = 64;
+    if (threads > 1024) threads = 1024;
+    router_topk_kernel<<<T, threads, (size_t) E * sizeof(double), s>>>(logits, E, k, ids, w, x, xq, H);
+    return cudaGetLastError();
+}
+
+static int grid_for(int64_t warps_needed) {
+    const int64_t blocks = (warps_needed + 7) / 8;
+    return (int) (blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
+}
+
+cudaError_t launch_quant_q8_1(const float* x, int64_t n, uint8_t* y, cudaStream_t s) {
+    quant_q8_1_kernel<<<grid_for(n / 32), 256, 0, s>>>(x, y, n / 32);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_q8(const float* g, const float* u, int64_t n, uint8_t* y, cudaStream_t s) {
+    swiglu_q8_kernel<<<grid_for(n / 32), 256, 0, s>>>(g, u, y, n / 32);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_f32_to_bf16(const float* x, uint16_t* y, int64_t n, cudaStream_t s) {
+    const int64_t blocks = (n + 255) / 256;
+    f32_to_bf16_kernel<<<(int) (blocks < 148 * 8 ? blocks : 148 * 8), 256, 0, s>>>(x, y, n);
+    return cudaGetLastError();
+}
+
+}  // namespace smoe

@@ -1,0 +1,7 @@
+// smoe_lib.cu - the library's single translation unit: every kernel file and the C ABI are compiled here
+// together, so the per-device status word (common.cuh) is one symbol without relocatable device code.
+#include "router.cu"
+#include "dispatch.cu"
+#include "expert.cu"
+#include "combine.cu"
+#include "api.cu"
