@@ -260,6 +260,7 @@ def run_ours(args, ws, rank, local):
     from stratametal_b200._lib import lib
     build.build()
     dev = torch.device("cuda", local)
+    torch.cuda.set_stream(torch.cuda.Stream(dev))  # the C ABI wants an explicit non-null stream
     spec, T = synth.config_spec(args.config)
     layers = [api.MoeLayer(synth.make_layer(spec, li, dev), T, dev) for li in range(args.layers)]
     n_batches = 4
@@ -285,6 +286,9 @@ def run_ours(args, ws, rank, local):
         step(i)
     # stage events for every timed step
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)] for _ in range(K)]
+    for row in ev:  # torch creates the CUDA event on its first record
+        for e in row:
+            e.record(stream)
     handles = [(C.c_void_p * len(STAGES))(*[e.cuda_event for e in row[1:]]) for row in ev]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()

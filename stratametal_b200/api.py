@@ -18,6 +18,8 @@ __all__ = ["SmoeError", "f32_to_bf16_bulk", "bf16_gemv", "router_top10", "router
 
 
 def _s() -> int:
+    """torch's current stream.  The C ABI refuses the null (legacy default) stream, as the reference's
+    contract does (native_router.hpp:15): run under `torch.cuda.stream(...)` / `torch.cuda.set_stream`."""
     return torch.cuda.current_stream().cuda_stream
 
 

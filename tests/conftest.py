@@ -25,4 +25,7 @@ def cuda():
         pytest.skip("no CUDA device")
     from stratametal_b200 import build
     build.build()
-    return torch.device("cuda:0")
+    dev = torch.device("cuda:0")
+    # the C ABI requires an explicit, non-null stream (torch's default stream is the null stream)
+    torch.cuda.set_stream(torch.cuda.Stream(dev))
+    return dev
