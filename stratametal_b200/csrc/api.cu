@@ -178,8 +178,8 @@ smoe_status smoe_router(const float* x, const uint16_t* w_router, int n_tokens, 
     if (n_embd <= 0 || n_embd % 8 || n_embd > 16384)
         return fail(SMOE_INVALID_ARG, "router: n_embd must be a positive multiple of 8, at most 16384");
     if (!stream) return fail(SMOE_INVALID_ARG, "router: a non-null stream is required");
-    if (!x || !w_router || !logits || !ids || !weights || !aligned(w_router, 16))
-        return fail(SMOE_INVALID_ARG, "router: null or misaligned buffer");
+    if (!x || !w_router || !logits || !ids || !weights || !aligned(w_router, 16) || !aligned(x, 16))
+        return fail(SMOE_INVALID_ARG, "router: null buffer, or x / w_router not 16-byte aligned");
     cudaError_t e = launch_bf16_gemv(x, true, w_router, nullptr, logits, nullptr, n_tokens, n_embd, n_expert,
                                      (cudaStream_t) stream);
     if (e != cudaSuccess) return cuda_fail(e, "router");
@@ -275,8 +275,8 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     if (n_tokens < 0) return fail(SMOE_INVALID_ARG, "moe_forward: negative token count");
     if (n_tokens == 0) return ok();
     if (!stream) return fail(SMOE_INVALID_ARG, "moe_forward: a non-null stream is required");
-    if (!x || !out || !scratch || !aligned(scratch, 256))
-        return fail(SMOE_INVALID_ARG, "moe_forward: null buffer or scratch not 256-byte aligned");
+    if (!x || !out || !scratch || !aligned(scratch, 256) || !aligned(x, 16))
+        return fail(SMOE_INVALID_ARG, "moe_forward: null buffer, x not 16-byte or scratch not 256-byte aligned");
     const Layout lo = layout_of(L, n_tokens);
     if (scratch_bytes < lo.total) return fail(SMOE_INVALID_ARG, "moe_forward: scratch is too small");
     cudaStream_t s = (cudaStream_t) stream;

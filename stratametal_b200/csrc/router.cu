@@ -18,63 +18,103 @@
 namespace smoe {
 
 // ------------------------------------------------------------------------------------------------
-// a1 + a2: logits.  One warp per output row, TT tokens per CTA staged in shared memory as bf16 bits.
+// a1 + a2: logits.  A CTA owns RPW rows per warp (4 warps) and TT tokens staged in shared memory as bf16
+// bits.  Per 256-value chunk a lane converts its 8 weights of each row to fp64 once and applies them to every
+// staged token, so each DFMA needs one converted activation and the weight stream is read once per CTA.
 // Rows [0, n_out) come from `w`; when `extra` is set, row n_out is that vector (the shared-expert gate
 // ffn_gate_inp_shexp) and its result goes to y_extra[t].
 // ------------------------------------------------------------------------------------------------
-template <bool kF32In>
+template <bool kF32In, int RPW>
 __global__ void __launch_bounds__(128) bf16_gemv_kernel(const void* __restrict__ xin, const uint16_t* __restrict__ w,
                                                         const uint16_t* __restrict__ extra, float* __restrict__ y,
                                                         float* __restrict__ y_extra, int T, int H, int n_out) {
     constexpr int TT = kRouterTokTile;
     extern __shared__ __align__(16) uint16_t xs[];  // [TT][H]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int o = blockIdx.x * 4 + warp;
+    const int o0 = (blockIdx.x * 4 + warp) * RPW;
     const int t0 = blockIdx.y * TT;
     const int nt = min(TT, T - t0);
-    for (int i = threadIdx.x; i < nt * H; i += blockDim.x) {
-        const size_t g = (size_t) t0 * H + i;
-        if (kF32In) xs[i] = bf16_bits(static_cast<const float*>(xin)[g]);
-        else xs[i] = static_cast<const uint16_t*>(xin)[g];
+    // stage: 4 floats (or 8 bf16) per load, several loads in flight per thread
+    if (kF32In) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(xin) + (size_t) t0 * H);
+        const int n4 = nt * H / 4;
+        for (int i = threadIdx.x; i < n4; i += 4 * blockDim.x) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (i + u * blockDim.x < n4) v[u] = __ldg(src + i + u * blockDim.x);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int j = i + u * blockDim.x;
+                if (j < n4) {
+                    uint2 b;
+                    b.x = (uint32_t) bf16_bits(v[u].x) | ((uint32_t) bf16_bits(v[u].y) << 16);
+                    b.y = (uint32_t) bf16_bits(v[u].z) | ((uint32_t) bf16_bits(v[u].w) << 16);
+                    reinterpret_cast<uint2*>(xs)[j] = b;
+                }
+            }
+        }
+    } else {
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(xin) + (size_t) t0 * H);
+        for (int i = threadIdx.x; i < nt * H / 8; i += blockDim.x) reinterpret_cast<uint4*>(xs)[i] = __ldg(src + i);
     }
     __syncthreads();
     const int n_rows = n_out + (extra ? 1 : 0);
-    if (o >= n_rows) return;
-    const uint16_t* row = o < n_out ? w + (size_t) o * H : extra;
-    double acc[TT];
+    if (o0 >= n_rows) return;
+    const uint16_t* rowp[RPW];
 #pragma unroll
-    for (int t = 0; t < TT; t++) acc[t] = 0.0;
+    for (int r = 0; r < RPW; r++) {
+        const int o = min(o0 + r, n_rows - 1);
+        rowp[r] = o < n_out ? w + (size_t) o * H : extra;
+    }
+    double acc[RPW][TT];
+#pragma unroll
+    for (int r = 0; r < RPW; r++)
+#pragma unroll
+        for (int t = 0; t < TT; t++) acc[r][t] = 0.0;
     for (int c = lane * 8; c < H; c += 256) {
-        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(row + c));
-        double wd[8];
-        const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+        double wd[RPW][8];
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            wd[2 * q] = (double) __uint_as_float(wu[q] << 16);
-            wd[2 * q + 1] = (double) __uint_as_float(wu[q] & 0xFFFF0000u);
+        for (int r = 0; r < RPW; r++) {
+            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(rowp[r] + c));
+            const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                wd[r][2 * q] = (double) __uint_as_float(wu[q] << 16);
+                wd[r][2 * q + 1] = (double) __uint_as_float(wu[q] & 0xFFFF0000u);
+            }
         }
 #pragma unroll
         for (int t = 0; t < TT; t++) {
             if (t < nt) {
                 const uint4 xv = *reinterpret_cast<const uint4*>(xs + t * H + c);
                 const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
+                double xd[8];
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
-                    acc[t] = fma((double) __uint_as_float(xu[q] << 16), wd[2 * q], acc[t]);
-                    acc[t] = fma((double) __uint_as_float(xu[q] & 0xFFFF0000u), wd[2 * q + 1], acc[t]);
+                    xd[2 * q] = (double) __uint_as_float(xu[q] << 16);
+                    xd[2 * q + 1] = (double) __uint_as_float(xu[q] & 0xFFFF0000u);
                 }
+#pragma unroll
+                for (int r = 0; r < RPW; r++)
+#pragma unroll
+                    for (int q = 0; q < 8; q++) acc[r][t] = fma(xd[q], wd[r][q], acc[r][t]);
             }
         }
     }
 #pragma unroll
-    for (int t = 0; t < TT; t++) {
-        if (t < nt) {
-            double v = acc[t];
+    for (int r = 0; r < RPW; r++) {
+        const int o = o0 + r;
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-            if (lane == 0) {
-                if (o < n_out) y[(size_t) (t0 + t) * n_out + o] = (float) v;
-                else y_extra[t0 + t] = (float) v;
+        for (int t = 0; t < TT; t++) {
+            if (t < nt) {
+                double v = acc[r][t];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+                if (lane == 0 && o < n_rows) {
+                    if (o < n_out) y[(size_t) (t0 + t) * n_out + o] = (float) v;
+                    else y_extra[t0 + t] = (float) v;
+                }
             }
         }
     }
@@ -196,18 +236,27 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restri
 cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, const uint16_t* extra, float* y,
                              float* y_extra, int T, int H, int n_out, cudaStream_t s) {
     const int n_rows = n_out + (extra ? 1 : 0);
-    const dim3 grid((n_rows + 3) / 4, (T + kRouterTokTile - 1) / kRouterTokTile);
     const size_t smem = (size_t) kRouterTokTile * H * 2;
-    cudaError_t err;
+    // few tokens: one row per warp spreads the weight stream over more SMs; many tokens: four rows per warp
+    // reuse each staged token four times
+    const int rpw = T <= 4 ? 1 : 4;
+    const dim3 grid((n_rows + 4 * rpw - 1) / (4 * rpw), (T + kRouterTokTile - 1) / kRouterTokTile);
+    cudaError_t err = cudaSuccess;
+#define SMOE_GEMV(F_, R_)                                                                                     \
+    do {                                                                                                      \
+        err = cudaFuncSetAttribute(bf16_gemv_kernel<F_, R_>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                   (int) smem);                                                               \
+        if (err != cudaSuccess) return err;                                                                   \
+        bf16_gemv_kernel<F_, R_><<<grid, 128, smem, s>>>(x, w, extra, y, y_extra, T, H, n_out);              \
+    } while (0)
     if (f32_in) {
-        err = cudaFuncSetAttribute(bf16_gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        if (err != cudaSuccess) return err;
-        bf16_gemv_kernel<true><<<grid, 128, smem, s>>>(x, w, extra, y, y_extra, T, H, n_out);
+        if (rpw == 1) SMOE_GEMV(true, 1);
+        else SMOE_GEMV(true, 4);
     } else {
-        err = cudaFuncSetAttribute(bf16_gemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
-        if (err != cudaSuccess) return err;
-        bf16_gemv_kernel<false><<<grid, 128, smem, s>>>(x, w, extra, y, y_extra, T, H, n_out);
+        if (rpw == 1) SMOE_GEMV(false, 1);
+        else SMOE_GEMV(false, 4);
     }
+#undef SMOE_GEMV
     return cudaGetLastError();
 }
 
