@@ -104,6 +104,16 @@ size_t smoe_moe_group_scratch_bytes(int n_tok, int k, int n_expert);
 smoe_status smoe_moe_group(const int32_t* ids, int n_tok, int k, int n_expert, void* scratch, int32_t* slot,
                            int32_t* src, void* stream);
 
+/* No counterpart in the reference.  The same grouping as smoe_moe_group for callers that cannot allocate
+ * device memory where they group tokens (code being captured into a CUDA graph, engines whose planner forbids
+ * allocation on the token path, plug-ins inside a process that owns the allocator): the grouping tables live
+ * in a static 12,544-byte device array instead of caller scratch, so at most 1024 experts (more is refused
+ * with SMOE_INVALID_ARG).  Allocates nothing.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress) and must come before any stream capture.  All calls on a device share the
+ * array; calls that overlap on the GPU race, so order them on one stream. */
+smoe_status smoe_moe_group_noalloc(const int32_t* ids, int n_tok, int k, int n_expert, int32_t* slot, int32_t* src,
+                                   void* stream);
+
 /* ---- the block ----------------------------------------------------------------------------------- */
 
 /* One MoE layer's weights on the device, named as the GGUF names them (layer_exec.cpp:369-452,

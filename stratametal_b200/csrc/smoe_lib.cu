@@ -5,3 +5,4 @@
 #include "expert.cu"
 #include "combine.cu"
 #include "api.cu"
+#include "noalloc.cu"
