@@ -43,7 +43,7 @@ size_t up256(size_t n) { return (n + 255) & ~(size_t) 255; }
 
 // Scratch regions of the block for T tokens.
 struct Layout {
-    size_t xq, logits, sh_logit, ids, w, slot, slot_token, tables, hq, parts, total;
+    size_t xq, xa, xa2, logits, sh_logit, ids, w, slot, slot_token, tables, sched, ha, parts, total;
 };
 
 Layout layout_of(const smoe_layer* L, int T) {
@@ -52,6 +52,8 @@ Layout layout_of(const smoe_layer* L, int T) {
     const size_t rows = (size_t) T * K + (L->has_shared ? (size_t) T : 0);
     size_t at = 0;
     o.xq = at; at += up256((size_t) T * (H / 32) * kQ8Block);
+    o.xa = at; at += up256(ka_bytes(T, (int) (H / 32)));
+    o.xa2 = at; at += up256(ka_bytes(T, (int) (H / 32)));
     o.logits = at; at += up256((size_t) T * E * 4);
     o.sh_logit = at; at += up256((size_t) T * 4);
     o.ids = at; at += up256((size_t) T * K * 4);
@@ -59,7 +61,8 @@ Layout layout_of(const smoe_layer* L, int T) {
     o.slot = at; at += up256((size_t) T * K * 4);
     o.slot_token = at; at += up256((size_t) T * K * 4);
     o.tables = at; at += group_tables_bytes((int) E);
-    o.hq = at; at += up256(rows * (F / 32) * kQ8Block);
+    o.sched = at; at += sched_bytes((int) E, T, (int) K);
+    o.ha = at; at += up256(ka_bytes((int64_t) rows, (int) (F / 32)));
     o.parts = at; at += up256(rows * H * 4);
     o.total = at;
     return o;
@@ -290,58 +293,69 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     int32_t* slot = reinterpret_cast<int32_t*>(base + lo.slot);
     int32_t* slot_tok = reinterpret_cast<int32_t*>(base + lo.slot_token);
     const GroupTables tabs = group_tables_at(base + lo.tables, E);
-    uint8_t* hq = base + lo.hq;
+    const Sched sc = sched_at(base + lo.sched, E, T, K);
+    const bool sh = L->has_shared != 0;
+    const int rows = T * K + (sh ? T : 0);
+    const KAct xa = ka_at(base + lo.xa, T, H / 32);
+    const KAct xa2 = ka_at(base + lo.xa2, T, H / 32);
+    const KAct ha = ka_at(base + lo.ha, rows, F / 32);
     float* parts = reinterpret_cast<float*>(base + lo.parts);
 
-    cudaError_t e = launch_bf16_gemv(x, true, L->router, L->has_shared ? L->gate_inp_shexp : nullptr, logits,
-                                     sh_logit, T, H, E, s);
+    cudaError_t e = launch_bf16_gemv(x, true, L->router, sh ? L->gate_inp_shexp : nullptr, logits, sh_logit, T, H,
+                                     E, s);
     if (e == cudaSuccess) e = mark(0, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: router");
-    e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s);
+    e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, &xa, L->gu_type == kQ2_0);
     if (e == cudaSuccess) e = mark(1, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: top-k");
-    e = launch_group(ids, T, K, E, tabs, slot, slot_tok, s);
+    e = launch_group(ids, T, K, E, tabs, slot, slot_tok, s, &sc);
     if (e == cudaSuccess) e = mark(2, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: dispatch");
 
-    GroupView g{};
-    g.offsets = tabs.offsets;
-    g.active = tabs.active;
-    g.n_active = tabs.n_active;
-    g.slot_token = slot_tok;
-    g.max_active = T * K < E ? T * K : E;
-    g.shared_base = T * K;
+    Work wk{};
+    wk.sched = sc;
+    wk.slot_token = slot_tok;
+    wk.max_entries = sched_capacity(E, T, K);
+    wk.shared_base = T * K;
     const int64_t gu_stride = (int64_t) F * (int64_t) row_bytes(L->gu_type, H);
     const int64_t d_stride = (int64_t) H * (int64_t) row_bytes(L->d_type, F);
     const Matrix mg{L->gate, gu_stride, L->gu_type}, mu{L->up, gu_stride, L->gu_type}, md{L->down, d_stride, L->d_type};
     const Matrix sg{L->sgate, 0, L->sg_type}, su{L->sup, 0, L->su_type}, sd{L->sdown, 0, L->sd_type};
 
-    // gate/up: the shared expert rides in the routed launch when its type matches
-    const bool sh = L->has_shared != 0;
-    const bool gu_same = sh && L->sg_type == L->gu_type;
-    GroupView g1 = g;
-    g1.shared_slots = gu_same ? T : 0;
-    e = launch_expert_gate_up(mg, mu, sg, su, g1, xq, hq, H, F, s);
+    // The shared expert rides in the routed launches when its types match; otherwise it gets its own.
+    const bool gu_same = sh && L->sg_type == L->gu_type && L->su_type == L->gu_type;
+    const bool d_same = sh && L->sd_type == L->d_type;
+    Work w1 = wk;
+    w1.shared_slots = gu_same ? T : 0;
+    w1.counter = tabs.work + 0;
+    e = launch_layer_gate_up(mg, mu, sg, su, w1, xa, ha, L->d_type == kQ2_0, H, F, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: gate/up");
     if (sh && !gu_same) {
-        GroupView g2 = g;
-        g2.no_routed = 1;
-        g2.shared_slots = T;
-        e = launch_expert_gate_up(sg, su, sg, su, g2, xq, hq, H, F, s);
+        const bool same_layout = (L->sg_type == kQ2_0) == (L->gu_type == kQ2_0);
+        if (!same_layout) {
+            e = launch_quant_ka(x, T, H, xa2, L->sg_type == kQ2_0, s);
+            if (e != cudaSuccess) return cuda_fail(e, "moe_forward: shared activation");
+        }
+        Work w2 = wk;
+        w2.no_routed = 1;
+        w2.shared_slots = T;
+        w2.counter = tabs.work + 1;
+        e = launch_layer_gate_up(sg, su, sg, su, w2, same_layout ? xa : xa2, ha, L->sd_type == kQ2_0, H, F, s);
         if (e != cudaSuccess) return cuda_fail(e, "moe_forward: shared gate/up");
     }
     e = mark(3, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: stage event");
-    const bool d_same = sh && L->sd_type == L->d_type;
-    GroupView g3 = g;
-    g3.shared_slots = d_same ? T : 0;
-    e = launch_expert_down(md, sd, g3, hq, 0, parts, H, F, H, s);
+    Work w3 = wk;
+    w3.shared_slots = d_same ? T : 0;
+    w3.counter = tabs.work + 2;
+    e = launch_layer_down(md, sd, w3, ha, parts, F, H, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: down");
     if (sh && !d_same) {
-        GroupView g4 = g;
-        g4.no_routed = 1;
-        g4.shared_slots = T;
-        e = launch_expert_down(sd, sd, g4, hq, 0, parts, H, F, H, s);
+        Work w4 = wk;
+        w4.no_routed = 1;
+        w4.shared_slots = T;
+        w4.counter = tabs.work + 3;
+        e = launch_layer_down(sd, sd, w4, ha, parts, F, H, s);
         if (e != cudaSuccess) return cuda_fail(e, "moe_forward: shared down");
     }
     e = mark(4, s);

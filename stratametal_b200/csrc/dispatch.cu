@@ -29,6 +29,20 @@ GroupTables group_tables_at(void* base, int n_expert) {
     return g;
 }
 
+size_t sched_bytes(int E, int T, int k) { return ((size_t) 3 * sched_capacity(E, T, k) * 4 + 4 + 255) & ~(size_t) 255; }
+
+Sched sched_at(void* base, int E, int T, int k) {
+    const int cap = sched_capacity(E, T, k);
+    int32_t* p = static_cast<int32_t*>(base);
+    return Sched{p, p + cap, p + 2 * cap, p + 3 * cap};
+}
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+    uint32_t m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
 __device__ __forceinline__ int block_excl_scan(int v, int* warp_sums, int* total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int x = v;
@@ -57,7 +71,7 @@ __device__ __forceinline__ int block_excl_scan(int v, int* warp_sums, int* total
 
 __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__ ids, int T, int k, int E,
                                                      GroupTables g, int32_t* __restrict__ slot,
-                                                     int32_t* __restrict__ src) {
+                                                     int32_t* __restrict__ src, Sched sched, int with_sched) {
     __shared__ unsigned long long mask[kMaxExperts];
     __shared__ int run[kMaxExperts];
     __shared__ int warp_sums[32];
@@ -122,11 +136,64 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__
             __syncthreads();
         }
     }
+    if (!with_sched) return;
+
+    // The work list: experts bucketed by min(count, 63), heaviest bucket first, ascending id inside a bucket
+    // (per-warp bucket counts, scanned bucket-major then warp-minor, plus the rank among same-bucket lanes),
+    // then each expert cut into chunks of at most kChunk slots.
+    __shared__ int whist[32][64];
+    __shared__ int bucket_off[64];
+    __shared__ int sorted[kMaxExperts];
+    const int lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < 32 * 64; i += blockDim.x) whist[i / 64][i % 64] = 0;
+    __syncthreads();
+    const int e = tid;
+    const int cnt = e < E ? g.counts[e] : 0;
+    const int b = cnt > 0 ? 63 - min(cnt, 63) : -1;
+    if (b >= 0) atomicAdd(&whist[warp][b], 1);
+    __syncthreads();
+    if (tid < 64) {
+        int acc = 0;
+        for (int w = 0; w < 32; w++) {
+            const int t = whist[w][tid];
+            whist[w][tid] = acc;
+            acc += t;
+        }
+        bucket_off[tid] = acc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int off = 0;
+        for (int i = 0; i < 64; i++) {
+            const int t = bucket_off[i];
+            bucket_off[i] = off;
+            off += t;
+        }
+    }
+    __syncthreads();
+    const uint32_t same = __match_any_sync(0xffffffffu, b);
+    if (b >= 0) sorted[bucket_off[b] + whist[warp][b] + __popc(same & lanemask_lt())] = e;
+    __syncthreads();
+    const int n_active = g.n_active[0];
+    const int ej = tid < n_active ? sorted[tid] : -1;
+    const int cj = ej >= 0 ? g.counts[ej] : 0;
+    const int nch = (cj + kChunk - 1) / kChunk;
+    int total = 0;
+    const int off = block_excl_scan(nch, warp_sums, &total);
+    if (ej >= 0) {
+        const int base = g.offsets[ej];
+        for (int c = 0; c < nch; c++) {
+            sched.e[off + c] = ej;
+            sched.beg[off + c] = base + c * kChunk;
+            sched.n[off + c] = min(kChunk, cj - c * kChunk);
+        }
+    }
+    if (tid == 0) sched.count[0] = total;
 }
 
 cudaError_t launch_group(const int32_t* ids, int T, int k, int E, GroupTables g, int32_t* slot, int32_t* src,
-                         cudaStream_t s) {
-    group_kernel<<<1, 1024, 0, s>>>(ids, T, k, E, g, slot, src);
+                         cudaStream_t s, const Sched* sched) {
+    group_kernel<<<1, 1024, 0, s>>>(ids, T, k, E, g, slot, src, sched ? *sched : Sched{}, sched ? 1 : 0);
     return cudaGetLastError();
 }
 

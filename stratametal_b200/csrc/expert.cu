@@ -1,9 +1,10 @@
 // expert.cu - dequant-fused grouped expert GEMVs on sm_100a (rows a5-a9 of the block).
 //
-// Work is grouped by expert: every (expert, row tile) item stages its weight rows into shared memory with
-// one bulk copy (cp.async.bulk, the TMA engine without a tensor map: 16-byte aligned tiles of whole rows),
-// keeps its rows' codes in registers, and walks the expert's tokens (slots).  Each weight byte is read from
-// HBM once per launch however many tokens the expert has.
+// Work is grouped by expert: every (expert, row tile) item is one bulk copy (cp.async.bulk, the TMA engine
+// without a tensor map: a 16-byte aligned tile of whole rows) into a ring of kStages shared-memory stages, so
+// a CTA keeps several tiles in flight while it computes.  Each warp decodes its rows' codes into registers
+// once per item and walks the expert's tokens (slots).  Each weight byte is read from HBM once per launch
+// however many tokens the expert has.
 //
 // Summation order.  Row r against a q8_1 column is the reference's iq_mmvq (iq.metal:459-514) and its host
 // transcription row_dot (iq_parity.cpp:275-292): the 32-value partial k (a Q2_0 half block, an IQ2_S 32-group)
@@ -13,10 +14,10 @@
 // every row's sum is formed from the same pairs as the reference's butterfly.  The result is bitwise the host
 // reference.
 //
-// Q2_0 integer dot.  A qs word holds 16 codes (4 per byte, LSB first).  Instead of unpacking codes to bytes,
-// the activation is re-laid out once per token so that byte b of word j holds value 4b + j of a 16-value run;
-// then (qs & (3 << 2j)) against that word is a dp4a of code * 4^j, and
-//   sum (code - 1) q = sum_j (dp4a_j >> 2j) - sum q       (exact integer arithmetic).
+// Q2_0 integer dot.  A qs word holds 16 codes (4 per byte, LSB first).  (qs >> 2j) & 0x03030303 holds, in
+// byte b, the code of value 4b + j; the activation is re-laid out once per token to match (byte b of word j
+// = value 4b + j of a 16-value run), so eight chained dp4a give sum code * q exactly and
+//   sum (code - 1) q = sum code * q - sum q       (exact integer arithmetic; sum q is staged per block).
 #include "common.cuh"
 #include "kernels.cuh"
 #include "q8.cuh"
@@ -29,8 +30,8 @@ __device__ const uint64_t k_iq2s_grid_dev[1024] = {
 #include "iq2s_grid.inc"
 };
 
-constexpr int kThreads = 256;  // 8 warps
 constexpr int kSlotChunk = 8;  // tokens staged per pass
+constexpr int kStages = 4;     // weight tiles in flight per CTA
 
 // ------------------------------------------------------------------------------------------------
 // group helpers
@@ -68,7 +69,7 @@ __device__ __forceinline__ int slot_token(const GroupView& g, const Item& it, in
 }
 
 // ------------------------------------------------------------------------------------------------
-// shared-memory loads and the partial dots
+// shared-memory loads, decoding and the partial dots
 // ------------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t lds_u32_unaligned(const uint8_t* p) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(p);
@@ -79,79 +80,97 @@ __device__ __forceinline__ uint32_t lds_u32_unaligned(const uint8_t* p) {
 
 __device__ __forceinline__ uint16_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
 
-// One staged q8_1 block: 8 words (re-laid out for Q2_0, natural order for IQ2_S), d as f32, sum of the q.
-struct ActBlock {
-    uint32_t w[8];
-};
-
-// Q2_0 weights of one partial (a 32-value half block): two qs words and d.
-struct Q2W {
-    uint32_t w0, w1;
+// One 32-value partial of a weight row, decoded: eight code words that pair with the eight staged
+// activation words of the matching q8_1 block, the block scale, and (IQ2_S) the two 4-bit sub-scales.
+struct Dec {
+    uint32_t c[8];
     float d;
+    uint32_t ls;
 };
 
-__device__ __forceinline__ Q2W q2_weights(const uint8_t* row, int k) {
+// Q2_0 half block k & 1 of block k >> 1: c[j] = codes of values 4b + j (j < 4) of the first 16 values,
+// c[4 + j] the same for the last 16.
+__device__ __forceinline__ void decode_q2(const uint8_t* row, int k, Dec& w) {
     const uint8_t* blk = row + (k >> 1) * 18;
-    Q2W q;
-    q.d = f16_to_f32(lds_u16(blk));
-    const uint8_t* qs = blk + 2 + 8 * (k & 1);
-    q.w0 = lds_u32_unaligned(qs);
-    q.w1 = lds_u32_unaligned(qs + 4);
-    return q;
-}
-
-__device__ __forceinline__ float q2_partial(const Q2W& q, const uint32_t* a, float dx, int qsum) {
-    const int s0 = dp4a_us(q.w1 & 0x03030303u, (int) a[4], dp4a_us(q.w0 & 0x03030303u, (int) a[0], 0));
-    const int s1 = dp4a_us(q.w1 & 0x0C0C0C0Cu, (int) a[5], dp4a_us(q.w0 & 0x0C0C0C0Cu, (int) a[1], 0));
-    const int s2 = dp4a_us(q.w1 & 0x30303030u, (int) a[6], dp4a_us(q.w0 & 0x30303030u, (int) a[2], 0));
-    const int s3 = dp4a_us(q.w1 & 0xC0C0C0C0u, (int) a[7], dp4a_us(q.w0 & 0xC0C0C0C0u, (int) a[3], 0));
-    const int sumi = s0 + (s1 >> 2) + (s2 >> 4) + (s3 >> 6) - qsum;
-    return __fmul_rn(__fmul_rn(q.d, dx), (float) sumi);
-}
-
-// IQ2_S weights of one partial (32-group g of a 256-block): qs word, sign word, qh and scale bytes, d.
-struct S2W {
-    uint32_t qs, sg, hs;  // hs = qh | scale << 8
-    float d;
-};
-
-__device__ __forceinline__ S2W s2_weights(const uint8_t* row, int k) {
-    const uint8_t* blk = row + (k >> 3) * 82;
-    const int g = k & 7;
-    S2W w;
     w.d = f16_to_f32(lds_u16(blk));
-    w.qs = lds_u32_unaligned(blk + 2 + 4 * g);
-    w.sg = lds_u32_unaligned(blk + 34 + 4 * g);
-    w.hs = (uint32_t) blk[66 + g] | ((uint32_t) blk[74 + g] << 8);
-    return w;
+    const uint8_t* qs = blk + 2 + 8 * (k & 1);
+    const uint32_t w0 = lds_u32_unaligned(qs), w1 = lds_u32_unaligned(qs + 4);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        w.c[j] = (w0 >> (2 * j)) & 0x03030303u;
+        w.c[4 + j] = (w1 >> (2 * j)) & 0x03030303u;
+    }
+    w.ls = 0;
 }
 
 // Bytes 0xFF where bit m of the 4-bit s is set (m = byte index).
 __device__ __forceinline__ uint32_t sign_mask4(uint32_t s) { return ((s * 0x00204081u) & 0x01010101u) * 0xFFu; }
 
-// IQ2_S partial (iq_parity.cpp:125-151): the codebook magnitudes are never 0, so negating a byte as
-// (m ^ 0xFF) + 1 never carries into its neighbour.
-__device__ __forceinline__ float s2_partial(const S2W& w, const uint32_t* a, float dx, const uint64_t* grid) {
-    int sum0 = 0, sum1 = 0;
+// IQ2_S 32-group k & 7 of block k >> 3 (format iq.metal:152-180): each 8-value chunk j is codebook entry
+// qs[4g + j] | ((qh[g] >> 2j) & 3) << 8, value m negated when bit m of signs[4g + j] is set.  The codebook
+// magnitudes are never 0, so negating a byte as (m ^ 0xFF) + 1 never carries into its neighbour.
+__device__ __forceinline__ void decode_s2(const uint8_t* row, int k, const uint64_t* grid, Dec& w) {
+    const uint8_t* blk = row + (k >> 3) * 82;
+    const int g = k & 7;
+    w.d = f16_to_f32(lds_u16(blk));
+    const uint32_t qs = lds_u32_unaligned(blk + 2 + 4 * g);
+    const uint32_t sg = lds_u32_unaligned(blk + 34 + 4 * g);
+    const uint32_t qh = blk[66 + g];
+    const uint32_t sc = blk[74 + g];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-        const uint32_t idx = ((w.qs >> (8 * j)) & 0xFFu) | (((w.hs >> (2 * j)) & 3u) << 8);
+        const uint32_t idx = ((qs >> (8 * j)) & 0xFFu) | (((qh >> (2 * j)) & 3u) << 8);
         const uint64_t e = grid[idx];
-        const uint32_t sb = (w.sg >> (8 * j)) & 0xFFu;
+        const uint32_t sb = (sg >> (8 * j)) & 0xFFu;
         const uint32_t mlo = sign_mask4(sb & 0xFu), mhi = sign_mask4(sb >> 4);
-        const uint32_t vlo = ((uint32_t) e ^ mlo) + (mlo & 0x01010101u);
-        const uint32_t vhi = ((uint32_t) (e >> 32) ^ mhi) + (mhi & 0x01010101u);
-        const int s = dp4a_ss((int) vhi, (int) a[2 * j + 1], dp4a_ss((int) vlo, (int) a[2 * j], 0));
-        if (j < 2) sum0 += s;
-        else sum1 += s;
+        w.c[2 * j] = ((uint32_t) e ^ mlo) + (mlo & 0x01010101u);
+        w.c[2 * j + 1] = ((uint32_t) (e >> 32) ^ mhi) + (mhi & 0x01010101u);
     }
-    const int sc = (int) (w.hs >> 8);
-    const int ls0 = sc & 0x0F, ls1 = sc >> 4;
-    const int sumi = (sum0 * ls0 + sum1 * ls1 + (sum0 + sum1) / 2) / 4;
-    return __fmul_rn(__fmul_rn(w.d, dx), (float) sumi);
+    w.ls = (sc & 0x0Fu) | ((sc >> 4) << 8);
 }
 
-// Stage one q8_1 block (36 bytes at src, 4-byte aligned) into the kernel layout.
+template <int TYPE>
+__device__ __forceinline__ void decode(const uint8_t* row, int k, const uint64_t* grid, Dec& w) {
+    if constexpr (TYPE == kQ2_0) decode_q2(row, k, w);
+    else decode_s2(row, k, grid, w);
+}
+
+// (float) v for |v| < 2^22 with two full-rate ops instead of a conversion: 1.5 * 2^23 + v is exact in f32.
+__device__ __forceinline__ float int_to_float_exact(int v) {
+    return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f);
+}
+
+// The partial (d_w * d_x) * sumi with the reference's two float multiplies (iq_parity.cpp:148-150, 247-251).
+template <int TYPE>
+__device__ __forceinline__ float partial(const Dec& w, const uint4& a0, const uint4& a1, float dx, int qsum) {
+    int sumi;
+    if constexpr (TYPE == kQ2_0) {
+        int s = dp4a_us(w.c[0], (int) a0.x, 0);
+        s = dp4a_us(w.c[1], (int) a0.y, s);
+        s = dp4a_us(w.c[2], (int) a0.z, s);
+        s = dp4a_us(w.c[3], (int) a0.w, s);
+        s = dp4a_us(w.c[4], (int) a1.x, s);
+        s = dp4a_us(w.c[5], (int) a1.y, s);
+        s = dp4a_us(w.c[6], (int) a1.z, s);
+        s = dp4a_us(w.c[7], (int) a1.w, s);
+        sumi = s - qsum;
+    } else {
+        int s0 = dp4a_ss((int) w.c[0], (int) a0.x, 0);
+        s0 = dp4a_ss((int) w.c[1], (int) a0.y, s0);
+        s0 = dp4a_ss((int) w.c[2], (int) a0.z, s0);
+        s0 = dp4a_ss((int) w.c[3], (int) a0.w, s0);
+        int s1 = dp4a_ss((int) w.c[4], (int) a1.x, 0);
+        s1 = dp4a_ss((int) w.c[5], (int) a1.y, s1);
+        s1 = dp4a_ss((int) w.c[6], (int) a1.z, s1);
+        s1 = dp4a_ss((int) w.c[7], (int) a1.w, s1);
+        const int ls0 = (int) (w.ls & 0xFFu), ls1 = (int) (w.ls >> 8);
+        sumi = (s0 * ls0 + s1 * ls1 + (s0 + s1) / 2) / 4;
+    }
+    return __fmul_rn(__fmul_rn(w.d, dx), int_to_float_exact(sumi));
+}
+
+// Stage one q8_1 block (36 bytes at src, 4-byte aligned): Q2_0 gets the code-matched layout (byte b of word
+// j = value 4b + j of each 16-value run), IQ2_S the natural order; also d as f32 and the sum of the q.
 template <int TYPE>
 __device__ __forceinline__ void stage_block(const uint8_t* __restrict__ src, uint32_t* __restrict__ dst_w,
                                             float* __restrict__ dst_d, int* __restrict__ dst_s) {
@@ -162,22 +181,25 @@ __device__ __forceinline__ void stage_block(const uint8_t* __restrict__ src, uin
     int qs = 0;
 #pragma unroll
     for (int i = 0; i < 8; i++) qs = dp4a_ss((int) x[i], 0x01010101, qs);
+    uint32_t o[8];
     if (TYPE == kQ2_0) {
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             const uint32_t* X = x + 4 * h;
             const uint32_t t0 = __byte_perm(X[0], X[1], 0x5140), t1 = __byte_perm(X[2], X[3], 0x5140);
             const uint32_t t2 = __byte_perm(X[0], X[1], 0x7362), t3 = __byte_perm(X[2], X[3], 0x7362);
-            dst_w[4 * h + 0] = __byte_perm(t0, t1, 0x5410);
-            dst_w[4 * h + 1] = __byte_perm(t0, t1, 0x7632);
-            dst_w[4 * h + 2] = __byte_perm(t2, t3, 0x5410);
-            dst_w[4 * h + 3] = __byte_perm(t2, t3, 0x7632);
+            o[4 * h + 0] = __byte_perm(t0, t1, 0x5410);
+            o[4 * h + 1] = __byte_perm(t0, t1, 0x7632);
+            o[4 * h + 2] = __byte_perm(t2, t3, 0x5410);
+            o[4 * h + 3] = __byte_perm(t2, t3, 0x7632);
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 8; i++) dst_w[i] = x[i];
+        for (int i = 0; i < 8; i++) o[i] = x[i];
     }
-    *dst_d = f16_to_f32((uint16_t) (s32[0] & 0xFFFFu));
+    reinterpret_cast<uint4*>(dst_w)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    reinterpret_cast<uint4*>(dst_w)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    *dst_d = f16_to_f32((uint16_t) (__ldg(s32) & 0xFFFFu));
     *dst_s = qs;
 }
 
@@ -208,215 +230,140 @@ __device__ __forceinline__ void tbfly(float (&v)[NV], int lane) {
 }
 
 // ------------------------------------------------------------------------------------------------
-// gate/up + SwiGLU + q8_1 of h.  Item = (expert, 32-row tile of n_ff).  Warp w owns tile rows w, w+8,
-// w+16, w+24 of both gate and up; lane L owns partials L, L+32, ... (PPL of them).
+// The tile ring.  Thread 0 issues item i + kStages - 1 at the top of iteration i into the stage that item
+// i - 1 released (every thread passed the barrier at the end of iteration i - 1).  Waits are bounded: on a
+// timeout the status word is set, thread 0 waits (bounded again) for every copy still in flight, and the CTA
+// returns.
 // ------------------------------------------------------------------------------------------------
-template <int TYPE, int PPL>
-__global__ void __launch_bounds__(kThreads) expert_gate_up_kernel(Matrix gate, Matrix up, Matrix sgate, Matrix sup,
-                                                                  GroupView g, const uint8_t* __restrict__ xq,
-                                                                  uint8_t* __restrict__ hq, int H, int F) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int rb = (TYPE == kQ2_0) ? (H / 64) * 18 : (H / 256) * 82;
-    const int nblk = H / 32;                 // q8_1 blocks of a token = partials of a row
-    const int tile_bytes = 32 * rb;
-    uint8_t* wbuf = smem;                                                      // [2][32][rb]
-    uint32_t* aw = reinterpret_cast<uint32_t*>(smem + ((2 * tile_bytes + 16 + 127) & ~127));  // [chunk][nblk][8]
-    float* ad = reinterpret_cast<float*>(aw + kSlotChunk * nblk * 8);          // [chunk][nblk]
-    int* as = reinterpret_cast<int*>(ad + kSlotChunk * nblk);                  // [chunk][nblk]
-    float* htile = reinterpret_cast<float*>(as + kSlotChunk * nblk);           // [chunk][32]
-    uint64_t* grid_s = reinterpret_cast<uint64_t*>(htile + kSlotChunk * 32);   // [1024] (IQ2_S)
-    uint64_t* bar = grid_s + (TYPE == kIQ2_S ? 1024 : 0);
-    __shared__ int s_ok;
+struct Ring {
+    uint8_t* base;
+    uint32_t stage_bytes;
+    uint64_t* bars;
+};
 
-    if (TYPE == kIQ2_S)
-        for (int i = tid; i < 1024; i += kThreads) grid_s[i] = k_iq2s_grid_dev[i];
-    if (tid == 0) {
-        mbar_init(bar, 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
-
-    const int n_tiles = F / 32;
-    const int n_items = group_count(g) * n_tiles;
-    const int hq_row = (F / 32) * kQ8Block;
-    uint32_t phase = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int j = item / n_tiles, tt = item % n_tiles;
-        const Item it = group_item(g, j);
-        const uint8_t* gsrc = it.shared ? sgate.base : gate.base + (int64_t) it.e * gate.expert_stride;
-        const uint8_t* usrc = it.shared ? sup.base : up.base + (int64_t) it.e * up.expert_stride;
-        if (tid == 0) {
-            fence_proxy_async();
-            mbar_expect_tx(bar, 2u * (uint32_t) tile_bytes);
-            bulk_g2s(wbuf, gsrc + (int64_t) tt * tile_bytes, (uint32_t) tile_bytes, bar);
-            bulk_g2s(wbuf + tile_bytes, usrc + (int64_t) tt * tile_bytes, (uint32_t) tile_bytes, bar);
-            bool ok = mbar_wait_bounded(bar, phase, kWaitLimitNs);
-            if (!ok) {
-                atomicOr(&g_smoe_status, kDevTimeout);
-                mbar_wait_bounded(bar, phase, kWaitLimitNs);
-            }
-            s_ok = ok ? 1 : 0;
-        }
-        __syncthreads();
-        if (!s_ok) return;
-        (void) mbar_try_wait(bar, phase);  // acquire the copied bytes in every thread
-        phase ^= 1u;
-
-        // this warp's rows: tile rows warp + 8 i, i = 0..3, of gate (v[i]) and up (v[4 + i])
-        using WT = typename std::conditional<TYPE == kQ2_0, Q2W, S2W>::type;
-        WT wg[4][PPL], wu[4][PPL];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint8_t* rg = wbuf + (warp + 8 * i) * rb;
-            const uint8_t* ru = wbuf + tile_bytes + (warp + 8 * i) * rb;
-#pragma unroll
-            for (int p = 0; p < PPL; p++) {
-                const int k = lane + 32 * p;
-                if (k < nblk) {
-                    if constexpr (TYPE == kQ2_0) { wg[i][p] = q2_weights(rg, k); wu[i][p] = q2_weights(ru, k); }
-                    else { wg[i][p] = s2_weights(rg, k); wu[i][p] = s2_weights(ru, k); }
-                }
-            }
-        }
-
-        for (int c0 = it.beg; c0 < it.end; c0 += kSlotChunk) {
-            const int nc = min(kSlotChunk, it.end - c0);
-            __syncthreads();  // previous chunk's staging and htile are consumed
-            for (int q = tid; q < nc * nblk; q += kThreads) {
-                const int s = q / nblk, b = q % nblk;
-                const int tok = slot_token(g, it, c0 + s);
-                stage_block<TYPE>(xq + ((int64_t) tok * nblk + b) * kQ8Block, aw + (s * nblk + b) * 8,
-                                  ad + s * nblk + b, as + s * nblk + b);
-            }
-            __syncthreads();
-            for (int s = 0; s < nc; s++) {
-                float v[8];
-#pragma unroll
-                for (int i = 0; i < 8; i++) v[i] = 0.f;
-#pragma unroll
-                for (int p = 0; p < PPL; p++) {
-                    const int k = lane + 32 * p;
-                    if (k < nblk) {
-                        const uint32_t* a = aw + (s * nblk + k) * 8;
-                        uint32_t av[8];
-#pragma unroll
-                        for (int q = 0; q < 8; q++) av[q] = a[q];
-                        const float dx = ad[s * nblk + k];
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            if constexpr (TYPE == kQ2_0) {
-                                const int qsum = as[s * nblk + k];
-                                v[i] = __fadd_rn(v[i], q2_partial(wg[i][p], av, dx, qsum));
-                                v[4 + i] = __fadd_rn(v[4 + i], q2_partial(wu[i][p], av, dx, qsum));
-                            } else {
-                                v[i] = __fadd_rn(v[i], s2_partial(wg[i][p], av, dx, grid_s));
-                                v[4 + i] = __fadd_rn(v[4 + i], s2_partial(wu[i][p], av, dx, grid_s));
-                            }
-                        }
-                    }
-                }
-                tbfly<8, 16>(v, lane);
-                // lane holds output 4*b4 + 2*b3 + b2: b4 = 0 gate, 1 up; row i = 2*b3 + b2
-                const float other = __shfl_xor_sync(0xffffffffu, v[0], 16);
-                if ((lane & 19) == 0) {
-                    const int i = (lane >> 2) & 3;
-                    htile[s * 32 + warp + 8 * i] = silu_mul(v[0], other);
-                }
-            }
-            __syncthreads();
-            for (int s = warp; s < nc; s += kThreads / 32)
-                quant_q8_1_warp(htile[s * 32 + lane], hq + (int64_t) (c0 + s) * hq_row + tt * kQ8Block, lane);
-        }
-        __syncthreads();  // every thread is done with wbuf before the next copy is issued
-    }
+__device__ __forceinline__ void ring_issue(const Ring& r, int i, const uint8_t* src0, uint32_t bytes0,
+                                           const uint8_t* src1, uint32_t bytes1) {
+    const int st = i % kStages;
+    uint8_t* dst = r.base + (size_t) st * r.stage_bytes;
+    const uint32_t b0 = bytes0 & ~15u, b1 = bytes1 & ~15u;
+    // a ragged tail (rows whose bytes are not a multiple of 16) by plain loads, nothing past the matrix
+    for (uint32_t b = b0; b < bytes0; b++) dst[b] = src0[b];
+    fence_proxy_async();
+    mbar_expect_tx(&r.bars[st], b0 + b1);
+    if (b0) bulk_g2s(dst, src0, b0, &r.bars[st]);
+    if (b1) bulk_g2s(dst + bytes0, src1, b1, &r.bars[st]);
 }
 
+// Thread 0 waits for item i; every thread then acquires it.  Returns false (for every thread) on timeout.
+__device__ __forceinline__ bool ring_wait(const Ring& r, int i, int issued, int* s_ok) {
+    const int st = i % kStages;
+    const uint32_t parity = (uint32_t) ((i / kStages) & 1);
+    if (threadIdx.x == 0) {
+        bool ok = mbar_wait_bounded(&r.bars[st], parity, kWaitLimitNs);
+        if (!ok) {
+            atomicOr(&g_smoe_status, kDevTimeout);
+            for (int j = i; j < issued; j++)
+                mbar_wait_bounded(&r.bars[j % kStages], (uint32_t) ((j / kStages) & 1), kWaitLimitNs);
+        }
+        *s_ok = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (!*s_ok) return false;
+    (void) mbar_try_wait(&r.bars[st], parity);  // acquire the copied bytes in every thread
+    return true;
+}
+
+constexpr int kGuThreads = 512;
+
 // ------------------------------------------------------------------------------------------------
-// Matrix rows against staged q8_1 columns: y[slot][r] = W_e[r] . act[row(slot)].
-// Lane groups of LPR lanes own one row each in RPG rows; lane l of a group owns partials l, l + LPR, ...
-// (PPL of them).  LPR = 16 is exact against the reference when a row has at most 16 partials: its lanes
-// 16..31 hold zeros and the butterfly's first level adds nothing.
+// Matrix rows against staged q8_1 columns: y[slot][r] = W_e[r] . act[row(slot)].  This is the stage entry
+// point's kernel (smoe_iq_mmvq: one matrix, columns in the standard q8_1 layout staged through shared memory);
+// the layer path uses layer_gate_up_kernel / layer_down_kernel below.
+// Lane groups of LPR lanes own RPG rows each; lane l of a group owns partials l, l + LPR, ... (PPL of them).
+// LPR = 16 is exact against the reference when a row has at most 16 partials: its lanes 16..31 hold zeros
+// and the butterfly's first level adds nothing.
 // ------------------------------------------------------------------------------------------------
+constexpr int kRowThreads = 256;
+
 template <int TYPE, int LPR, int PPL>
-__global__ void __launch_bounds__(kThreads) expert_rows_kernel(Matrix wm, Matrix swm, GroupView g,
-                                                               const uint8_t* __restrict__ act, int act_by_token,
-                                                               float* __restrict__ y, int64_t y_stride, int n_in,
-                                                               int n_out) {
+__global__ void __launch_bounds__(kRowThreads) expert_rows_kernel(Matrix wm, Matrix swm, GroupView g,
+                                                                  const uint8_t* __restrict__ act, int act_by_token,
+                                                                  float* __restrict__ y, int64_t y_stride, int n_in,
+                                                                  int n_out) {
     constexpr int RPG = 4;
     constexpr int GROUPS = 32 / LPR;
-    constexpr int ROWS = (kThreads / 32) * GROUPS * RPG;  // rows per tile
+    constexpr int ROWS = (kRowThreads / 32) * GROUPS * RPG;  // rows per tile
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int grp = lane / LPR, gl = lane % LPR;
     const int rb = (TYPE == kQ2_0) ? (n_in / 64) * 18 : (n_in / 256) * 82;
     const int nblk = n_in / 32;
-    uint8_t* wbuf = smem;  // [ROWS][rb] (+16 slack)
-    uint32_t* aw = reinterpret_cast<uint32_t*>(smem + ((ROWS * rb + 16 + 127) & ~127));
+    const uint32_t stage_bytes = ((uint32_t) (ROWS * rb) + 16u + 127u) & ~127u;
+    Ring ring{smem, stage_bytes, nullptr};
+    uint32_t* aw = reinterpret_cast<uint32_t*>(smem + (size_t) kStages * stage_bytes);
     float* ad = reinterpret_cast<float*>(aw + kSlotChunk * nblk * 8);
     int* as = reinterpret_cast<int*>(ad + kSlotChunk * nblk);
     uint64_t* grid_s = reinterpret_cast<uint64_t*>(as + kSlotChunk * nblk + 2);
-    uint64_t* bar = grid_s + (TYPE == kIQ2_S ? 1024 : 0);
+    ring.bars = grid_s + (TYPE == kIQ2_S ? 1024 : 0);
     __shared__ int s_ok;
 
     if (TYPE == kIQ2_S)
-        for (int i = tid; i < 1024; i += kThreads) grid_s[i] = k_iq2s_grid_dev[i];
+        for (int i = tid; i < 1024; i += kRowThreads) grid_s[i] = k_iq2s_grid_dev[i];
     if (tid == 0) {
-        mbar_init(bar, 1);
+        for (int i = 0; i < kStages; i++) mbar_init(&ring.bars[i], 1);
         fence_mbar_init();
     }
     __syncthreads();
 
     const int n_tiles = (n_out + ROWS - 1) / ROWS;
     const int n_items = group_count(g) * n_tiles;
-    uint32_t phase = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int j = item / n_tiles, tt = item % n_tiles;
-        const Item it = group_item(g, j);
-        const uint8_t* src = it.shared ? swm.base : wm.base + (int64_t) it.e * wm.expert_stride;
+    const int my_n = blockIdx.x < n_items ? (n_items - 1 - (int) blockIdx.x) / (int) gridDim.x + 1 : 0;
+    auto item_src = [&](int i, uint32_t* bytes) -> const uint8_t* {
+        const int item = blockIdx.x + i * gridDim.x;
+        const int tt = item % n_tiles;
+        const Item it = group_item(g, item / n_tiles);
+        const int r0 = tt * ROWS;
+        *bytes = (uint32_t) (min(ROWS, n_out - r0) * rb);
+        return (it.shared ? swm.base : wm.base + (int64_t) it.e * wm.expert_stride) + (int64_t) r0 * rb;
+    };
+    int issued = 0;
+    if (tid == 0) {
+        for (; issued < kStages - 1 && issued < my_n; issued++) {
+            uint32_t bytes;
+            const uint8_t* src = item_src(issued, &bytes);
+            ring_issue(ring, issued, src, bytes, nullptr, 0);
+        }
+    }
+    for (int i = 0; i < my_n; i++) {
+        if (tid == 0 && issued < my_n) {
+            uint32_t bytes;
+            const uint8_t* src = item_src(issued, &bytes);
+            ring_issue(ring, issued, src, bytes, nullptr, 0);
+            issued++;
+        }
+        if (!ring_wait(ring, i, issued, &s_ok)) return;
+        const int item = blockIdx.x + i * gridDim.x;
+        const int tt = item % n_tiles;
+        const Item it = group_item(g, item / n_tiles);
         const int r0 = tt * ROWS;
         const int nrows = min(ROWS, n_out - r0);
-        // whole 16-byte units by one bulk copy; a ragged tail (rows whose bytes are not a multiple of 16)
-        // by plain loads, so nothing past the matrix is read
-        const uint32_t bytes = (uint32_t) (nrows * rb);
-        const uint32_t bulk = bytes & ~15u;
-        for (uint32_t b = bulk + tid; b < bytes; b += kThreads) wbuf[b] = src[(int64_t) r0 * rb + b];
-        if (tid == 0) {
-            fence_proxy_async();
-            mbar_expect_tx(bar, bulk);
-            if (bulk) bulk_g2s(wbuf, src + (int64_t) r0 * rb, bulk, bar);
-            bool ok = mbar_wait_bounded(bar, phase, kWaitLimitNs);
-            if (!ok) {
-                atomicOr(&g_smoe_status, kDevTimeout);
-                mbar_wait_bounded(bar, phase, kWaitLimitNs);
-            }
-            s_ok = ok ? 1 : 0;
-        }
-        __syncthreads();
-        if (!s_ok) return;
-        (void) mbar_try_wait(bar, phase);
-        phase ^= 1u;
+        const uint8_t* wt = ring.base + (size_t) (i % kStages) * stage_bytes;
 
-        using WT = typename std::conditional<TYPE == kQ2_0, Q2W, S2W>::type;
-        WT wr[RPG][PPL];
+        Dec wr[RPG][PPL];
         const int row_base = (warp * GROUPS + grp) * RPG;  // tile row of this group's v[0]
 #pragma unroll
-        for (int i = 0; i < RPG; i++) {
-            const int r = min(row_base + i, nrows - 1);
-            const uint8_t* rp = wbuf + r * rb;
+        for (int q = 0; q < RPG; q++) {
+            const uint8_t* rp = wt + min(row_base + q, nrows - 1) * rb;
 #pragma unroll
             for (int p = 0; p < PPL; p++) {
                 const int k = gl + LPR * p;
-                if (k < nblk) {
-                    if constexpr (TYPE == kQ2_0) wr[i][p] = q2_weights(rp, k);
-                    else wr[i][p] = s2_weights(rp, k);
-                }
+                if (k < nblk) decode<TYPE>(rp, k, grid_s, wr[q][p]);
             }
         }
         for (int c0 = it.beg; c0 < it.end; c0 += kSlotChunk) {
             const int nc = min(kSlotChunk, it.end - c0);
             __syncthreads();
-            for (int q = tid; q < nc * nblk; q += kThreads) {
+            for (int q = tid; q < nc * nblk; q += kRowThreads) {
                 const int s = q / nblk, b = q % nblk;
                 const int arow = act_by_token ? slot_token(g, it, c0 + s) : c0 + s;
                 stage_block<TYPE>(act + ((int64_t) arow * nblk + b) * kQ8Block, aw + (s * nblk + b) * 8,
@@ -426,36 +373,290 @@ __global__ void __launch_bounds__(kThreads) expert_rows_kernel(Matrix wm, Matrix
             for (int s = 0; s < nc; s++) {
                 float v[RPG];
 #pragma unroll
-                for (int i = 0; i < RPG; i++) v[i] = 0.f;
+                for (int q = 0; q < RPG; q++) v[q] = 0.f;
 #pragma unroll
                 for (int p = 0; p < PPL; p++) {
                     const int k = gl + LPR * p;
                     if (k < nblk) {
-                        const uint32_t* a = aw + (s * nblk + k) * 8;
-                        uint32_t av[8];
-#pragma unroll
-                        for (int q = 0; q < 8; q++) av[q] = a[q];
+                        const uint4* a = reinterpret_cast<const uint4*>(aw + (s * nblk + k) * 8);
+                        const uint4 a0 = a[0], a1 = a[1];
                         const float dx = ad[s * nblk + k];
+                        const int qsum = as[s * nblk + k];
 #pragma unroll
-                        for (int i = 0; i < RPG; i++) {
-                            if constexpr (TYPE == kQ2_0)
-                                v[i] = __fadd_rn(v[i], q2_partial(wr[i][p], av, dx, as[s * nblk + k]));
-                            else
-                                v[i] = __fadd_rn(v[i], s2_partial(wr[i][p], av, dx, grid_s));
-                        }
+                        for (int q = 0; q < RPG; q++) v[q] = __fadd_rn(v[q], partial<TYPE>(wr[q][p], a0, a1, dx, qsum));
                     }
                 }
                 tbfly<RPG, LPR / 2>(v, lane);
                 // lane holds row 2 * b(LPR/2) + b(LPR/4) of its group; lanes with the low bits clear store
                 constexpr int low_mask = LPR / 4 - 1;
                 if ((gl & low_mask) == 0) {
-                    const int i = (gl / (LPR / 4)) & 3;
-                    const int r = row_base + i;
+                    const int r = row_base + ((gl / (LPR / 4)) & 3);
                     if (r < nrows) y[(int64_t) (c0 + s) * y_stride + r0 + r] = v[0];
                 }
             }
         }
         __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// The layer path.  Items are (work-list entry, row tile): a work-list entry is at most kChunk slots of one
+// expert, entries are ordered heaviest expert first (the shared expert's chunks lead), and CTAs claim items
+// from a counter, so large groups start first and small ones fill in.  Activations come straight from HBM/L2
+// in the KAct layout through the read-only path: no staging and no barrier per token.
+// ------------------------------------------------------------------------------------------------
+struct Entry {
+    int e, beg, n;
+    bool shared;
+};
+
+__device__ __forceinline__ int shared_entries(const Work& w) {
+    return w.shared_slots > 0 ? (w.shared_slots + kChunk - 1) / kChunk : 0;
+}
+
+__device__ __forceinline__ int work_entries(const Work& w) {
+    return shared_entries(w) + (w.no_routed ? 0 : *w.sched.count);
+}
+
+__device__ __forceinline__ Entry work_entry(const Work& w, int j) {
+    Entry en;
+    const int sh = shared_entries(w);
+    if (j < sh) {
+        en.e = -1;
+        en.beg = w.shared_base + j * kChunk;
+        en.n = min(kChunk, w.shared_slots - j * kChunk);
+        en.shared = true;
+    } else {
+        const int jj = j - sh;
+        en.e = w.sched.e[jj];
+        en.beg = w.sched.beg[jj];
+        en.n = w.sched.n[jj];
+        en.shared = false;
+    }
+    return en;
+}
+
+__device__ __forceinline__ int entry_token(const Work& w, const Entry& en, int slot) {
+    return en.shared ? slot - w.shared_base : w.slot_token[slot];
+}
+
+__device__ __forceinline__ int claim(int32_t* counter) { return atomicAdd(counter, 1); }
+
+// Thread 0 waits for item i's stage (bounded); on a timeout it also waits, bounded, for every copy it still
+// has in flight.  Every thread then acquires the stage, or every thread returns false.
+template <int NST>
+__device__ __forceinline__ bool stage_wait(uint64_t* bars, int i, const int* s_item, int n_items, int* s_ok) {
+    const int st = i % NST;
+    const uint32_t parity = (uint32_t) ((i / NST) & 1);
+    if (threadIdx.x == 0) {
+        const bool ok = mbar_wait_bounded(&bars[st], parity, kWaitLimitNs);
+        if (!ok) {
+            atomicOr(&g_smoe_status, kDevTimeout);
+            for (int j = i + 1; j < i + NST; j++)
+                if (s_item[j % NST] < n_items)
+                    mbar_wait_bounded(&bars[j % NST], (uint32_t) ((j / NST) & 1), kWaitLimitNs);
+        }
+        *s_ok = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (!*s_ok) return false;
+    (void) mbar_try_wait(&bars[st], parity);
+    return true;
+}
+
+// One staged activation block (kKaBlock bytes, 16-byte aligned) and a partial against it.
+template <int TYPE>
+__device__ __forceinline__ float partial_ka(const Dec& w, const uint8_t* blk) {
+    const uint4 a0 = reinterpret_cast<const uint4*>(blk)[0];
+    const uint4 a1 = reinterpret_cast<const uint4*>(blk)[1];
+    const float2 ds = reinterpret_cast<const float2*>(blk)[4];
+    return partial<TYPE>(w, a0, a1, ds.x, __float_as_int(ds.y));
+}
+
+constexpr int kGuStages = 3;
+
+// gate/up + SwiGLU + q8_1 of h.  Item = (work entry, 32-row tile of n_ff).  A ring stage holds the gate tile,
+// the up tile and the entry's token activations (one bulk copy each).  16 warps; warp w owns tile rows w and
+// w + 16 of both gate and up; lane L owns partials L, L + 32, ... (PPL of them).
+template <int TYPE, int DQ2, int PPL>
+__global__ void __launch_bounds__(kGuThreads, 1) layer_gate_up_kernel(Matrix gate, Matrix up, Matrix sgate,
+                                                                      Matrix sup, Work w, KAct xa, KAct ha, int H,
+                                                                      int F) {
+    constexpr int NST = kGuStages;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rb = (TYPE == kQ2_0) ? (H / 64) * 18 : (H / 256) * 82;
+    const int nblk = H / 32, nblk_h = F / 32;
+    const uint32_t tile_bytes = 32u * (uint32_t) rb;
+    const uint32_t act_row = (uint32_t) nblk * kKaBlock;
+    const uint32_t stage_bytes = (2u * tile_bytes + kChunk * act_row + 16u + 127u) & ~127u;
+    float* htile = reinterpret_cast<float*>(smem + (size_t) NST * stage_bytes);  // [kChunk][gate 32 | up 32]
+    uint64_t* grid_s = reinterpret_cast<uint64_t*>(htile + kChunk * 64);        // [1024] (IQ2_S)
+    uint64_t* bars = grid_s + (TYPE == kIQ2_S ? 1024 : 0);
+    __shared__ int s_item[NST];
+    __shared__ int s_ok;
+
+    if (TYPE == kIQ2_S)
+        for (int i = tid; i < 1024; i += kGuThreads) grid_s[i] = k_iq2s_grid_dev[i];
+    const int n_tiles = F / 32;
+    const int n_items = work_entries(w) * n_tiles;
+    auto issue = [&](int st) {
+        const int id = claim(w.counter);
+        s_item[st] = id;
+        if (id >= n_items) return;
+        const Entry en = work_entry(w, id / n_tiles);
+        const int64_t off = (int64_t) (id % n_tiles) * tile_bytes;
+        const uint8_t* gs = (en.shared ? sgate.base : gate.base + (int64_t) en.e * gate.expert_stride) + off;
+        const uint8_t* us = (en.shared ? sup.base : up.base + (int64_t) en.e * up.expert_stride) + off;
+        uint8_t* dst = smem + (size_t) st * stage_bytes;
+        fence_proxy_async();
+        mbar_expect_tx(&bars[st], 2u * tile_bytes + (uint32_t) en.n * act_row);
+        bulk_g2s(dst, gs, tile_bytes, &bars[st]);
+        bulk_g2s(dst + tile_bytes, us, tile_bytes, &bars[st]);
+        for (int s = 0; s < en.n; s++) {
+            const int tok = entry_token(w, en, en.beg + s);
+            bulk_g2s(dst + 2 * tile_bytes + s * act_row, xa.base + (size_t) tok * act_row, act_row, &bars[st]);
+        }
+    };
+    if (tid == 0) {
+        for (int i = 0; i < NST; i++) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+        for (int st = 0; st < NST - 1; st++) issue(st);
+    }
+    __syncthreads();
+    for (int i = 0;; i++) {
+        if (tid == 0 && s_item[(i + NST - 2) % NST] < n_items) issue((i + NST - 1) % NST);
+        __syncthreads();
+        const int id = s_item[i % NST];
+        if (id >= n_items) break;
+        if (!stage_wait<NST>(bars, i, s_item, n_items, &s_ok)) return;
+        const Entry en = work_entry(w, id / n_tiles);
+        const int tt = id % n_tiles;
+        const uint8_t* wt = smem + (size_t) (i % NST) * stage_bytes;
+        const uint8_t* acts = wt + 2 * tile_bytes;
+
+        Dec wd[4][PPL];  // v[0] gate row warp, v[1] gate row warp + 16, v[2] up row warp, v[3] up row warp + 16
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint8_t* rp = wt + (q >> 1) * tile_bytes + (warp + 16 * (q & 1)) * rb;
+#pragma unroll
+            for (int p = 0; p < PPL; p++) {
+                const int k = lane + 32 * p;
+                if (k < nblk) decode<TYPE>(rp, k, grid_s, wd[q][p]);
+            }
+        }
+        for (int s = 0; s < en.n; s++) {
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int p = 0; p < PPL; p++) {
+                const int k = lane + 32 * p;
+                if (k < nblk) {
+                    const uint8_t* ab = acts + s * act_row + k * kKaBlock;
+#pragma unroll
+                    for (int q = 0; q < 4; q++) v[q] = __fadd_rn(v[q], partial_ka<TYPE>(wd[q][p], ab));
+                }
+            }
+            tbfly<4, 16>(v, lane);
+            // lane holds output 2*b4 + b3: b4 = 0 gate, 1 up; tile row = warp + 16 * b3
+            if ((lane & 7) == 0) htile[s * 64 + 32 * ((lane >> 4) & 1) + warp + 16 * ((lane >> 3) & 1)] = v[0];
+        }
+        __syncthreads();
+        // SwiGLU then q8_1 of h: one warp per token, one row per lane
+        for (int s = warp; s < en.n; s += kGuThreads / 32)
+            quant_ka_warp(silu_mul(htile[s * 64 + lane], htile[s * 64 + 32 + lane]),
+                          ha.base + ((size_t) (en.beg + s) * nblk_h + tt) * kKaBlock, lane, DQ2 != 0);
+        __syncthreads();  // the stage and htile are free
+    }
+}
+
+constexpr int kDownStages = 4;
+
+// down.  Item = (work entry, ROWS-row tile of n_embd).  A stage holds the tile and the entry's h rows (its
+// slots are contiguous, so one bulk copy).
+template <int TYPE, int LPR, int PPL>
+__global__ void __launch_bounds__(kRowThreads) layer_down_kernel(Matrix wm, Matrix swm, Work w, KAct ha,
+                                                                 float* __restrict__ y, int n_in, int n_out) {
+    constexpr int NST = kDownStages;
+    constexpr int RPG = 4;
+    constexpr int GROUPS = 32 / LPR;
+    constexpr int ROWS = (kRowThreads / 32) * GROUPS * RPG;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int grp = lane / LPR, gl = lane % LPR;
+    const int rb = (TYPE == kQ2_0) ? (n_in / 64) * 18 : (n_in / 256) * 82;
+    const int nblk = n_in / 32;
+    const uint32_t tile_bytes = (uint32_t) (ROWS * rb);
+    const uint32_t act_row = (uint32_t) nblk * kKaBlock;
+    const uint32_t stage_bytes = (tile_bytes + kChunk * act_row + 16u + 127u) & ~127u;
+    uint64_t* grid_s = reinterpret_cast<uint64_t*>(smem + (size_t) NST * stage_bytes);
+    uint64_t* bars = grid_s + (TYPE == kIQ2_S ? 1024 : 0);
+    __shared__ int s_item[NST];
+    __shared__ int s_ok;
+
+    if (TYPE == kIQ2_S)
+        for (int i = tid; i < 1024; i += kRowThreads) grid_s[i] = k_iq2s_grid_dev[i];
+    const int n_tiles = n_out / ROWS;  // the layer check guarantees whole tiles
+    const int n_items = work_entries(w) * n_tiles;
+    auto issue = [&](int st) {
+        const int id = claim(w.counter);
+        s_item[st] = id;
+        if (id >= n_items) return;
+        const Entry en = work_entry(w, id / n_tiles);
+        const int r0 = (id % n_tiles) * ROWS;
+        const uint8_t* src = (en.shared ? swm.base : wm.base + (int64_t) en.e * wm.expert_stride) + (int64_t) r0 * rb;
+        uint8_t* dst = smem + (size_t) st * stage_bytes;
+        fence_proxy_async();
+        mbar_expect_tx(&bars[st], tile_bytes + (uint32_t) en.n * act_row);
+        bulk_g2s(dst, src, tile_bytes, &bars[st]);
+        bulk_g2s(dst + tile_bytes, ha.base + (size_t) en.beg * act_row, (uint32_t) en.n * act_row, &bars[st]);
+    };
+    if (tid == 0) {
+        for (int i = 0; i < NST; i++) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+        for (int st = 0; st < NST - 1; st++) issue(st);
+    }
+    __syncthreads();
+    for (int i = 0;; i++) {
+        if (tid == 0 && s_item[(i + NST - 2) % NST] < n_items) issue((i + NST - 1) % NST);
+        __syncthreads();
+        const int id = s_item[i % NST];
+        if (id >= n_items) break;
+        if (!stage_wait<NST>(bars, i, s_item, n_items, &s_ok)) return;
+        const Entry en = work_entry(w, id / n_tiles);
+        const int r0 = (id % n_tiles) * ROWS;
+        const uint8_t* wt = smem + (size_t) (i % NST) * stage_bytes;
+        const uint8_t* acts = wt + tile_bytes;
+
+        Dec wr[RPG][PPL];
+        const int row_base = (warp * GROUPS + grp) * RPG;
+#pragma unroll
+        for (int q = 0; q < RPG; q++) {
+            const uint8_t* rp = wt + (row_base + q) * rb;
+#pragma unroll
+            for (int p = 0; p < PPL; p++) {
+                const int k = gl + LPR * p;
+                if (k < nblk) decode<TYPE>(rp, k, grid_s, wr[q][p]);
+            }
+        }
+        for (int s = 0; s < en.n; s++) {
+            float v[RPG];
+#pragma unroll
+            for (int q = 0; q < RPG; q++) v[q] = 0.f;
+#pragma unroll
+            for (int p = 0; p < PPL; p++) {
+                const int k = gl + LPR * p;
+                if (k < nblk) {
+                    const uint8_t* ab = acts + s * act_row + k * kKaBlock;
+#pragma unroll
+                    for (int q = 0; q < RPG; q++) v[q] = __fadd_rn(v[q], partial_ka<TYPE>(wr[q][p], ab));
+                }
+            }
+            tbfly<RPG, LPR / 2>(v, lane);
+            constexpr int low_mask = LPR / 4 - 1;
+            if ((gl & low_mask) == 0)
+                y[(int64_t) (en.beg + s) * n_out + r0 + row_base + ((gl / (LPR / 4)) & 3)] = v[0];
+        }
+        __syncthreads();  // the stage is free
     }
 }
 
@@ -474,11 +675,11 @@ static int sm_count() {
 }
 
 template <typename K>
-static cudaError_t launch_persistent(K kernel, size_t smem, int max_items, cudaStream_t s, dim3* out_grid) {
+static cudaError_t launch_persistent(K kernel, int threads, size_t smem, int max_items, dim3* out_grid) {
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     if (err != cudaSuccess) return err;
     int per_sm = 0;
-    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
     if (err != cudaSuccess) return err;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     int blocks = sm_count() * per_sm;
@@ -492,39 +693,6 @@ static int max_groups(const GroupView& g) {
     return (g.no_routed ? 0 : g.max_active) + (g.shared_slots > 0 ? 1 : 0);
 }
 
-cudaError_t launch_expert_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, GroupView g, const uint8_t* xq,
-                                  uint8_t* hq, int n_embd, int n_ff, cudaStream_t s) {
-    const int type = gate.type;
-    const int rb = type == kQ2_0 ? (n_embd / 64) * 18 : (n_embd / 256) * 82;
-    const int nblk = n_embd / 32;
-    size_t smem = ((size_t) (2 * 32 * rb + 16 + 127) & ~(size_t) 127) + (size_t) kSlotChunk * nblk * 40 +
-                  kSlotChunk * 32 * 4 + (type == kIQ2_S ? 8192 : 0) + 16;
-    const int ppl = (nblk + 31) / 32;
-    const int max_items = max_groups(g) * (n_ff / 32);
-    dim3 grid;
-    cudaError_t err;
-#define SMOE_GU(T_, P_)                                                                                        \
-    do {                                                                                                       \
-        err = launch_persistent(expert_gate_up_kernel<T_, P_>, smem, max_items, s, &grid);                    \
-        if (err != cudaSuccess) return err;                                                                    \
-        expert_gate_up_kernel<T_, P_><<<grid, kThreads, smem, s>>>(gate, up, sgate, sup, g, xq, hq, n_embd,    \
-                                                                   n_ff);                                      \
-    } while (0)
-    if (type == kQ2_0) {
-        if (ppl == 1) SMOE_GU(kQ2_0, 1);
-        else if (ppl == 2) SMOE_GU(kQ2_0, 2);
-        else if (ppl == 3) SMOE_GU(kQ2_0, 3);
-        else SMOE_GU(kQ2_0, 4);
-    } else {
-        if (ppl == 1) SMOE_GU(kIQ2_S, 1);
-        else if (ppl == 2) SMOE_GU(kIQ2_S, 2);
-        else if (ppl == 3) SMOE_GU(kIQ2_S, 3);
-        else SMOE_GU(kIQ2_S, 4);
-    }
-#undef SMOE_GU
-    return cudaGetLastError();
-}
-
 cudaError_t launch_expert_down(Matrix down, Matrix sdown, GroupView g, const uint8_t* act, int act_by_token,
                                float* y, int64_t y_stride, int n_in, int n_out, cudaStream_t s) {
     const int type = down.type;
@@ -532,18 +700,19 @@ cudaError_t launch_expert_down(Matrix down, Matrix sdown, GroupView g, const uin
     const int nblk = n_in / 32;
     const int lpr = nblk <= 16 ? 16 : 32;
     const int ppl = (nblk + lpr - 1) / lpr;
-    const int rows = (kThreads / 32) * (32 / lpr) * 4;
-    size_t smem = ((size_t) (rows * rb + 16 + 127) & ~(size_t) 127) + (size_t) kSlotChunk * nblk * 40 + 16 +
-                  (type == kIQ2_S ? 8192 : 0) + 16;
+    const int rows = (kRowThreads / 32) * (32 / lpr) * 4;
+    const size_t stage = ((size_t) rows * rb + 16 + 127) & ~(size_t) 127;
+    const size_t smem = kStages * stage + (size_t) kSlotChunk * nblk * 40 + 16 + (type == kIQ2_S ? 8192 : 0) +
+                        kStages * 8;
     const int max_items = max_groups(g) * ((n_out + rows - 1) / rows);
     dim3 grid;
     cudaError_t err;
 #define SMOE_ROWS(T_, L_, P_)                                                                                  \
     do {                                                                                                       \
-        err = launch_persistent(expert_rows_kernel<T_, L_, P_>, smem, max_items, s, &grid);                   \
+        err = launch_persistent(expert_rows_kernel<T_, L_, P_>, kRowThreads, smem, max_items, &grid);         \
         if (err != cudaSuccess) return err;                                                                    \
-        expert_rows_kernel<T_, L_, P_><<<grid, kThreads, smem, s>>>(down, sdown, g, act, act_by_token, y,      \
-                                                                    y_stride, n_in, n_out);                    \
+        expert_rows_kernel<T_, L_, P_><<<grid, kRowThreads, smem, s>>>(down, sdown, g, act, act_by_token, y,   \
+                                                                       y_stride, n_in, n_out);                 \
     } while (0)
     if (type == kQ2_0) {
         if (lpr == 16) SMOE_ROWS(kQ2_0, 16, 1);
@@ -559,6 +728,88 @@ cudaError_t launch_expert_down(Matrix down, Matrix sdown, GroupView g, const uin
         else SMOE_ROWS(kIQ2_S, 32, 4);
     }
 #undef SMOE_ROWS
+    return cudaGetLastError();
+}
+
+}  // namespace smoe
+
+namespace smoe {
+
+static int max_work_entries(const Work& w) {
+    return (w.no_routed ? 0 : w.max_entries) + (w.shared_slots > 0 ? (w.shared_slots + kChunk - 1) / kChunk : 0);
+}
+
+cudaError_t launch_layer_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, Work w, KAct xa, KAct ha,
+                                 int down_q2, int n_embd, int n_ff, cudaStream_t s) {
+    const int type = gate.type;
+    const int rb = type == kQ2_0 ? (n_embd / 64) * 18 : (n_embd / 256) * 82;
+    const int nblk = n_embd / 32;
+    const size_t stage = ((size_t) 2 * 32 * rb + (size_t) kChunk * nblk * kKaBlock + 16 + 127) & ~(size_t) 127;
+    const size_t smem = kGuStages * stage + kChunk * 64 * 4 + (type == kIQ2_S ? 8192 : 0) + kGuStages * 8;
+    const int ppl = (nblk + 31) / 32;
+    const int max_items = max_work_entries(w) * (n_ff / 32);
+    dim3 grid;
+    cudaError_t err;
+#define SMOE_LGU(T_, D_, P_)                                                                                    \
+    do {                                                                                                        \
+        err = launch_persistent(layer_gate_up_kernel<T_, D_, P_>, kGuThreads, smem, max_items, &grid);         \
+        if (err != cudaSuccess) return err;                                                                     \
+        layer_gate_up_kernel<T_, D_, P_><<<grid, kGuThreads, smem, s>>>(gate, up, sgate, sup, w, xa, ha, n_embd,\
+                                                                        n_ff);                                  \
+    } while (0)
+#define SMOE_LGU_P(T_, D_)                                                                                      \
+    do {                                                                                                        \
+        if (ppl == 1) SMOE_LGU(T_, D_, 1);                                                                      \
+        else if (ppl == 2) SMOE_LGU(T_, D_, 2);                                                                 \
+        else if (ppl == 3) SMOE_LGU(T_, D_, 3);                                                                 \
+        else SMOE_LGU(T_, D_, 4);                                                                               \
+    } while (0)
+    if (type == kQ2_0) {
+        if (down_q2) SMOE_LGU_P(kQ2_0, 1);
+        else SMOE_LGU_P(kQ2_0, 0);
+    } else {
+        if (down_q2) SMOE_LGU_P(kIQ2_S, 1);
+        else SMOE_LGU_P(kIQ2_S, 0);
+    }
+#undef SMOE_LGU_P
+#undef SMOE_LGU
+    return cudaGetLastError();
+}
+
+cudaError_t launch_layer_down(Matrix down, Matrix sdown, Work w, KAct ha, float* y, int n_ff, int n_embd,
+                              cudaStream_t s) {
+    const int type = down.type;
+    const int n_in = n_ff, n_out = n_embd;
+    const int rb = type == kQ2_0 ? (n_in / 64) * 18 : (n_in / 256) * 82;
+    const int nblk = n_in / 32;
+    const int lpr = nblk <= 16 ? 16 : 32;
+    const int ppl = (nblk + lpr - 1) / lpr;
+    const int rows = (kRowThreads / 32) * (32 / lpr) * 4;
+    const size_t stage = ((size_t) rows * rb + (size_t) kChunk * nblk * kKaBlock + 16 + 127) & ~(size_t) 127;
+    const size_t smem = kDownStages * stage + (type == kIQ2_S ? 8192 : 0) + kDownStages * 8;
+    const int max_items = max_work_entries(w) * (n_out / rows);
+    dim3 grid;
+    cudaError_t err;
+#define SMOE_LD(T_, L_, P_)                                                                                     \
+    do {                                                                                                        \
+        err = launch_persistent(layer_down_kernel<T_, L_, P_>, kRowThreads, smem, max_items, &grid);           \
+        if (err != cudaSuccess) return err;                                                                     \
+        layer_down_kernel<T_, L_, P_><<<grid, kRowThreads, smem, s>>>(down, sdown, w, ha, y, n_in, n_out);      \
+    } while (0)
+    if (type == kQ2_0) {
+        if (lpr == 16) SMOE_LD(kQ2_0, 16, 1);
+        else if (ppl == 1) SMOE_LD(kQ2_0, 32, 1);
+        else if (ppl == 2) SMOE_LD(kQ2_0, 32, 2);
+        else if (ppl == 3) SMOE_LD(kQ2_0, 32, 3);
+        else SMOE_LD(kQ2_0, 32, 4);
+    } else {
+        if (lpr == 16) SMOE_LD(kIQ2_S, 16, 1);
+        else if (ppl == 1) SMOE_LD(kIQ2_S, 32, 1);
+        else if (ppl == 2) SMOE_LD(kIQ2_S, 32, 2);
+        else if (ppl == 3) SMOE_LD(kIQ2_S, 32, 3);
+        else SMOE_LD(kIQ2_S, 32, 4);
+    }
+#undef SMOE_LD
     return cudaGetLastError();
 }
 

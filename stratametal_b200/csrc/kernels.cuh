@@ -10,14 +10,31 @@ constexpr int kRouterTokTile = 16;  // tokens per CTA in the router GEMV (x stag
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxK = 64;
 
+// Activations in the expert kernels' layout ("ka"): per 32-value block 48 bytes = 8 words (Q2_0 weights:
+// byte b of word j of each half = value 4b + j of that 16-value half; IQ2_S weights: natural order), the q8_1
+// scale as f32 (the fp16 d read back), the sum of the 32 q, and 8 bytes of padding so every block is 16-byte
+// aligned and a row of blocks is one bulk copy.
+constexpr int kKaBlock = 48;
+struct KAct {
+    uint8_t* base;  // [rows][nblk][48]
+};
+inline size_t ka_bytes(int64_t rows, int nblk) { return (size_t) rows * nblk * kKaBlock; }
+inline KAct ka_at(void* base, int64_t rows, int nblk) {
+    (void) rows;
+    (void) nblk;
+    return KAct{static_cast<uint8_t*>(base)};
+}
+
 // ---- router.cu ----
 cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, const uint16_t* extra, float* y,
                              float* y_extra, int T, int H, int n_out, cudaStream_t s);
+// xa (optional): the activation in the expert kernels' layout, permuted for Q2_0 gate/up when xa_q2 != 0.
 cudaError_t launch_router_topk(const float* logits, int T, int E, int k, int32_t* ids, float* w, const float* x,
-                               uint8_t* xq, int H, cudaStream_t s);
+                               uint8_t* xq, int H, cudaStream_t s, const KAct* xa = nullptr, int xa_q2 = 1);
 cudaError_t launch_quant_q8_1(const float* x, int64_t n, uint8_t* y, cudaStream_t s);
 cudaError_t launch_swiglu_q8(const float* g, const float* u, int64_t n, uint8_t* y, cudaStream_t s);
 cudaError_t launch_f32_to_bf16(const float* x, uint16_t* y, int64_t n, cudaStream_t s);
+cudaError_t launch_quant_ka(const float* x, int64_t rows, int H, const KAct& xa, int q2, cudaStream_t s);
 
 // ---- dispatch.cu ----
 // Grouping tables inside the caller's scratch: counts[E], offsets[E + 1], active[E], n_active[1],
@@ -31,8 +48,25 @@ struct GroupTables {
 };
 size_t group_tables_bytes(int n_expert);
 GroupTables group_tables_at(void* base, int n_expert);
+
+// Work list of the layer path: the active experts ordered heaviest first (token count descending, expert id
+// ascending), each split into chunks of at most kChunk slots.  Entry c covers slots [beg[c], beg[c] + n[c])
+// of expert e[c].
+constexpr int kChunk = 8;
+struct Sched {
+    int32_t* e;
+    int32_t* beg;
+    int32_t* n;
+    int32_t* count;  // [1] entries
+};
+inline int sched_capacity(int E, int T, int k) { return E + (T * k + kChunk - 1) / kChunk + 1; }
+size_t sched_bytes(int E, int T, int k);
+Sched sched_at(void* base, int E, int T, int k);
+
+// `sched` may be null (the stage entry points): then only the grouping tables are written.
 cudaError_t launch_group(const int32_t* ids, int T, int k, int E, GroupTables g, int32_t* slot, int32_t* src,
-                         cudaStream_t s);
+                         cudaStream_t s, const Sched* sched = nullptr);
+
 
 // ---- expert.cu ----
 // Which rows of which expert a grouped launch covers.  Routed experts are the n_active entries of `active`
@@ -58,13 +92,25 @@ struct Matrix {
     int type;              // ggml type
 };
 
-// gate/up + SwiGLU + q8_1 of h for every slot of every expert in `g`:
-// hq[slot][n_ff / 32 q8_1 blocks] from xq[token][n_embd / 32 blocks].
-cudaError_t launch_expert_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, GroupView g, const uint8_t* xq,
-                                  uint8_t* hq, int n_embd, int n_ff, cudaStream_t s);
 // y[slot][r] = down_e[r] . act[slot] for every slot, y row stride y_stride floats; act rows n_in / 32 blocks.
 cudaError_t launch_expert_down(Matrix down, Matrix sdown, GroupView g, const uint8_t* act, int act_by_token,
                                float* y, int64_t y_stride, int n_in, int n_out, cudaStream_t s);
+
+// The layer path (v3): work items are (work-list entry, row tile), claimed dynamically from `counter`
+// (zeroed by the dispatch) heaviest first; the shared expert's chunks come first when shared_slots > 0.
+struct Work {
+    Sched sched;
+    const int32_t* slot_token;
+    int max_entries;   // capacity of the routed work list (bounds the grid)
+    int shared_base;   // first shared slot (T * k)
+    int shared_slots;  // T, or 0 when the shared expert is not in this launch
+    int no_routed;     // 1: the shared expert only
+    int32_t* counter;
+};
+cudaError_t launch_layer_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, Work w, KAct xa, KAct ha,
+                                 int down_q2, int n_embd, int n_ff, cudaStream_t s);
+cudaError_t launch_layer_down(Matrix down, Matrix sdown, Work w, KAct ha, float* y, int n_ff, int n_embd,
+                              cudaStream_t s);
 
 // ---- combine.cu ----
 // out[t][j] = sum_i w[t][i] * parts[slot(t, i)][j] (+ shared[t][j] * sigmoid(gate_logit[t]) when shared)

@@ -35,6 +35,38 @@ __device__ __forceinline__ void quant_q8_1_warp(float xi, uint8_t* __restrict__ 
     }
 }
 
+// The same q8_1 rule, written in the expert kernels' layout (KAct): 8 words (permuted for Q2_0 weights:
+// byte b of word j of half h = value 16h + 4b + j; natural order otherwise), the stored scale read back as the
+// dot reads it (f32 of the fp16 d) and the sum of the 32 q.
+__device__ __forceinline__ void quant_ka_warp(float xi, uint8_t* __restrict__ blk48, int lane, bool q2_layout) {
+    float amax = fabsf(xi);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float d = __fdiv_rn(amax, 127.f);
+    if (fabsf(d) > 65504.f) d = copysignf(65504.f, d);
+    int q = 0;
+    if (amax != 0.f) {
+        float r = roundf(__fdiv_rn(xi, d));
+        r = fminf(fmaxf(r, -127.f), 127.f);
+        q = (int) r;
+    }
+    int qs = q;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+    const int L = lane & 7;
+    const int src0 = q2_layout ? 16 * (L >> 2) + (L & 3) : 4 * L;
+    const int stride = q2_layout ? 4 : 1;
+    uint32_t word = 0;
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+        const int qb = __shfl_sync(0xffffffffu, q, src0 + b * stride);
+        word |= ((uint32_t) qb & 0xFFu) << (8 * b);
+    }
+    if (lane < 8) reinterpret_cast<uint32_t*>(blk48)[lane] = word;
+    if (lane == 8) reinterpret_cast<float*>(blk48)[8] = f16_to_f32(f16_bits(d));
+    if (lane == 9) reinterpret_cast<int*>(blk48)[9] = qs;
+}
+
 // silu(g) * u (iq.metal:630-663).  exp is taken in fp64 and rounded to f32: that is the correctly rounded
 // expf, which the host reference's libm expf returns on all but a vanishing fraction of inputs.
 __device__ __forceinline__ float silu_mul(float g, float u) {

@@ -18,20 +18,20 @@
 namespace smoe {
 
 // ------------------------------------------------------------------------------------------------
-// a1 + a2: logits.  A CTA owns RPW rows per warp (4 warps) and TT tokens staged in shared memory as bf16
+// a1 + a2: logits.  A CTA owns RPW rows per warp (8 warps) and TT tokens staged in shared memory as bf16
 // bits.  Per 256-value chunk a lane converts its 8 weights of each row to fp64 once and applies them to every
 // staged token, so each DFMA needs one converted activation and the weight stream is read once per CTA.
 // Rows [0, n_out) come from `w`; when `extra` is set, row n_out is that vector (the shared-expert gate
 // ffn_gate_inp_shexp) and its result goes to y_extra[t].
 // ------------------------------------------------------------------------------------------------
 template <bool kF32In, int RPW>
-__global__ void __launch_bounds__(128) bf16_gemv_kernel(const void* __restrict__ xin, const uint16_t* __restrict__ w,
+__global__ void __launch_bounds__(256) bf16_gemv_kernel(const void* __restrict__ xin, const uint16_t* __restrict__ w,
                                                         const uint16_t* __restrict__ extra, float* __restrict__ y,
                                                         float* __restrict__ y_extra, int T, int H, int n_out) {
     constexpr int TT = kRouterTokTile;
     extern __shared__ __align__(16) uint16_t xs[];  // [TT][H]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int o0 = (blockIdx.x * 4 + warp) * RPW;
+    const int o0 = (blockIdx.x * 8 + warp) * RPW;
     const int t0 = blockIdx.y * TT;
     const int nt = min(TT, T - t0);
     // stage: 4 floats (or 8 bf16) per load, several loads in flight per thread
@@ -149,7 +149,7 @@ __device__ __forceinline__ bool better(double v, int i, double bv, int bi) { ret
 __global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restrict__ logits, int E, int k,
                                                            int32_t* __restrict__ ids, float* __restrict__ wout,
                                                            const float* __restrict__ x, uint8_t* __restrict__ xq,
-                                                           int H) {
+                                                           int H, KAct xa, int xa_q2) {
     extern __shared__ double sp[];  // [E] probabilities
     __shared__ double red[32];
     __shared__ double sbv[64];
@@ -225,7 +225,12 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restri
     if (xq) {
         const float* xt = x + (size_t) t * H;
         uint8_t* yt = xq + (size_t) t * (H / 32) * kQ8Block;
-        for (int b = warp; b < H / 32; b += nw) quant_q8_1_warp(xt[b * 32 + lane], yt + b * kQ8Block, lane);
+        const int nb = H / 32;
+        for (int b = warp; b < nb; b += nw) {
+            const float xi = xt[b * 32 + lane];
+            quant_q8_1_warp(xi, yt + b * kQ8Block, lane);
+            if (xa.base) quant_ka_warp(xi, xa.base + ((size_t) t * nb + b) * kKaBlock, lane, xa_q2 != 0);
+        }
     }
 }
 
@@ -237,35 +242,36 @@ cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, cons
                              float* y_extra, int T, int H, int n_out, cudaStream_t s) {
     const int n_rows = n_out + (extra ? 1 : 0);
     const size_t smem = (size_t) kRouterTokTile * H * 2;
-    // few tokens: one row per warp spreads the weight stream over more SMs; many tokens: four rows per warp
-    // reuse each staged token four times
-    const int rpw = T <= 4 ? 1 : 4;
-    const dim3 grid((n_rows + 4 * rpw - 1) / (4 * rpw), (T + kRouterTokTile - 1) / kRouterTokTile);
+    // few tokens: one row per warp spreads the weight stream over more SMs; many tokens: two rows per warp
+    // reuse each staged token twice while 8 warps per CTA keep the fp64 pipe fed
+    const int rpw = T <= 4 ? 1 : 2;
+    const dim3 grid((n_rows + 8 * rpw - 1) / (8 * rpw), (T + kRouterTokTile - 1) / kRouterTokTile);
     cudaError_t err = cudaSuccess;
 #define SMOE_GEMV(F_, R_)                                                                                     \
     do {                                                                                                      \
         err = cudaFuncSetAttribute(bf16_gemv_kernel<F_, R_>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
                                    (int) smem);                                                               \
         if (err != cudaSuccess) return err;                                                                   \
-        bf16_gemv_kernel<F_, R_><<<grid, 128, smem, s>>>(x, w, extra, y, y_extra, T, H, n_out);              \
+        bf16_gemv_kernel<F_, R_><<<grid, 256, smem, s>>>(x, w, extra, y, y_extra, T, H, n_out);              \
     } while (0)
     if (f32_in) {
         if (rpw == 1) SMOE_GEMV(true, 1);
-        else SMOE_GEMV(true, 4);
+        else SMOE_GEMV(true, 2);
     } else {
         if (rpw == 1) SMOE_GEMV(false, 1);
-        else SMOE_GEMV(false, 4);
+        else SMOE_GEMV(false, 2);
     }
 #undef SMOE_GEMV
     return cudaGetLastError();
 }
 
 cudaError_t launch_router_topk(const float* logits, int T, int E, int k, int32_t* ids, float* w, const float* x,
-                               uint8_t* xq, int H, cudaStream_t s) {
+                               uint8_t* xq, int H, cudaStream_t s, const KAct* xa, int xa_q2) {
     int threads = ((E + 31) / 32) * 32;
     if (threads < 64) threads = 64;
     if (threads > 1024) threads = 1024;
-    router_topk_kernel<<<T, threads, (size_t) E * sizeof(double), s>>>(logits, E, k, ids, w, x, xq, H);
+    router_topk_kernel<<<T, threads, (size_t) E * sizeof(double), s>>>(logits, E, k, ids, w, x, xq, H,
+                                                                       xa ? *xa : KAct{}, xa_q2);
     return cudaGetLastError();
 }
 
@@ -281,6 +287,19 @@ cudaError_t launch_quant_q8_1(const float* x, int64_t n, uint8_t* y, cudaStream_
 
 cudaError_t launch_swiglu_q8(const float* g, const float* u, int64_t n, uint8_t* y, cudaStream_t s) {
     swiglu_q8_kernel<<<grid_for(n / 32), 256, 0, s>>>(g, u, y, n / 32);
+    return cudaGetLastError();
+}
+
+__global__ void quant_ka_kernel(const float* __restrict__ x, int64_t n_blocks, KAct xa, int q2) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t b = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks; b += warps)
+        quant_ka_warp(x[b * 32 + lane], xa.base + b * kKaBlock, lane, q2 != 0);
+}
+
+cudaError_t launch_quant_ka(const float* x, int64_t rows, int H, const KAct& xa, int q2, cudaStream_t s) {
+    const int64_t nb = rows * (H / 32);
+    quant_ka_kernel<<<grid_for(nb), 256, 0, s>>>(x, nb, xa, q2);
     return cudaGetLastError();
 }
 
