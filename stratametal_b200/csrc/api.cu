@@ -43,7 +43,7 @@ size_t up256(size_t n) { return (n + 255) & ~(size_t) 255; }
 
 // Scratch regions of the block for T tokens.
 struct Layout {
-    size_t xq, xa, xa2, logits, sh_logit, ids, w, slot, slot_token, tables, sched, ha, parts, total;
+    size_t xq, xa, xa2, logits, sh_logit, ids, w, slot, slot_token, tables, sched, gu, ha, parts, total;
 };
 
 Layout layout_of(const smoe_layer* L, int T) {
@@ -62,6 +62,7 @@ Layout layout_of(const smoe_layer* L, int T) {
     o.slot_token = at; at += up256((size_t) T * K * 4);
     o.tables = at; at += group_tables_bytes((int) E);
     o.sched = at; at += sched_bytes((int) E, T, (int) K);
+    o.gu = at; at += up256(rows * 2 * F * 4);
     o.ha = at; at += up256(ka_bytes((int64_t) rows, (int) (F / 32)));
     o.parts = at; at += up256(rows * H * 4);
     o.total = at;
@@ -299,6 +300,7 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     const KAct xa = ka_at(base + lo.xa, T, H / 32);
     const KAct xa2 = ka_at(base + lo.xa2, T, H / 32);
     const KAct ha = ka_at(base + lo.ha, rows, F / 32);
+    float* gu = reinterpret_cast<float*>(base + lo.gu);
     float* parts = reinterpret_cast<float*>(base + lo.parts);
 
     cudaError_t e = launch_bf16_gemv(x, true, L->router, sh ? L->gate_inp_shexp : nullptr, logits, sh_logit, T, H,
@@ -328,7 +330,7 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     Work w1 = wk;
     w1.shared_slots = gu_same ? T : 0;
     w1.counter = tabs.work + 0;
-    e = launch_layer_gate_up(mg, mu, sg, su, w1, xa, ha, L->d_type == kQ2_0, H, F, s);
+    e = launch_layer_gate_up(mg, mu, sg, su, w1, xa, gu, H, F, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: gate/up");
     if (sh && !gu_same) {
         const bool same_layout = (L->sg_type == kQ2_0) == (L->gu_type == kQ2_0);
@@ -340,9 +342,16 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
         w2.no_routed = 1;
         w2.shared_slots = T;
         w2.counter = tabs.work + 1;
-        e = launch_layer_gate_up(sg, su, sg, su, w2, same_layout ? xa : xa2, ha, L->sd_type == kQ2_0, H, F, s);
+        e = launch_layer_gate_up(sg, su, sg, su, w2, same_layout ? xa : xa2, gu, H, F, s);
         if (e != cudaSuccess) return cuda_fail(e, "moe_forward: shared gate/up");
     }
+    // SwiGLU + q8_1 of h, each slot in its down matrix's activation layout
+    const int routed_rows = T * K;
+    e = launch_swiglu_ka(gu, ha, sh && L->sd_type == L->d_type ? rows : routed_rows, F, L->d_type == kQ2_0, s);
+    if (e == cudaSuccess && sh && L->sd_type != L->d_type)
+        e = launch_swiglu_ka(gu + (int64_t) routed_rows * 2 * F, KAct{ha.base + ka_bytes(routed_rows, F / 32)}, T, F,
+                             L->sd_type == kQ2_0, s);
+    if (e != cudaSuccess) return cuda_fail(e, "moe_forward: swiglu");
     e = mark(3, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: stage event");
     Work w3 = wk;

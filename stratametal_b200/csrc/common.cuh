@@ -158,6 +158,21 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return true;
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Named barrier over `n` threads that also ANDs a predicate across them (every thread gets the result).
+__device__ __forceinline__ bool bar_and(int id, int n, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{ .reg .pred p, q; setp.ne.u32 p, %1, 0; bar.red.and.pred q, %2, %3, p; selp.u32 %0, 1, 0, q; }"
+        : "=r"(r)
+        : "r"((uint32_t) pred), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
+}
+
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legal copy, far below a hang
 
 }  // namespace smoe

@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__
     __shared__ int whist[32][64];
     __shared__ int bucket_off[64];
     __shared__ int sorted[kMaxExperts];
-    const int lane = tid & 31, warp = tid >> 5;
+    const int warp = tid >> 5;
     for (int i = tid; i < 32 * 64; i += blockDim.x) whist[i / 64][i % 64] = 0;
     __syncthreads();
     const int e = tid;

@@ -440,7 +440,25 @@ __device__ __forceinline__ int entry_token(const Work& w, const Entry& en, int s
     return en.shared ? slot - w.shared_base : w.slot_token[slot];
 }
 
-__device__ __forceinline__ int claim(int32_t* counter) { return atomicAdd(counter, 1); }
+// Copy the work list and the slot -> token map into shared memory (tab: 3 * cap + n_slot ints) and point the
+// Work at the copies, so the producer's per-item table reads are shared-memory reads.
+__device__ __forceinline__ void tables_to_smem(Work& w, int32_t* tab, int cap, int n_slot, int nthreads) {
+    const int n_ent = *w.sched.count;
+    for (int i = threadIdx.x; i < n_ent; i += nthreads) {
+        tab[i] = w.sched.e[i];
+        tab[cap + i] = w.sched.beg[i];
+        tab[2 * cap + i] = w.sched.n[i];
+    }
+    for (int i = threadIdx.x; i < n_slot; i += nthreads) tab[3 * cap + i] = w.slot_token[i];
+    __syncthreads();
+    if (threadIdx.x == 0) tab[3 * cap + n_slot] = n_ent;
+    __syncthreads();
+    w.sched.e = tab;
+    w.sched.beg = tab + cap;
+    w.sched.n = tab + 2 * cap;
+    w.sched.count = tab + 3 * cap + n_slot;
+    w.slot_token = tab + 3 * cap;
+}
 
 // Thread 0 waits for item i's stage (bounded); on a timeout it also waits, bounded, for every copy it still
 // has in flight.  Every thread then acquires the stage, or every thread returns false.
@@ -473,113 +491,209 @@ __device__ __forceinline__ float partial_ka(const Dec& w, const uint8_t* blk) {
     return partial<TYPE>(w, a0, a1, ds.x, __float_as_int(ds.y));
 }
 
-constexpr int kGuStages = 3;
+// Layer-path dot: the dp4a chain starts from the bits of 1.5 * 2^23 minus the block's sum of q, so after the
+// eight unsigned-code dp4a it holds the float 1.5 * 2^23 + sum (code - 1) q exactly (|sum| < 2^22), and one
+// subtraction gives (float) sumi.  The seed is per (token, block) and shared by every row.
+template <int TYPE>
+__device__ __forceinline__ void decode_layer(const uint8_t* row, int k, const uint64_t* grid, Dec& w) {
+    decode<TYPE>(row, k, grid, w);
+}
 
-// gate/up + SwiGLU + q8_1 of h.  Item = (work entry, 32-row tile of n_ff).  A ring stage holds the gate tile,
-// the up tile and the entry's token activations (one bulk copy each).  16 warps; warp w owns tile rows w and
-// w + 16 of both gate and up; lane L owns partials L, L + 32, ... (PPL of them).
-template <int TYPE, int DQ2, int PPL>
-__global__ void __launch_bounds__(kGuThreads, 1) layer_gate_up_kernel(Matrix gate, Matrix up, Matrix sgate,
-                                                                      Matrix sup, Work w, KAct xa, KAct ha, int H,
-                                                                      int F) {
+struct ActRegs {
+    uint4 a0, a1;
+    float dx;
+    int seed;  // Q2_0: 0x4B400000 - sum q
+};
+
+__device__ __forceinline__ ActRegs load_act(const uint8_t* blk) {
+    ActRegs r;
+    r.a0 = reinterpret_cast<const uint4*>(blk)[0];
+    r.a1 = reinterpret_cast<const uint4*>(blk)[1];
+    const float2 ds = reinterpret_cast<const float2*>(blk)[4];
+    r.dx = ds.x;
+    r.seed = 0x4B400000 - __float_as_int(ds.y);
+    return r;
+}
+
+template <int TYPE>
+__device__ __forceinline__ float partial_layer(const Dec& w, const ActRegs& a) {
+    float f;
+    if constexpr (TYPE == kQ2_0) {
+        int s = dp4a_us(w.c[0], (int) a.a0.x, a.seed);
+        s = dp4a_us(w.c[1], (int) a.a0.y, s);
+        s = dp4a_us(w.c[2], (int) a.a0.z, s);
+        s = dp4a_us(w.c[3], (int) a.a0.w, s);
+        s = dp4a_us(w.c[4], (int) a.a1.x, s);
+        s = dp4a_us(w.c[5], (int) a.a1.y, s);
+        s = dp4a_us(w.c[6], (int) a.a1.z, s);
+        s = dp4a_us(w.c[7], (int) a.a1.w, s);
+        f = __fsub_rn(__int_as_float(s), 12582912.0f);
+    } else {
+        int s0 = dp4a_ss((int) w.c[0], (int) a.a0.x, 0);
+        s0 = dp4a_ss((int) w.c[1], (int) a.a0.y, s0);
+        s0 = dp4a_ss((int) w.c[2], (int) a.a0.z, s0);
+        s0 = dp4a_ss((int) w.c[3], (int) a.a0.w, s0);
+        int s1 = dp4a_ss((int) w.c[4], (int) a.a1.x, 0);
+        s1 = dp4a_ss((int) w.c[5], (int) a.a1.y, s1);
+        s1 = dp4a_ss((int) w.c[6], (int) a.a1.z, s1);
+        s1 = dp4a_ss((int) w.c[7], (int) a.a1.w, s1);
+        const int ls0 = (int) (w.ls & 0xFFu), ls1 = (int) (w.ls >> 8);
+        f = int_to_float_exact((s0 * ls0 + s1 * ls1 + (s0 + s1) / 2) / 4);
+    }
+    return __fmul_rn(__fmul_rn(w.d, a.dx), f);
+}
+
+constexpr int kGuStages = 4;
+constexpr int kGuConsumers = kGuThreads / 32;   // 16 consumer warps
+constexpr int kGuBlock = kGuThreads + 32;       // + 1 producer warp
+
+// gate and up.  Item = (work entry, 32-row tile of gate or of up).  Warp-specialised: one producer warp claims
+// items and bulk-copies, per ring stage, the tile and the entry's token activations; 16 consumer warps compute,
+// warp w owning tile rows w and w + 16, lane L partials L, L + 32, ... (PPL of them).  Stages are handed back
+// through `empty` barriers, so the producer runs ahead and its claim / table reads stay off the consumers'
+// path.  Results go to gu[slot][gate n_ff | up n_ff] as f32; consumer warps never wait for each other.
+template <int TYPE, int PPL>
+__global__ void __launch_bounds__(kGuBlock, 1) layer_gate_up_kernel(Matrix gate, Matrix up, Matrix sgate,
+                                                                    Matrix sup, Work w, KAct xa,
+                                                                    float* __restrict__ gu, int H, int F,
+                                                                    int tab_in_smem) {
     constexpr int NST = kGuStages;
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int rb = (TYPE == kQ2_0) ? (H / 64) * 18 : (H / 256) * 82;
-    const int nblk = H / 32, nblk_h = F / 32;
+    const int nblk = H / 32;
     const uint32_t tile_bytes = 32u * (uint32_t) rb;
     const uint32_t act_row = (uint32_t) nblk * kKaBlock;
-    const uint32_t stage_bytes = (2u * tile_bytes + kChunk * act_row + 16u + 127u) & ~127u;
-    float* htile = reinterpret_cast<float*>(smem + (size_t) NST * stage_bytes);  // [kChunk][gate 32 | up 32]
-    uint64_t* grid_s = reinterpret_cast<uint64_t*>(htile + kChunk * 64);        // [1024] (IQ2_S)
-    uint64_t* bars = grid_s + (TYPE == kIQ2_S ? 1024 : 0);
+    const uint32_t stage_bytes = (tile_bytes + kChunk * act_row + 16u + 127u) & ~127u;
+    uint64_t* grid_s = reinterpret_cast<uint64_t*>(smem + (size_t) NST * stage_bytes);  // [1024] (IQ2_S)
+    uint64_t* full = grid_s + (TYPE == kIQ2_S ? 1024 : 0);
+    uint64_t* empty = full + NST;
+    int32_t* tab = reinterpret_cast<int32_t*>(empty + NST);  // work list + slot -> token map
     __shared__ int s_item[NST];
-    __shared__ int s_ok;
 
     if (TYPE == kIQ2_S)
-        for (int i = tid; i < 1024; i += kGuThreads) grid_s[i] = k_iq2s_grid_dev[i];
-    const int n_tiles = F / 32;
-    const int n_items = work_entries(w) * n_tiles;
-    auto issue = [&](int st) {
-        const int id = claim(w.counter);
-        s_item[st] = id;
-        if (id >= n_items) return;
-        const Entry en = work_entry(w, id / n_tiles);
-        const int64_t off = (int64_t) (id % n_tiles) * tile_bytes;
-        const uint8_t* gs = (en.shared ? sgate.base : gate.base + (int64_t) en.e * gate.expert_stride) + off;
-        const uint8_t* us = (en.shared ? sup.base : up.base + (int64_t) en.e * up.expert_stride) + off;
-        uint8_t* dst = smem + (size_t) st * stage_bytes;
-        fence_proxy_async();
-        mbar_expect_tx(&bars[st], 2u * tile_bytes + (uint32_t) en.n * act_row);
-        bulk_g2s(dst, gs, tile_bytes, &bars[st]);
-        bulk_g2s(dst + tile_bytes, us, tile_bytes, &bars[st]);
-        for (int s = 0; s < en.n; s++) {
-            const int tok = entry_token(w, en, en.beg + s);
-            bulk_g2s(dst + 2 * tile_bytes + s * act_row, xa.base + (size_t) tok * act_row, act_row, &bars[st]);
-        }
-    };
+        for (int i = tid; i < 1024; i += kGuBlock) grid_s[i] = k_iq2s_grid_dev[i];
+    if (tab_in_smem) tables_to_smem(w, tab, w.max_entries, w.shared_base, kGuBlock);
     if (tid == 0) {
-        for (int i = 0; i < NST; i++) mbar_init(&bars[i], 1);
+        for (int i = 0; i < NST; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kGuConsumers);
+        }
         fence_mbar_init();
-        for (int st = 0; st < NST - 1; st++) issue(st);
     }
     __syncthreads();
+    const int rt = F / 32;            // row tiles per matrix
+    const int n_tiles = 2 * rt;       // gate tiles then up tiles
+    const int n_items = work_entries(w) * n_tiles;
+
+    if (warp == kGuConsumers) {  // producer
+        if (lane != 0) return;
+        for (int j = 0;; j++) {
+            const int st = j % NST;
+            if (j >= NST && !mbar_wait_bounded(&empty[st], (uint32_t) ((j / NST - 1) & 1), kWaitLimitNs)) {
+                atomicOr(&g_smoe_status, kDevTimeout);
+                for (int q = j - NST + 1; q < j; q++)  // copies still in flight
+                    mbar_wait_bounded(&full[q % NST], (uint32_t) ((q / NST) & 1), kWaitLimitNs);
+                return;
+            }
+            const int id = (int) blockIdx.x + j * (int) gridDim.x;  // heaviest items first, round robin
+            s_item[st] = id;
+            if (id >= n_items) {
+                mbar_arrive(&full[st]);  // hands the consumers the end marker
+                return;
+            }
+            const Entry en = work_entry(w, id / n_tiles);
+            const int tt = id % n_tiles;
+            const Matrix m = tt < rt ? (en.shared ? sgate : gate) : (en.shared ? sup : up);
+            const uint8_t* src = (en.shared ? m.base : m.base + (int64_t) en.e * m.expert_stride) +
+                                 (int64_t) (tt % rt) * tile_bytes;
+            uint8_t* dst = smem + (size_t) st * stage_bytes;
+            fence_proxy_async();
+            mbar_expect_tx(&full[st], tile_bytes + (uint32_t) en.n * act_row);
+            bulk_g2s(dst, src, tile_bytes, &full[st]);
+            for (int s = 0; s < en.n; s++) {
+                const int tok = entry_token(w, en, en.beg + s);
+                bulk_g2s(dst + tile_bytes + s * act_row, xa.base + (size_t) tok * act_row, act_row, &full[st]);
+            }
+        }
+    }
+
     for (int i = 0;; i++) {
-        if (tid == 0 && s_item[(i + NST - 2) % NST] < n_items) issue((i + NST - 1) % NST);
-        __syncthreads();
-        const int id = s_item[i % NST];
+        const int st = i % NST;
+        const uint32_t parity = (uint32_t) ((i / NST) & 1);
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait_bounded(&full[st], parity, kWaitLimitNs);
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+            if (lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
+            return;
+        }
+        (void) mbar_try_wait(&full[st], parity);  // acquire in every lane
+        const int id = s_item[st];
         if (id >= n_items) break;
-        if (!stage_wait<NST>(bars, i, s_item, n_items, &s_ok)) return;
         const Entry en = work_entry(w, id / n_tiles);
         const int tt = id % n_tiles;
-        const uint8_t* wt = smem + (size_t) (i % NST) * stage_bytes;
-        const uint8_t* acts = wt + 2 * tile_bytes;
+        const uint8_t* wt = smem + (size_t) st * stage_bytes;
+        const uint8_t* acts = wt + tile_bytes;
 
-        Dec wd[4][PPL];  // v[0] gate row warp, v[1] gate row warp + 16, v[2] up row warp, v[3] up row warp + 16
+        Dec wd[2][PPL];  // tile rows warp, warp + 16
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const uint8_t* rp = wt + (q >> 1) * tile_bytes + (warp + 16 * (q & 1)) * rb;
+        for (int q = 0; q < 2; q++) {
+            const uint8_t* rp = wt + (warp + 16 * q) * rb;
 #pragma unroll
             for (int p = 0; p < PPL; p++) {
                 const int k = lane + 32 * p;
-                if (k < nblk) decode<TYPE>(rp, k, grid_s, wd[q][p]);
+                if (k < nblk) decode_layer<TYPE>(rp, k, grid_s, wd[q][p]);
             }
         }
+        float* out = gu + (tt < rt ? 0 : F) + (tt % rt) * 32 + warp;
         for (int s = 0; s < en.n; s++) {
-            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            float v[2] = {0.f, 0.f};
 #pragma unroll
             for (int p = 0; p < PPL; p++) {
                 const int k = lane + 32 * p;
                 if (k < nblk) {
-                    const uint8_t* ab = acts + s * act_row + k * kKaBlock;
+                    const ActRegs a = load_act(acts + s * act_row + k * kKaBlock);
 #pragma unroll
-                    for (int q = 0; q < 4; q++) v[q] = __fadd_rn(v[q], partial_ka<TYPE>(wd[q][p], ab));
+                    for (int q = 0; q < 2; q++) v[q] = __fadd_rn(v[q], partial_layer<TYPE>(wd[q][p], a));
                 }
             }
-            tbfly<4, 16>(v, lane);
-            // lane holds output 2*b4 + b3: b4 = 0 gate, 1 up; tile row = warp + 16 * b3
-            if ((lane & 7) == 0) htile[s * 64 + 32 * ((lane >> 4) & 1) + warp + 16 * ((lane >> 3) & 1)] = v[0];
+            tbfly<2, 16>(v, lane);  // lane holds tile row warp + 16 * b4
+            if ((lane & 15) == 0) out[(int64_t) (en.beg + s) * 2 * F + 16 * (lane >> 4)] = v[0];
         }
-        __syncthreads();
-        // SwiGLU then q8_1 of h: one warp per token, one row per lane
-        for (int s = warp; s < en.n; s += kGuThreads / 32)
-            quant_ka_warp(silu_mul(htile[s * 64 + lane], htile[s * 64 + 32 + lane]),
-                          ha.base + ((size_t) (en.beg + s) * nblk_h + tt) * kKaBlock, lane, DQ2 != 0);
-        __syncthreads();  // the stage and htile are free
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+    }
+}
+
+// SwiGLU then q8_1 of h, in the down kernel's layout: one warp per (slot, 32-value block).
+template <int DQ2>
+__global__ void swiglu_ka_kernel(const float* __restrict__ gu, KAct ha, int64_t rows, int F) {
+    const int lane = threadIdx.x & 31;
+    const int nb = F / 32;
+    const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
+    for (int64_t q = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); q < rows * nb; q += warps) {
+        const int64_t r = q / nb;
+        const int b = (int) (q % nb);
+        const float* g = gu + r * 2 * F + b * 32;
+        quant_ka_warp(silu_mul(g[lane], g[F + lane]), ha.base + q * kKaBlock, lane, DQ2 != 0);
     }
 }
 
 constexpr int kDownStages = 4;
+constexpr int kDownConsumers = kRowThreads / 32;  // 8 consumer warps
+constexpr int kDownBlock = kRowThreads + 32;      // + 1 producer warp
 
-// down.  Item = (work entry, ROWS-row tile of n_embd).  A stage holds the tile and the entry's h rows (its
-// slots are contiguous, so one bulk copy).
+// down.  Item = (work entry, ROWS-row tile of n_embd).  A stage holds the tile and the entry's h rows (its slots
+// are contiguous: one bulk copy).  Same producer / consumer split as the gate/up kernel; consumer warps never
+// synchronise with each other.
 template <int TYPE, int LPR, int PPL>
-__global__ void __launch_bounds__(kRowThreads) layer_down_kernel(Matrix wm, Matrix swm, Work w, KAct ha,
-                                                                 float* __restrict__ y, int n_in, int n_out) {
+__global__ void __launch_bounds__(kDownBlock) layer_down_kernel(Matrix wm, Matrix swm, Work w, KAct ha,
+                                                                float* __restrict__ y, int n_in, int n_out,
+                                                                int tab_in_smem) {
     constexpr int NST = kDownStages;
     constexpr int RPG = 4;
     constexpr int GROUPS = 32 / LPR;
-    constexpr int ROWS = (kRowThreads / 32) * GROUPS * RPG;
+    constexpr int ROWS = kDownConsumers * GROUPS * RPG;
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int grp = lane / LPR, gl = lane % LPR;
@@ -589,42 +703,68 @@ __global__ void __launch_bounds__(kRowThreads) layer_down_kernel(Matrix wm, Matr
     const uint32_t act_row = (uint32_t) nblk * kKaBlock;
     const uint32_t stage_bytes = (tile_bytes + kChunk * act_row + 16u + 127u) & ~127u;
     uint64_t* grid_s = reinterpret_cast<uint64_t*>(smem + (size_t) NST * stage_bytes);
-    uint64_t* bars = grid_s + (TYPE == kIQ2_S ? 1024 : 0);
+    uint64_t* full = grid_s + (TYPE == kIQ2_S ? 1024 : 0);
+    uint64_t* empty = full + NST;
+    int32_t* tab = reinterpret_cast<int32_t*>(empty + NST);
     __shared__ int s_item[NST];
-    __shared__ int s_ok;
 
     if (TYPE == kIQ2_S)
-        for (int i = tid; i < 1024; i += kRowThreads) grid_s[i] = k_iq2s_grid_dev[i];
-    const int n_tiles = n_out / ROWS;  // the layer check guarantees whole tiles
-    const int n_items = work_entries(w) * n_tiles;
-    auto issue = [&](int st) {
-        const int id = claim(w.counter);
-        s_item[st] = id;
-        if (id >= n_items) return;
-        const Entry en = work_entry(w, id / n_tiles);
-        const int r0 = (id % n_tiles) * ROWS;
-        const uint8_t* src = (en.shared ? swm.base : wm.base + (int64_t) en.e * wm.expert_stride) + (int64_t) r0 * rb;
-        uint8_t* dst = smem + (size_t) st * stage_bytes;
-        fence_proxy_async();
-        mbar_expect_tx(&bars[st], tile_bytes + (uint32_t) en.n * act_row);
-        bulk_g2s(dst, src, tile_bytes, &bars[st]);
-        bulk_g2s(dst + tile_bytes, ha.base + (size_t) en.beg * act_row, (uint32_t) en.n * act_row, &bars[st]);
-    };
+        for (int i = tid; i < 1024; i += kDownBlock) grid_s[i] = k_iq2s_grid_dev[i];
+    if (tab_in_smem) tables_to_smem(w, tab, w.max_entries, 0, kDownBlock);
     if (tid == 0) {
-        for (int i = 0; i < NST; i++) mbar_init(&bars[i], 1);
+        for (int i = 0; i < NST; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kDownConsumers);
+        }
         fence_mbar_init();
-        for (int st = 0; st < NST - 1; st++) issue(st);
     }
     __syncthreads();
+    const int n_tiles = n_out / ROWS;  // the layer check guarantees whole tiles
+    const int n_items = work_entries(w) * n_tiles;
+
+    if (warp == kDownConsumers) {  // producer
+        if (lane != 0) return;
+        for (int j = 0;; j++) {
+            const int st = j % NST;
+            if (j >= NST && !mbar_wait_bounded(&empty[st], (uint32_t) ((j / NST - 1) & 1), kWaitLimitNs)) {
+                atomicOr(&g_smoe_status, kDevTimeout);
+                for (int q = j - NST + 1; q < j; q++)
+                    mbar_wait_bounded(&full[q % NST], (uint32_t) ((q / NST) & 1), kWaitLimitNs);
+                return;
+            }
+            const int id = (int) blockIdx.x + j * (int) gridDim.x;
+            s_item[st] = id;
+            if (id >= n_items) {
+                mbar_arrive(&full[st]);
+                return;
+            }
+            const Entry en = work_entry(w, id / n_tiles);
+            const int r0 = (id % n_tiles) * ROWS;
+            const uint8_t* src =
+                (en.shared ? swm.base : wm.base + (int64_t) en.e * wm.expert_stride) + (int64_t) r0 * rb;
+            uint8_t* dst = smem + (size_t) st * stage_bytes;
+            fence_proxy_async();
+            mbar_expect_tx(&full[st], tile_bytes + (uint32_t) en.n * act_row);
+            bulk_g2s(dst, src, tile_bytes, &full[st]);
+            bulk_g2s(dst + tile_bytes, ha.base + (size_t) en.beg * act_row, (uint32_t) en.n * act_row, &full[st]);
+        }
+    }
+
     for (int i = 0;; i++) {
-        if (tid == 0 && s_item[(i + NST - 2) % NST] < n_items) issue((i + NST - 1) % NST);
-        __syncthreads();
-        const int id = s_item[i % NST];
+        const int st = i % NST;
+        const uint32_t parity = (uint32_t) ((i / NST) & 1);
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait_bounded(&full[st], parity, kWaitLimitNs);
+        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+            if (lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
+            return;
+        }
+        (void) mbar_try_wait(&full[st], parity);
+        const int id = s_item[st];
         if (id >= n_items) break;
-        if (!stage_wait<NST>(bars, i, s_item, n_items, &s_ok)) return;
         const Entry en = work_entry(w, id / n_tiles);
         const int r0 = (id % n_tiles) * ROWS;
-        const uint8_t* wt = smem + (size_t) (i % NST) * stage_bytes;
+        const uint8_t* wt = smem + (size_t) st * stage_bytes;
         const uint8_t* acts = wt + tile_bytes;
 
         Dec wr[RPG][PPL];
@@ -635,7 +775,7 @@ __global__ void __launch_bounds__(kRowThreads) layer_down_kernel(Matrix wm, Matr
 #pragma unroll
             for (int p = 0; p < PPL; p++) {
                 const int k = gl + LPR * p;
-                if (k < nblk) decode<TYPE>(rp, k, grid_s, wr[q][p]);
+                if (k < nblk) decode_layer<TYPE>(rp, k, grid_s, wr[q][p]);
             }
         }
         for (int s = 0; s < en.n; s++) {
@@ -646,9 +786,9 @@ __global__ void __launch_bounds__(kRowThreads) layer_down_kernel(Matrix wm, Matr
             for (int p = 0; p < PPL; p++) {
                 const int k = gl + LPR * p;
                 if (k < nblk) {
-                    const uint8_t* ab = acts + s * act_row + k * kKaBlock;
+                    const ActRegs a = load_act(acts + s * act_row + k * kKaBlock);
 #pragma unroll
-                    for (int q = 0; q < RPG; q++) v[q] = __fadd_rn(v[q], partial_ka<TYPE>(wr[q][p], ab));
+                    for (int q = 0; q < RPG; q++) v[q] = __fadd_rn(v[q], partial_layer<TYPE>(wr[q][p], a));
                 }
             }
             tbfly<RPG, LPR / 2>(v, lane);
@@ -656,7 +796,8 @@ __global__ void __launch_bounds__(kRowThreads) layer_down_kernel(Matrix wm, Matr
             if ((gl & low_mask) == 0)
                 y[(int64_t) (en.beg + s) * n_out + r0 + row_base + ((gl / (LPR / 4)) & 3)] = v[0];
         }
-        __syncthreads();  // the stage is free
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
     }
 }
 
@@ -735,44 +876,54 @@ cudaError_t launch_expert_down(Matrix down, Matrix sdown, GroupView g, const uin
 
 namespace smoe {
 
+constexpr size_t kTableSmemMax = 24 * 1024;  // work tables larger than this are read from global memory
+
 static int max_work_entries(const Work& w) {
     return (w.no_routed ? 0 : w.max_entries) + (w.shared_slots > 0 ? (w.shared_slots + kChunk - 1) / kChunk : 0);
 }
 
-cudaError_t launch_layer_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, Work w, KAct xa, KAct ha,
-                                 int down_q2, int n_embd, int n_ff, cudaStream_t s) {
+cudaError_t launch_layer_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, Work w, KAct xa, float* gu,
+                                 int n_embd, int n_ff, cudaStream_t s) {
     const int type = gate.type;
     const int rb = type == kQ2_0 ? (n_embd / 64) * 18 : (n_embd / 256) * 82;
     const int nblk = n_embd / 32;
-    const size_t stage = ((size_t) 2 * 32 * rb + (size_t) kChunk * nblk * kKaBlock + 16 + 127) & ~(size_t) 127;
-    const size_t smem = kGuStages * stage + kChunk * 64 * 4 + (type == kIQ2_S ? 8192 : 0) + kGuStages * 8;
+    const size_t stage = ((size_t) 32 * rb + (size_t) kChunk * nblk * kKaBlock + 16 + 127) & ~(size_t) 127;
+    const size_t tab = ((size_t) 3 * w.max_entries + w.shared_base + 1) * 4;
+    const int tab_in_smem = tab <= kTableSmemMax ? 1 : 0;
+    const size_t smem = kGuStages * stage + (type == kIQ2_S ? 8192 : 0) + 2 * kGuStages * 8 + (tab_in_smem ? tab : 0);
     const int ppl = (nblk + 31) / 32;
-    const int max_items = max_work_entries(w) * (n_ff / 32);
+    const int max_items = max_work_entries(w) * 2 * (n_ff / 32);
     dim3 grid;
     cudaError_t err;
-#define SMOE_LGU(T_, D_, P_)                                                                                    \
+#define SMOE_LGU(T_, P_)                                                                                        \
     do {                                                                                                        \
-        err = launch_persistent(layer_gate_up_kernel<T_, D_, P_>, kGuThreads, smem, max_items, &grid);         \
+        err = launch_persistent(layer_gate_up_kernel<T_, P_>, kGuBlock, smem, max_items, &grid);               \
         if (err != cudaSuccess) return err;                                                                     \
-        layer_gate_up_kernel<T_, D_, P_><<<grid, kGuThreads, smem, s>>>(gate, up, sgate, sup, w, xa, ha, n_embd,\
-                                                                        n_ff);                                  \
-    } while (0)
-#define SMOE_LGU_P(T_, D_)                                                                                      \
-    do {                                                                                                        \
-        if (ppl == 1) SMOE_LGU(T_, D_, 1);                                                                      \
-        else if (ppl == 2) SMOE_LGU(T_, D_, 2);                                                                 \
-        else if (ppl == 3) SMOE_LGU(T_, D_, 3);                                                                 \
-        else SMOE_LGU(T_, D_, 4);                                                                               \
+        layer_gate_up_kernel<T_, P_><<<grid, kGuBlock, smem, s>>>(gate, up, sgate, sup, w, xa, gu, n_embd,      \
+                                                                  n_ff, tab_in_smem);                           \
     } while (0)
     if (type == kQ2_0) {
-        if (down_q2) SMOE_LGU_P(kQ2_0, 1);
-        else SMOE_LGU_P(kQ2_0, 0);
+        if (ppl == 1) SMOE_LGU(kQ2_0, 1);
+        else if (ppl == 2) SMOE_LGU(kQ2_0, 2);
+        else if (ppl == 3) SMOE_LGU(kQ2_0, 3);
+        else SMOE_LGU(kQ2_0, 4);
     } else {
-        if (down_q2) SMOE_LGU_P(kIQ2_S, 1);
-        else SMOE_LGU_P(kIQ2_S, 0);
+        if (ppl == 1) SMOE_LGU(kIQ2_S, 1);
+        else if (ppl == 2) SMOE_LGU(kIQ2_S, 2);
+        else if (ppl == 3) SMOE_LGU(kIQ2_S, 3);
+        else SMOE_LGU(kIQ2_S, 4);
     }
-#undef SMOE_LGU_P
 #undef SMOE_LGU
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_ka(const float* gu, KAct ha, int64_t rows, int n_ff, int down_q2, cudaStream_t s) {
+    const int64_t warps = rows * (n_ff / 32);
+    int64_t blocks = (warps + 7) / 8;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks < 1) blocks = 1;
+    if (down_q2) swiglu_ka_kernel<1><<<(unsigned) blocks, 256, 0, s>>>(gu, ha, rows, n_ff);
+    else swiglu_ka_kernel<0><<<(unsigned) blocks, 256, 0, s>>>(gu, ha, rows, n_ff);
     return cudaGetLastError();
 }
 
@@ -786,15 +937,18 @@ cudaError_t launch_layer_down(Matrix down, Matrix sdown, Work w, KAct ha, float*
     const int ppl = (nblk + lpr - 1) / lpr;
     const int rows = (kRowThreads / 32) * (32 / lpr) * 4;
     const size_t stage = ((size_t) rows * rb + (size_t) kChunk * nblk * kKaBlock + 16 + 127) & ~(size_t) 127;
-    const size_t smem = kDownStages * stage + (type == kIQ2_S ? 8192 : 0) + kDownStages * 8;
+    const size_t tab = ((size_t) 3 * w.max_entries + 1) * 4;
+    const int tab_in_smem = tab <= kTableSmemMax ? 1 : 0;
+    const size_t smem = kDownStages * stage + (type == kIQ2_S ? 8192 : 0) + 2 * kDownStages * 8 + (tab_in_smem ? tab : 0);
     const int max_items = max_work_entries(w) * (n_out / rows);
     dim3 grid;
     cudaError_t err;
 #define SMOE_LD(T_, L_, P_)                                                                                     \
     do {                                                                                                        \
-        err = launch_persistent(layer_down_kernel<T_, L_, P_>, kRowThreads, smem, max_items, &grid);           \
+        err = launch_persistent(layer_down_kernel<T_, L_, P_>, kDownBlock, smem, max_items, &grid);            \
         if (err != cudaSuccess) return err;                                                                     \
-        layer_down_kernel<T_, L_, P_><<<grid, kRowThreads, smem, s>>>(down, sdown, w, ha, y, n_in, n_out);      \
+        layer_down_kernel<T_, L_, P_><<<grid, kDownBlock, smem, s>>>(down, sdown, w, ha, y, n_in, n_out,        \
+                                                                     tab_in_smem);                              \
     } while (0)
     if (type == kQ2_0) {
         if (lpr == 16) SMOE_LD(kQ2_0, 16, 1);

@@ -107,8 +107,10 @@ struct Work {
     int no_routed;     // 1: the shared expert only
     int32_t* counter;
 };
-cudaError_t launch_layer_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, Work w, KAct xa, KAct ha,
-                                 int down_q2, int n_embd, int n_ff, cudaStream_t s);
+// gate and up rows into gu[slot][gate n_ff | up n_ff] (f32), then SwiGLU + q8_1 of h into ha.
+cudaError_t launch_layer_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, Work w, KAct xa, float* gu,
+                                 int n_embd, int n_ff, cudaStream_t s);
+cudaError_t launch_swiglu_ka(const float* gu, KAct ha, int64_t rows, int n_ff, int down_q2, cudaStream_t s);
 cudaError_t launch_layer_down(Matrix down, Matrix sdown, Work w, KAct ha, float* y, int n_ff, int n_embd,
                               cudaStream_t s);
 
