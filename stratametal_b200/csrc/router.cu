@@ -141,57 +141,68 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, uint16_t* __rest
 }
 
 // ------------------------------------------------------------------------------------------------
-// a3 (+ a4): one CTA per token.  Softmax in fp64, top-k by (probability desc, index asc), renormalise.
-// When xq != nullptr the CTA also writes the q8_1 image of the token's activation x.
+// a3 (+ a4): one warp per token, 8 tokens per CTA.  Lane l holds experts l, l + 32, ... (E <= 1024).
+// p_e = exp(l_e - max) in fp64; the ranking is by p_e descending with the lower index on a tie (the order of
+// the normalised probabilities: one positive divisor for all); the k chosen are then normalised exactly as
+// route_ref does: w = (float)(p / sum), chosen = sum of those quotients in rank order, clamped at 2^-14,
+// final (float)((double) w / chosen).  With xq the CTA then writes the q8_1 image of its 8 tokens.
 // ------------------------------------------------------------------------------------------------
 __device__ __forceinline__ bool better(double v, int i, double bv, int bi) { return v > bv || (v == bv && i < bi); }
 
-__global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restrict__ logits, int E, int k,
-                                                           int32_t* __restrict__ ids, float* __restrict__ wout,
-                                                           const float* __restrict__ x, uint8_t* __restrict__ xq,
-                                                           int H, KAct xa, int xa_q2) {
-    extern __shared__ double sp[];  // [E] probabilities
-    __shared__ double red[32];
-    __shared__ double sbv[64];
-    __shared__ int sbi[64];
-    const int t = blockIdx.x;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const float* l = logits + (size_t) t * E;
+constexpr int kTopkWarps = 8;
 
-    // block max of the logits
-    float mxf = -INFINITY;
-    for (int e = tid; e < E; e += blockDim.x) mxf = fmaxf(mxf, l[e]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mxf = fmaxf(mxf, __shfl_xor_sync(0xffffffffu, mxf, o));
-    if (lane == 0) red[warp] = (double) mxf;
-    __syncthreads();
-    double mx = red[0];
-    for (int i = 1; i < nw; i++) mx = fmax(mx, red[i]);
-    __syncthreads();
-
-    // p = exp(l - mx), fp64 sum
-    double part = 0;
-    for (int e = tid; e < E; e += blockDim.x) {
-        const double p = exp((double) l[e] - mx);
-        sp[e] = p;
-        part += p;
+template <int PER_LANE>
+__global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const float* __restrict__ logits, int T, int E,
+                                                                      int k, int32_t* __restrict__ ids,
+                                                                      float* __restrict__ wout,
+                                                                      const float* __restrict__ x,
+                                                                      uint8_t* __restrict__ xq, int H, KAct xa,
+                                                                      int xa_q2) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int route_blocks = (T + kTopkWarps - 1) / kTopkWarps;
+    if ((int) blockIdx.x >= route_blocks) {
+        // the remaining CTAs write the q8_1 image of x: one 32-value block per warp
+        const int nb = H / 32;
+        const int64_t q = (int64_t) (blockIdx.x - route_blocks) * kTopkWarps + warp;
+        if (q < (int64_t) T * nb) {
+            const float xi = x[q * 32 + lane];
+            quant_q8_1_warp(xi, xq + q * kQ8Block, lane);
+            if (xa.base) quant_ka_warp(xi, xa.base + q * kKaBlock, lane, xa_q2 != 0);
+        }
+        return;
     }
+    const int t = blockIdx.x * kTopkWarps + warp;
+    if (t < T) {
+        const float* l = logits + (size_t) t * E;
+        float lv[PER_LANE];
+        float mx = -INFINITY;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if (lane == 0) red[warp] = part;
-    __syncthreads();
-    double sum = 0;
-    for (int i = 0; i < nw; i++) sum += red[i];
-    for (int e = tid; e < E; e += blockDim.x) sp[e] = sp[e] / sum;
-    __syncthreads();
-
-    // top-k by warp 0: every lane owns experts lane, lane + 32, ...
-    if (warp == 0) {
-        uint32_t taken = 0;  // bit j: expert lane + 32 j is taken (E <= 1024)
+        for (int j = 0; j < PER_LANE; j++) {
+            const int e = lane + 32 * j;
+            lv[j] = e < E ? l[e] : -INFINITY;
+            mx = fmaxf(mx, lv[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        double pv[PER_LANE];
+        double part = 0.0;
+#pragma unroll
+        for (int j = 0; j < PER_LANE; j++) {
+            const int e = lane + 32 * j;
+            pv[j] = e < E ? exp((double) lv[j] - (double) mx) : -1.0;
+            if (e < E) part += pv[j];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        const double sum = part;
+        uint32_t taken = 0;
         double bv = -1.0;
         int bi = 0x7fffffff;
-        for (int j = 0, e = lane; e < E; j++, e += 32)
-            if (better(sp[e], e, bv, bi)) { bv = sp[e]; bi = e; }
+#pragma unroll
+        for (int j = 0; j < PER_LANE; j++)
+            if (better(pv[j], lane + 32 * j, bv, bi)) { bv = pv[j]; bi = lane + 32 * j; }
+        double chosen = 0.0, my_p = 0.0;
+        int my_id = 0;
         for (int i = 0; i < k; i++) {
             double v = bv;
             int ix = bi;
@@ -201,35 +212,31 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(const float* __restri
                 const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
                 if (better(ov, oi, v, ix)) { v = ov; ix = oi; }
             }
-            if (lane == 0) { sbv[i] = v; sbi[i] = ix; }
+            const double pn = v / sum;
+            chosen += pn;
+            if (lane == (i & 31)) { my_p = pn; my_id = ix; }  // lane i keeps rank i (k <= 64: two rounds)
+            if (i == 31 || i == k - 1) {
+                // flush ranks [i & ~31, i] written so far by their lanes
+                const int r = (i & ~31) + lane;
+                if (lane <= (i & 31)) {
+                    ids[(size_t) t * k + r] = my_id;
+                    wout[(size_t) t * k + r] = (float) my_p;  // raw (float) p; renormalised below
+                }
+            }
             if ((ix & 31) == lane) {
                 taken |= 1u << (ix >> 5);
                 bv = -1.0;
                 bi = 0x7fffffff;
-                for (int j = 0, e = lane; e < E; j++, e += 32)
-                    if (!((taken >> j) & 1u) && better(sp[e], e, bv, bi)) { bv = sp[e]; bi = e; }
+#pragma unroll
+                for (int j = 0; j < PER_LANE; j++)
+                    if (!((taken >> j) & 1u) && better(pv[j], lane + 32 * j, bv, bi)) { bv = pv[j]; bi = lane + 32 * j; }
             }
         }
+        chosen = fmax(chosen, 6.103515625e-05);
         __syncwarp();
-        if (lane == 0) {
-            double chosen = 0;
-            for (int i = 0; i < k; i++) chosen += sbv[i];
-            chosen = fmax(chosen, 6.103515625e-05);
-            for (int i = 0; i < k; i++) {
-                ids[(size_t) t * k + i] = sbi[i];
-                wout[(size_t) t * k + i] = (float) ((double) (float) sbv[i] / chosen);
-            }
-        }
-    }
-
-    if (xq) {
-        const float* xt = x + (size_t) t * H;
-        uint8_t* yt = xq + (size_t) t * (H / 32) * kQ8Block;
-        const int nb = H / 32;
-        for (int b = warp; b < nb; b += nw) {
-            const float xi = xt[b * 32 + lane];
-            quant_q8_1_warp(xi, yt + b * kQ8Block, lane);
-            if (xa.base) quant_ka_warp(xi, xa.base + ((size_t) t * nb + b) * kKaBlock, lane, xa_q2 != 0);
+        for (int r = lane; r < k; r += 32) {
+            float* wp = wout + (size_t) t * k + r;
+            *wp = (float) ((double) *wp / chosen);
         }
     }
 }
@@ -267,11 +274,12 @@ cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, cons
 
 cudaError_t launch_router_topk(const float* logits, int T, int E, int k, int32_t* ids, float* w, const float* x,
                                uint8_t* xq, int H, cudaStream_t s, const KAct* xa, int xa_q2) {
-    int threads = ((E + 31) / 32) * 32;
-    if (threads < 64) threads = 64;
-    if (threads > 1024) threads = 1024;
-    router_topk_kernel<<<T, threads, (size_t) E * sizeof(double), s>>>(logits, E, k, ids, w, x, xq, H,
-                                                                       xa ? *xa : KAct{}, xa_q2);
+    int blocks = (T + kTopkWarps - 1) / kTopkWarps;
+    if (xq) blocks += (int) (((int64_t) T * (H / 32) + kTopkWarps - 1) / kTopkWarps);
+    const KAct a = xa ? *xa : KAct{};
+    if (E <= 256) router_topk_kernel<8><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);
+    else if (E <= 512) router_topk_kernel<16><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);
+    else router_topk_kernel<32><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);
     return cudaGetLastError();
 }
 
