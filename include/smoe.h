@@ -153,6 +153,17 @@ typedef struct smoe_trace {
 enum { SMOE_STAGES = 6 };
 void smoe_set_stage_events(void** events, int n);
 
+/* Expert-kernel path of smoe_moe_forward (no reference counterpart: the reference has one GPU path).
+ * 0 (default) automatic: the tensor-core kernels for batches of 512 tokens or more when the layer qualifies,
+ * the SIMT kernels otherwise; 1 the SIMT kernels always; 2 the tensor-core kernels whenever the layer
+ * qualifies (every routed and shared matrix Q2_0, n_embd and n_ff multiples of 512).  The SIMT kernels
+ * evaluate the reference's q8_1 integer contract; the tensor-core kernels evaluate the same products from an
+ * exact fp16 hi/lo split of the q8_1 activation with f32 accumulation, so results agree up to the order of
+ * the f32 additions.  Process-wide. */
+smoe_status smoe_set_expert_path(int path);
+/* The path smoe_moe_forward takes for this layer and batch: 1 SIMT, 2 tensor cores, -1 invalid layer. */
+int smoe_expert_path_for(const smoe_layer* L, int n_tokens);
+
 /* Validates the layer's geometry and types: SMOE_OK when smoe_moe_forward can run it. */
 smoe_status smoe_layer_check(const smoe_layer* L);
 

@@ -14,7 +14,8 @@ from . import synth
 from ._lib import SmoeError, SmoeLayer, SmoeTrace, check, lib
 
 __all__ = ["SmoeError", "f32_to_bf16_bulk", "bf16_gemv", "router_top10", "router", "iq_quantize_q8_1", "iq_mmvq",
-           "iq_swiglu_q8", "moe_combine", "moe_group", "row_bytes", "q8_1_bytes", "MoeLayer", "device_status"]
+           "iq_swiglu_q8", "moe_combine", "moe_group", "row_bytes", "q8_1_bytes", "MoeLayer", "device_status",
+           "set_expert_path"]
 
 
 def _s() -> int:
@@ -37,6 +38,11 @@ def q8_1_bytes(n: int) -> int:
 
 def device_status(clear: bool = True) -> int:
     return int(lib().smoe_device_status(1 if clear else 0))
+
+
+def set_expert_path(path: int) -> None:
+    """0 automatic, 1 the SIMT expert kernels, 2 the tensor-core expert kernels where the layer qualifies."""
+    check(lib().smoe_set_expert_path(path))
 
 
 def f32_to_bf16_bulk(x: torch.Tensor, y: torch.Tensor, n: int | None = None) -> None:

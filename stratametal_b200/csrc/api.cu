@@ -4,6 +4,7 @@
 #include "common.cuh"
 #include "kernels.cuh"
 
+#include <atomic>
 #include <string>
 
 namespace smoe {
@@ -43,8 +44,29 @@ size_t up256(size_t n) { return (n + 255) & ~(size_t) 255; }
 
 // Scratch regions of the block for T tokens.
 struct Layout {
-    size_t xq, xa, xa2, logits, sh_logit, ids, w, slot, slot_token, tables, sched, gu, ha, parts, total;
+    size_t xq, xa, xa2, logits, sh_logit, ids, w, slot, slot_token, tables, sched, gu, ha, parts;
+    size_t sched_tc, xh, hh;  // the tensor-core path (0 bytes when the layer does not qualify)
+    size_t total;
 };
+
+// Expert path: 0 automatic (tensor cores from kTcAutoTokens tokens on), 1 the SIMT kernels, 2 tensor cores
+// whenever the layer qualifies.
+std::atomic<int> g_expert_path{0};
+constexpr int kTcAutoTokens = 512;
+
+// The tensor-core kernels take Q2_0 everywhere and rows whose byte length is a multiple of 16 (TMA strides):
+// n_embd and n_ff multiples of 512.
+bool tc_qualifies(const smoe_layer* L) {
+    const bool q2 = L->gu_type == kQ2_0 && L->d_type == kQ2_0 &&
+                    (!L->has_shared || (L->sg_type == kQ2_0 && L->su_type == kQ2_0 && L->sd_type == kQ2_0));
+    return q2 && L->n_embd % 512 == 0 && L->n_ff % 512 == 0;
+}
+
+bool use_tc(const smoe_layer* L, int T) {
+    const int p = g_expert_path.load(std::memory_order_relaxed);
+    if (p == 1 || !tc_qualifies(L)) return false;
+    return p == 2 || T >= kTcAutoTokens;
+}
 
 Layout layout_of(const smoe_layer* L, int T) {
     Layout o;
@@ -65,6 +87,12 @@ Layout layout_of(const smoe_layer* L, int T) {
     o.gu = at; at += up256(rows * 2 * F * 4);
     o.ha = at; at += up256(ka_bytes((int64_t) rows, (int) (F / 32)));
     o.parts = at; at += up256(rows * H * 4);
+    o.sched_tc = o.xh = o.hh = at;
+    if (tc_qualifies(L)) {
+        o.sched_tc = at; at += sched_bytes((int) E, T, (int) K, kTcChunk);
+        o.xh = at; at += up256((size_t) 2 * T * H * 2);
+        o.hh = at; at += up256(rows * 2 * F * 2);
+    }
     o.total = at;
     return o;
 }
@@ -104,6 +132,17 @@ using namespace smoe;
 extern "C" {
 
 const char* smoe_last_error(void) { return g_err.c_str(); }
+
+smoe_status smoe_set_expert_path(int path) {
+    if (path < 0 || path > 2) return fail(SMOE_INVALID_ARG, "set_expert_path: path must be 0, 1 or 2");
+    g_expert_path.store(path);
+    return ok();
+}
+
+int smoe_expert_path_for(const smoe_layer* L, int n_tokens) {
+    if (check_layer(L) != SMOE_OK || n_tokens <= 0) return -1;
+    return use_tc(L, n_tokens) ? 2 : 1;
+}
 
 void smoe_set_stage_events(void** events, int n) {
     g_stage_events = (events && n >= SMOE_STAGES) ? reinterpret_cast<cudaEvent_t*>(events) : nullptr;
@@ -307,10 +346,14 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
                                      E, s);
     if (e == cudaSuccess) e = mark(0, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: router");
-    e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, &xa, L->gu_type == kQ2_0);
+    const bool tc = use_tc(L, T);
+    e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, tc ? nullptr : &xa, L->gu_type == kQ2_0);
+    __half* xh = reinterpret_cast<__half*>(base + lo.xh);
+    if (e == cudaSuccess && tc) e = launch_quant_xh(x, T, H, xh, s);
     if (e == cudaSuccess) e = mark(1, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: top-k");
-    e = launch_group(ids, T, K, E, tabs, slot, slot_tok, s, &sc);
+    const Sched sct = tc ? sched_at(base + lo.sched_tc, E, T, K, kTcChunk) : sc;
+    e = launch_group(ids, T, K, E, tabs, slot, slot_tok, s, &sct);
     if (e == cudaSuccess) e = mark(2, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: dispatch");
 
@@ -324,6 +367,20 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     const Matrix mg{L->gate, gu_stride, L->gu_type}, mu{L->up, gu_stride, L->gu_type}, md{L->down, d_stride, L->d_type};
     const Matrix sg{L->sgate, 0, L->sg_type}, su{L->sup, 0, L->su_type}, sd{L->sdown, 0, L->sd_type};
 
+    if (tc) {
+        // tensor-core path: every matrix is Q2_0, so the shared expert rides in the routed launches
+        __half* hh = reinterpret_cast<__half*>(base + lo.hh);
+        Work wt = wk;
+        wt.sched = sct;
+        wt.max_entries = sched_capacity(E, T, K, kTcChunk);
+        wt.shared_slots = sh ? T : 0;
+        e = launch_tc_gate_up(mg, mu, sg, su, wt, E, xh, T, hh, rows, H, F, s);
+        if (e == cudaSuccess) e = mark(3, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: gate/up (tensor cores)");
+        e = launch_tc_down(md, sd, wt, E, hh, rows, parts, F, H, s);
+        if (e == cudaSuccess) e = mark(4, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: down (tensor cores)");
+    } else {
     // The shared expert rides in the routed launches when its types match; otherwise it gets its own.
     const bool gu_same = sh && L->sg_type == L->gu_type && L->su_type == L->gu_type;
     const bool d_same = sh && L->sd_type == L->d_type;
@@ -369,6 +426,7 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     }
     e = mark(4, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: stage event");
+    }
     e = launch_combine(parts, slot, w, sh ? parts + (int64_t) T * K * H : nullptr, sh ? sh_logit : nullptr, out,
                        trace ? trace->shared : nullptr, H, K, T, H, s);
     if (e == cudaSuccess) e = mark(5, s);

@@ -29,12 +29,14 @@ GroupTables group_tables_at(void* base, int n_expert) {
     return g;
 }
 
-size_t sched_bytes(int E, int T, int k) { return ((size_t) 3 * sched_capacity(E, T, k) * 4 + 4 + 255) & ~(size_t) 255; }
+size_t sched_bytes(int E, int T, int k, int chunk) {
+    return ((size_t) 3 * sched_capacity(E, T, k, chunk) * 4 + 4 + 255) & ~(size_t) 255;
+}
 
-Sched sched_at(void* base, int E, int T, int k) {
-    const int cap = sched_capacity(E, T, k);
+Sched sched_at(void* base, int E, int T, int k, int chunk) {
+    const int cap = sched_capacity(E, T, k, chunk);
     int32_t* p = static_cast<int32_t*>(base);
-    return Sched{p, p + cap, p + 2 * cap, p + 3 * cap};
+    return Sched{p, p + cap, p + 2 * cap, p + 3 * cap, chunk};
 }
 
 __device__ __forceinline__ uint32_t lanemask_lt() {
@@ -140,7 +142,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__
 
     // The work list: experts bucketed by min(count, 63), heaviest bucket first, ascending id inside a bucket
     // (per-warp bucket counts, scanned bucket-major then warp-minor, plus the rank among same-bucket lanes),
-    // then each expert cut into chunks of at most kChunk slots.
+    // then each expert cut into chunks of at most sched.chunk slots.
     __shared__ int whist[32][64];
     __shared__ int bucket_off[64];
     __shared__ int sorted[kMaxExperts];
@@ -177,15 +179,16 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__
     const int n_active = g.n_active[0];
     const int ej = tid < n_active ? sorted[tid] : -1;
     const int cj = ej >= 0 ? g.counts[ej] : 0;
-    const int nch = (cj + kChunk - 1) / kChunk;
+    const int chunk = sched.chunk;
+    const int nch = (cj + chunk - 1) / chunk;
     int total = 0;
     const int off = block_excl_scan(nch, warp_sums, &total);
     if (ej >= 0) {
         const int base = g.offsets[ej];
         for (int c = 0; c < nch; c++) {
             sched.e[off + c] = ej;
-            sched.beg[off + c] = base + c * kChunk;
-            sched.n[off + c] = min(kChunk, cj - c * kChunk);
+            sched.beg[off + c] = base + c * chunk;
+            sched.n[off + c] = min(chunk, cj - c * chunk);
         }
     }
     if (tid == 0) sched.count[0] = total;

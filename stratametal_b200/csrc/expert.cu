@@ -411,7 +411,7 @@ struct Entry {
 };
 
 __device__ __forceinline__ int shared_entries(const Work& w) {
-    return w.shared_slots > 0 ? (w.shared_slots + kChunk - 1) / kChunk : 0;
+    return w.shared_slots > 0 ? (w.shared_slots + w.sched.chunk - 1) / w.sched.chunk : 0;
 }
 
 __device__ __forceinline__ int work_entries(const Work& w) {
@@ -423,8 +423,8 @@ __device__ __forceinline__ Entry work_entry(const Work& w, int j) {
     const int sh = shared_entries(w);
     if (j < sh) {
         en.e = -1;
-        en.beg = w.shared_base + j * kChunk;
-        en.n = min(kChunk, w.shared_slots - j * kChunk);
+        en.beg = w.shared_base + j * w.sched.chunk;
+        en.n = min(w.sched.chunk, w.shared_slots - j * w.sched.chunk);
         en.shared = true;
     } else {
         const int jj = j - sh;

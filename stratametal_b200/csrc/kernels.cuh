@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 namespace smoe {
@@ -52,16 +53,18 @@ GroupTables group_tables_at(void* base, int n_expert);
 // Work list of the layer path: the active experts ordered heaviest first (token count descending, expert id
 // ascending), each split into chunks of at most kChunk slots.  Entry c covers slots [beg[c], beg[c] + n[c])
 // of expert e[c].
-constexpr int kChunk = 8;
+constexpr int kChunk = 8;     // the SIMT expert kernels
+constexpr int kTcChunk = 64;  // the tensor-core expert kernels
 struct Sched {
     int32_t* e;
     int32_t* beg;
     int32_t* n;
     int32_t* count;  // [1] entries
+    int chunk = kChunk;
 };
-inline int sched_capacity(int E, int T, int k) { return E + (T * k + kChunk - 1) / kChunk + 1; }
-size_t sched_bytes(int E, int T, int k);
-Sched sched_at(void* base, int E, int T, int k);
+inline int sched_capacity(int E, int T, int k, int chunk = kChunk) { return E + (T * k + chunk - 1) / chunk + 1; }
+size_t sched_bytes(int E, int T, int k, int chunk = kChunk);
+Sched sched_at(void* base, int E, int T, int k, int chunk = kChunk);
 
 // `sched` may be null (the stage entry points): then only the grouping tables are written.
 cudaError_t launch_group(const int32_t* ids, int T, int k, int E, GroupTables g, int32_t* slot, int32_t* src,
@@ -113,6 +116,16 @@ cudaError_t launch_layer_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix su
 cudaError_t launch_swiglu_ka(const float* gu, KAct ha, int64_t rows, int n_ff, int down_q2, cudaStream_t s);
 cudaError_t launch_layer_down(Matrix down, Matrix sdown, Work w, KAct ha, float* y, int n_ff, int n_embd,
                               cudaStream_t s);
+
+// ---- tc.cu ---- (Q2_0 weights; n_embd and n_ff multiples of 512; work list built with chunk kTcChunk)
+// xh: hi/lo fp16 image of the q8_1 activation, rows [0, T) hi and [T, 2T) lo.
+cudaError_t launch_quant_xh(const float* x, int T, int H, __half* xh, cudaStream_t s);
+// gate/up + SwiGLU + q8_1 of h into hh (hi rows [0, R), lo rows [R, 2R), R = slot rows).
+cudaError_t launch_tc_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, Work w, int n_expert,
+                              const __half* xh, int T, __half* hh, int R, int n_embd, int n_ff, cudaStream_t s);
+// down rows of every slot into parts[slot][n_embd].
+cudaError_t launch_tc_down(Matrix down, Matrix sdown, Work w, int n_expert, const __half* hh, int R, float* parts,
+                           int n_ff, int n_embd, cudaStream_t s);
 
 // ---- combine.cu ----
 // out[t][j] = sum_i w[t][i] * parts[slot(t, i)][j] (+ shared[t][j] * sigmoid(gate_logit[t]) when shared)

@@ -4,5 +4,6 @@
 #include "dispatch.cu"
 #include "expert.cu"
 #include "combine.cu"
+#include "tc.cu"
 #include "api.cu"
 #include "noalloc.cu"
