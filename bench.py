@@ -30,8 +30,9 @@ METRIC = "MoE-layer tokens/s (decode b1/b64, prefill 4k); expert-weight HBM GB/s
 UNIT = "tokens/s"
 STAGES = ["router_gemv", "router_topk_q8", "dispatch", "expert_gate_up", "expert_down", "combine"]
 KERNEL_OF_STAGE = {"router_gemv": "bf16_gemv_kernel", "router_topk_q8": "router_topk_kernel",
-                   "dispatch": "group_kernel", "expert_gate_up": "expert_gate_up_kernel",
-                   "expert_down": "expert_rows_kernel", "combine": "combine_kernel"}
+                   "dispatch": "group_kernel", "expert_gate_up": "layer_gate_up_kernel",
+                   "expert_down": "layer_down_kernel", "combine": "combine_kernel"}
+KERNEL_OF_STAGE_TC = dict(KERNEL_OF_STAGE, expert_gate_up="tc_expert_kernel<0>", expert_down="tc_expert_kernel<1>")
 
 
 def parse():
@@ -40,7 +41,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 4])
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
+    ap.add_argument("--expert-path", type=int, default=0, choices=[0, 1, 2],
+                    help="0 automatic, 1 SIMT expert kernels, 2 tensor-core expert kernels")
     ap.add_argument("--layers", type=int, default=4, help="distinct layers rotated through the steps")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -206,7 +209,7 @@ def max_over_ranks(v: float, ws: int) -> float:
 
 
 def config_dict(args, spec, T, D_mean):
-    return {"workload": f"configs[{args.config}]: one MoE layer, {T} decode tokens/step"
+    return {"workload": f"configs[{args.config}]: one MoE layer, {T} {'decode' if T <= 64 else 'prefill'} tokens/step"
                         + (", Zipf(1.1) expert popularity" if spec.zipf else "")
                         + (", IQ2_S gate/up" if spec.gu_type == 22 else ""),
             "tokens_per_step": T, "n_embd": spec.n_embd, "n_ff": spec.n_ff, "n_expert": spec.n_expert,
@@ -262,7 +265,9 @@ def run_ours(args, ws, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_stream(torch.cuda.Stream(dev))  # the C ABI wants an explicit non-null stream
     spec, T = synth.config_spec(args.config)
+    api.set_expert_path(args.expert_path)
     layers = [api.MoeLayer(synth.make_layer(spec, li, dev), T, dev) for li in range(args.layers)]
+    tc = lib().smoe_expert_path_for(C.byref(layers[0].c), T) == 2
     n_batches = 4
     xs = [synth.make_x(spec.seed + 1000 * local, T, spec.n_embd, dev, stream=b) for b in range(n_batches)]
     out = torch.empty(T, spec.n_embd, device=dev)
@@ -360,13 +365,22 @@ def run_ours(args, ws, rank, local):
         cpu = cpu_baseline(synth.make_layer(spec, 0, "cpu"), xs[0].cpu().numpy(), args.cpu_seconds)
 
     if rank == 0:
-        launches_per_step = 6 + (0 if spec.sg_type == spec.gu_type else 1) + (0 if spec.sd_type == spec.d_type else 1)
+        # router GEMV, top-k (+ q8_1), dispatch, gate/up, [SwiGLU], down, combine; the tensor-core path adds the
+        # hi/lo activation image and fuses SwiGLU into gate/up
+        if tc:
+            launches_per_step = 7
+        else:
+            launches_per_step = 7 + (0 if spec.sg_type == spec.gu_type else 2) + \
+                (0 if spec.sd_type == spec.d_type else 2)
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
                 "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "int8 x int2 dot (q8_1 contract), f32/f64 sums", "data": "synthetic",
+                "dtype": ("fp16 x fp16 tcgen05 (exact hi/lo q8_1 image), f32 accumulate" if tc
+                          else "int8 x int2 dot (q8_1 contract), f32/f64 sums"), "data": "synthetic",
+                "expert_path": "tensor cores (tcgen05)" if tc else "SIMT",
                 "config": config_dict(args, spec, T, D_mean),
                 "expert_weight_gbs": expert_gbs, "expert_weight_frac_of_peak": expert_gbs / hbm_peak,
-                "roofline": {"bound": "hbm", "kernel": KERNEL_OF_STAGE[dominant], "achieved": achieved,
+                "roofline": {"bound": "hbm", "kernel": (KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE)[dominant],
+                             "achieved": achieved,
                              "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
                              "frac": achieved / hbm_peak if achieved else None, "traffic": traffic,
                              "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms},

@@ -158,6 +158,28 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     return true;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase has not completed sleeps until it completes or the
+// hint elapses, instead of spinning on the issue slots its neighbours need.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait_bounded built on the sleeping try_wait.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
+        if (global_timer_ns() - t0 > limit_ns) return false;
+    }
+    return true;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }

@@ -1,8 +1,8 @@
 // tc.cu - grouped expert GEMMs on the 5th-generation tensor cores (tcgen05.mma kind::f16, f32 accumulators in
 // tensor memory) for work entries with many tokens: the prefill path.
 //
-// Shapes (swap-AB): M = 128 weight rows per tile (tensor-memory lanes), N = the entry's tokens (<= 64, padded to
-// a multiple of 16), K streamed in 64-wide stages (one Q2_0 block per row).
+// Shapes (swap-AB): M = 128 weight rows per tile (tensor-memory lanes), N = 2 x the entry's tokens (hi and lo
+// halves of <= 64 tokens each, padded to a multiple of 16), K streamed in 64-wide stages (one Q2_0 block per row).
 //
 //   gate/up item (MODE 0): 128 rows of gate and of up (two accumulators, so the thread that owns row r holds
 //                g_r and u_r), epilogue SwiGLU and the q8_1 rule over each warp's 32 rows (one block of h),
@@ -10,15 +10,20 @@
 //   down item (MODE 1):    128 output rows, K = n_ff, epilogue stores f32 per (slot, row).
 //
 // Operands.  Weights: Q2_0 blocks are TMA-loaded raw (2D boxes of 144 B x 128 rows = 8 blocks per row) and
-// decoded by four warps to fp16 (code - 1) * d, exact in fp16, into a K-major unswizzled shared-memory tile.
+// decoded by eight warps to fp16 (code - 1) * d, exact in fp16, into a K-major unswizzled shared-memory tile.
+// The decode ORs a code pair straight into the mantissas of an fp16 pair of power-of-two magnitude 2^E (the code
+// lands at the mantissa bit of weight 1), so one HADD2 of -(2^E + 1) gives code - 1 exactly and one HMUL2 by d
+// gives the weight.  That fixes the K order inside each 64-value block (tc_kpos): the activation images are
+// written in the same order, and a dot product does not depend on it.
 // Activations: the q8_1 image x~ = q * d (q the int8 code, d the fp16 scale) is exact in f32 but not in fp16, so
-// it is carried as two fp16 halves, hi = fp16(x~) and lo = fp16(x~ - hi), which together are exact.  Each K
-// step runs two MMAs into the same accumulator (A * hi, A * lo): the result is the integer contract's dot
-// product up to the order of the f32 additions.  Activation rows are gathered per token by TMA (tile::gather4)
-// into a 128-byte-swizzled tile: hi in rows 0..63, lo in rows 64..127.
+// it is carried as two fp16 halves, hi = fp16(x~) and lo = fp16(x~ - hi), which together are exact.  The B
+// tile stacks them, hi in rows [0, npad) and lo in rows [npad, 2 npad), so one MMA per K step yields both
+// partial products in adjacent accumulator columns and the epilogue adds them: the result is the integer
+// contract's dot product up to the order of the f32 additions.  Activation rows are gathered per token by TMA
+// (tile::gather4) into a 128-byte-swizzled tile.
 //
-// Warps: 0 producer (TMA; also allocates tensor memory), 1 MMA issuer (lane 0), 4-7 decoders, 8-11 epilogue
-// (warp 8 + q reads tensor-memory lanes 32q..32q+31).  Rings: raw weight quarters (2), A/B stages (3),
+// Warps: 0 producer (TMA; also allocates tensor memory), 1 MMA issuer (lane 0), 4-11 decoders, 12-15 epilogue
+// (warp 12 + q reads tensor-memory lanes 32q..32q+31).  Rings: raw weight quarters (2), A/B stages (3),
 // accumulators (2).  Every wait is bounded; on a timeout the kernel records kDevTimeout, drains the copies and
 // MMAs it issued (bounded), frees tensor memory and returns.
 #include "common.cuh"
@@ -34,7 +39,8 @@
 
 namespace smoe {
 
-constexpr int kTcThreads = 384;
+constexpr int kTcThreads = 512;
+constexpr int kTcDecWarps = 8;
 constexpr int kTcM = 128;
 constexpr int kTcK = 64;                          // K per A/B stage: one Q2_0 block per row
 constexpr int kTcQ = 512;                         // K per raw quarter: 8 blocks = 144 bytes per row
@@ -42,8 +48,7 @@ constexpr int kTcAB = 3;                          // A/B stages
 constexpr int kTcRaw = 2;                         // raw weight stages
 constexpr uint32_t kRawMat = kTcM * 144;          // 18,432 B: one matrix quarter
 constexpr uint32_t kAMat = kTcM * kTcK * 2;       // 16,384 B: one fp16 A tile
-constexpr uint32_t kBHalf = kTcChunk * kTcK * 2;  // 8,192 B: 64 activation rows of one half (hi or lo)
-constexpr uint32_t kBTile = 2 * kBHalf;
+constexpr uint32_t kBTile = 2 * kTcChunk * kTcK * 2;  // 16,384 B: up to 64 hi + 64 lo activation rows
 
 struct TcArgs {
     Work w;
@@ -80,23 +85,30 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(const void* smem_ptr) {
            (2ull << 61);
 }
 
-// fp16 of (code - 1) * d for 8 codes (two bytes of a Q2_0 block, value i at bits 2i): the 4-entry table
-// {-d, 0, d, 2d} as two fp16 pairs, selected with byte permutes.  Output word i = values 2i (low) and 2i + 1.
-__device__ __forceinline__ uint4 dec8_q2(uint32_t b2, uint32_t lo, uint32_t hi) {
-    uint32_t out[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const uint32_t t = (b2 >> (4 * i)) & 0xFu;  // c0 | c1 << 2
-        const uint32_t x = (t * 65u) & 0x303u;      // c0 | c1 << 8
-        const uint32_t sel = x * 0x22u + 0x1010u;   // byte selectors 2c0, 2c0 + 1, 2c1, 2c1 + 1
-        out[i] = __byte_perm(lo, hi, sel);
-    }
-    return make_uint4(out[0], out[1], out[2], out[3]);
+// K order inside a 64-value block.  A code word (16 codes, code v at bits 2v) decodes as 8 fp16 pairs: pair s
+// holds values s (low) and 8 + s (high), from bits 2s and 16 + 2s (s < 5) or of the word shifted right by 10
+// (s >= 5).  Word j fills 16-byte chunks 2j (pairs 0-3) and 2j + 1 (pairs 4-7), so value v of the block sits at
+// position tc_kpos(v).
+__host__ __device__ constexpr int tc_kpos(int v) {
+    return 16 * (v >> 4) + 8 * ((v & 7) >> 2) + 2 * (v & 3) + ((v >> 3) & 1);
+}
+
+// Pair s of code word w (see tc_kpos) as fp16 (code - 1) * d; d2 = d in both halves.
+template <int S>
+__device__ __forceinline__ uint32_t dec_pair(uint32_t w, uint32_t w10, __half2 d2) {
+    constexpr int s = S < 5 ? S : S - 5;                        // code bit position 2s after the shift
+    constexpr uint32_t mask = 0x00030003u << (2 * s);
+    constexpr uint32_t magic[5] = {0x64006400u, 0x5C005C00u, 0x54005400u, 0x4C004C00u, 0x44004400u};  // 2^(10-2s)
+    constexpr float bias[5] = {-1025.f, -257.f, -65.f, -17.f, -5.f};                                    // -(2^E + 1)
+    const uint32_t x = ((S < 5 ? w : w10) & mask) | magic[s];  // fp16 pair (2^E + c_lo, 2^E + c_hi)
+    const __half2 c = __hadd2(*reinterpret_cast<const __half2*>(&x), __float2half2_rn(bias[s]));
+    const __half2 v = __hmul2(c, d2);
+    return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 // A whole warp waits (bounded) for a phase; the verdict is the same for every lane.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-    const bool ok = mbar_wait_bounded(bar, parity, kWaitLimitNs);
+    const bool ok = mbar_wait_sleep(bar, parity, kWaitLimitNs);
     return __all_sync(0xffffffffu, ok);
 }
 
@@ -104,7 +116,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
 // before a role returns while copies or MMAs it issued may still be in flight.
 __device__ __forceinline__ void drain_ring(uint64_t* bars, int n, int count) {
     for (int i = max(0, count - n); i < count; i++)
-        mbar_wait_bounded(&bars[i % n], (uint32_t) ((i / n) & 1), kWaitLimitNs);
+        mbar_wait_sleep(&bars[i % n], (uint32_t) ((i / n) & 1), kWaitLimitNs);
 }
 
 template <int MODE>
@@ -115,19 +127,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                                                                   const __grid_constant__ CUtensorMap mact,
                                                                   TcArgs args) {
     constexpr int NMAT = MODE == 0 ? 2 : 1;
-    constexpr uint32_t kAccCols = NMAT * kTcChunk;  // one accumulator buffer
-    constexpr uint32_t kTmemCols = 2 * kAccCols;    // two buffers: 256 (gate/up) or 128 (down)
+    constexpr uint32_t kMatCols = 2 * kTcChunk;     // one matrix: hi columns [0, npad), lo [npad, 2 npad)
+    constexpr uint32_t kAccCols = NMAT * kMatCols;  // one accumulator buffer
+    constexpr uint32_t kTmemCols = 2 * kAccCols;    // two buffers: 512 (gate/up) or 256 (down)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    uint8_t* sB = smem;                                   // [kTcAB][hi 64 rows | lo 64 rows] x 128 B, swizzled
+    uint8_t* sB = smem;                                   // [kTcAB][hi npad rows | lo npad rows] x 128 B, swizzled
     uint8_t* sA = sB + kTcAB * kBTile;                    // [kTcAB][NMAT] 128 x 64 fp16, core-matrix layout
     uint8_t* sRaw = sA + kTcAB * NMAT * kAMat;            // [kTcRaw][NMAT] 128 rows x 144 B
     uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + kTcRaw * NMAT * kRawMat);
     uint64_t* raw_full = bars;                 // producer arrive + tx
-    uint64_t* raw_empty = raw_full + kTcRaw;   // 4 decoder warps
+    uint64_t* raw_empty = raw_full + kTcRaw;   // the decoder warps
     uint64_t* b_full = raw_empty + kTcRaw;     // producer arrive + tx
-    uint64_t* a_full = b_full + kTcAB;         // 4 decoder warps
+    uint64_t* a_full = b_full + kTcAB;         // the decoder warps
     uint64_t* ab_empty = a_full + kTcAB;       // MMA commit
     uint64_t* acc_full = ab_empty + kTcAB;     // MMA commit
     uint64_t* acc_empty = acc_full + 2;        // 4 epilogue warps
@@ -144,11 +157,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
     if (tid == 0) {
         for (int i = 0; i < kTcRaw; i++) {
             mbar_init(&raw_full[i], 1);
-            mbar_init(&raw_empty[i], 4);
+            mbar_init(&raw_empty[i], kTcDecWarps);
         }
         for (int i = 0; i < kTcAB; i++) {
             mbar_init(&b_full[i], 1);
-            mbar_init(&a_full[i], 4);
+            mbar_init(&a_full[i], kTcDecWarps);
             mbar_init(&ab_empty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
@@ -210,16 +223,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                         break;
                     }
                     uint8_t* bdst = sB + (size_t) st * kBTile;
+                    if (lane == 0) mbar_expect_tx(&b_full[st], (uint32_t) (2 * npad * kTcK * 2));
+                    __syncwarp();
                     if (MODE == 0) {
-                        if (lane == 0) mbar_expect_tx(&b_full[st], (uint32_t) (2 * npad * kTcK * 2));
-                        __syncwarp();
+                        // lane g < 16: hi rows 4g..4g+3; lane 16 + g: the same tokens' lo rows at npad + 4g
                         if (gather_lane)
-                            tma_gather4(bdst + (lane >= 16 ? kBHalf : 0) + g * 4 * 128, &mact, ks * kTcK, tk[0], tk[1],
+                            tma_gather4(bdst + ((lane >= 16 ? npad : 0) + 4 * g) * 128, &mact, ks * kTcK, tk[0], tk[1],
                                         tk[2], tk[3], &b_full[st]);
-                    } else if (lane == 0) {
-                        mbar_expect_tx(&b_full[st], kBTile);
-                        tma_load_2d(bdst, &mact, ks * kTcK, en.beg, &b_full[st]);
-                        tma_load_2d(bdst + kBHalf, &mact, ks * kTcK, args.act_rows + en.beg, &b_full[st]);
+                    } else {
+                        // 16-row boxes of consecutive slots: lane i < npad/16 hi rows, lane 8 + i lo rows
+                        const int i = lane & 7;
+                        if (lane < 16 && 16 * i < npad)
+                            tma_load_2d(bdst + ((lane >= 8 ? npad : 0) + 16 * i) * 128, &mact, ks * kTcK,
+                                        (lane >= 8 ? args.act_rows : 0) + en.beg + 16 * i, &b_full[st]);
                     }
                     sc++;
                 }
@@ -243,18 +259,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                 const Entry en = work_entry(w, id / args.m_tiles);
                 const int npad = (en.n + 15) & ~15;
                 const int a = j & 1;
-                if (j >= 2 && !mbar_wait_bounded(&acc_empty[a], (uint32_t) ((j / 2 - 1) & 1), kWaitLimitNs)) {
+                if (j >= 2 && !mbar_wait_sleep(&acc_empty[a], (uint32_t) ((j / 2 - 1) & 1), kWaitLimitNs)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t idesc = umma_idesc_f16(kTcM, npad);
+                const uint32_t idesc = umma_idesc_f16(kTcM, 2 * npad);
                 const uint32_t d0 = tmem + (uint32_t) a * kAccCols;
                 for (int ks = 0; ks < KS; ks++) {
                     const int st = sc % kTcAB;
                     const uint32_t par = (uint32_t) ((sc / kTcAB) & 1);
-                    if (!mbar_wait_bounded(&b_full[st], par, kWaitLimitNs) ||
-                        !mbar_wait_bounded(&a_full[st], par, kWaitLimitNs)) {
+                    if (!mbar_wait_sleep(&b_full[st], par, kWaitLimitNs) ||
+                        !mbar_wait_sleep(&a_full[st], par, kWaitLimitNs)) {
                         ok = false;
                         break;
                     }
@@ -263,13 +279,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
 #pragma unroll
                     for (int m = 0; m < NMAT; m++) {
                         const uint8_t* at = sA + ((size_t) st * NMAT + m) * kAMat;
-                        const uint32_t d = d0 + (uint32_t) (m * kTcChunk);
+                        const uint32_t d = d0 + (uint32_t) m * kMatCols;
 #pragma unroll
-                        for (int s = 0; s < kTcK / 16; s++) {
-                            const uint64_t ad = umma_desc(at + s * 256, 128, 1024);
-                            umma_f16(d, ad, umma_desc_sw128(bt + s * 32), idesc, (ks > 0 || s > 0) ? 1u : 0u);
-                            umma_f16(d, ad, umma_desc_sw128(bt + kBHalf + s * 32), idesc, 1u);
-                        }
+                        for (int s = 0; s < kTcK / 16; s++)
+                            umma_f16(d, umma_desc(at + s * 256, 128, 1024), umma_desc_sw128(bt + s * 32), idesc,
+                                     (ks > 0 || s > 0) ? 1u : 0u);
                     }
                     umma_commit(&ab_empty[st]);  // the stage is free once these MMAs have read it
                     issued = true;
@@ -281,15 +295,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
             if (!ok) atomicOr(&g_smoe_status, kDevTimeout);
             if (issued) {  // every MMA has retired before tensor memory is freed
                 umma_commit(mma_done);
-                mbar_wait_bounded(mma_done, 0, kWaitLimitNs);
+                mbar_wait_sleep(mma_done, 0, kWaitLimitNs);
             }
         }
         __syncwarp();
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 4 && warp < 4 + kTcDecWarps) {
         // ---------------- decoders: raw Q2_0 -> fp16 A tiles ----------------
-        // Pass i of 8 covers row dw*32 + (i/2)*8 + (lane&7), 8-value chunk (i&1)*4 + (lane>>3): a quarter-warp
-        // stores one 128-byte run of a core matrix, and the code reads of a warp fall in distinct banks.
+        // Pass i covers rows 8 (2 dw + i) + (lane&7), code word j = lane>>3 (chunks 2j, 2j + 1): a quarter-warp
+        // stores 128-byte runs of a core matrix, and the code reads of a warp fall in distinct banks.
         const int dw = warp - 4;
+        const int j4 = lane >> 3;
         int rc = 0, sc = 0;
         bool ok = true;
         for (int j = 0; ok; j++) {
@@ -315,17 +330,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                         uint8_t* at = sA + ((size_t) st * NMAT + m) * kAMat;
                         const uint8_t* rm = raw + m * kRawMat;
 #pragma unroll
-                        for (int i = 0; i < 8; i++) {
-                            const int r = dw * 32 + (i >> 1) * 8 + (lane & 7);
-                            const int kc = (i & 1) * 4 + (lane >> 3);
+                        for (int i = 0; i < 16 / kTcDecWarps; i++) {
+                            const int r = (2 * dw + i) * 8 + (lane & 7);
                             const uint8_t* blk = rm + r * 144 + boff;
-                            const __half d = __ushort_as_half(*reinterpret_cast<const uint16_t*>(blk));
-                            const uint32_t b2 = *reinterpret_cast<const uint16_t*>(blk + 2 + 2 * kc);
-                            const __half2 lo2 = __halves2half2(__hneg(d), __ushort_as_half((unsigned short) 0));
-                            const __half2 hi2 = __halves2half2(d, __hadd(d, d));
-                            *reinterpret_cast<uint4*>(at + kc * 128 + (r >> 3) * 1024 + (r & 7) * 16) =
-                                dec8_q2(b2, *reinterpret_cast<const uint32_t*>(&lo2),
-                                        *reinterpret_cast<const uint32_t*>(&hi2));
+                            const uint16_t* cw = reinterpret_cast<const uint16_t*>(blk + 2 + 4 * j4);
+                            const uint32_t w = (uint32_t) cw[0] | ((uint32_t) cw[1] << 16);
+                            const uint32_t w10 = w >> 10;
+                            const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
+                            uint8_t* dst = at + (2 * j4) * 128 + (r >> 3) * 1024 + (r & 7) * 16;
+                            *reinterpret_cast<uint4*>(dst) =
+                                make_uint4(dec_pair<0>(w, w10, d2), dec_pair<1>(w, w10, d2), dec_pair<2>(w, w10, d2),
+                                           dec_pair<3>(w, w10, d2));
+                            *reinterpret_cast<uint4*>(dst + 128) =
+                                make_uint4(dec_pair<4>(w, w10, d2), dec_pair<5>(w, w10, d2), dec_pair<6>(w, w10, d2),
+                                           dec_pair<7>(w, w10, d2));
                         }
                     }
                     fence_proxy_async();  // generic-proxy stores -> the tensor core's reads
@@ -340,15 +358,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
             }
         }
         if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
-    } else if (warp >= 8) {
+    } else if (warp >= 4 + kTcDecWarps) {
         // ---------------- epilogue: tensor memory -> h (gate/up) or the slot rows (down) ----------------
-        const int wq = warp - 8;  // tensor-memory lanes 32 wq .. 32 wq + 31
+        const int wq = warp & 3;  // tensor-memory lanes 32 wq .. 32 wq + 31
         bool ok = true;
         for (int j = 0; ok; j++) {
             const int id = (int) blockIdx.x + j * (int) gridDim.x;
             if (id >= n_items) break;
             const Entry en = work_entry(w, id / args.m_tiles);
             const int mt = id % args.m_tiles;
+            const int npad = (en.n + 15) & ~15;
             const int a = j & 1;
             if (!warp_wait(&acc_full[a], (uint32_t) ((j / 2) & 1))) {
                 ok = false;
@@ -358,9 +377,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
             const uint32_t tbase = tmem + ((uint32_t) (32 * wq) << 16) + (uint32_t) a * kAccCols;
             const int row = mt * kTcM + 32 * wq + lane;  // this thread's output row
             for (int c0 = 0; c0 < en.n; c0 += 8) {
-                uint32_t g8[8], u8[8];
+                uint32_t g8[8], gl8[8], u8[8], ul8[8];
                 tmem_ld8(tbase + (uint32_t) c0, g8);
-                if (MODE == 0) tmem_ld8(tbase + (uint32_t) (kTcChunk + c0), u8);
+                tmem_ld8(tbase + (uint32_t) (npad + c0), gl8);
+                if (MODE == 0) {
+                    tmem_ld8(tbase + kMatCols + (uint32_t) c0, u8);
+                    tmem_ld8(tbase + kMatCols + (uint32_t) (npad + c0), ul8);
+                }
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
@@ -369,7 +392,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                     const int slot = en.beg + t;
                     if (MODE == 0) {
                         // SwiGLU, then the q8_1 rule over the warp's 32 rows (one block of h), stored as hi/lo
-                        const float h = silu_mul(__uint_as_float(g8[i]), __uint_as_float(u8[i]));
+                        const float h = silu_mul(__fadd_rn(__uint_as_float(g8[i]), __uint_as_float(gl8[i])),
+                                                 __fadd_rn(__uint_as_float(u8[i]), __uint_as_float(ul8[i])));
                         float amax = fabsf(h);
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -380,10 +404,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                         const float v = __fmul_rn(qv, f16_to_f32(f16_bits(d)));
                         const __half hi = __float2half_rn(v);
                         const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
-                        args.hh[(size_t) slot * args.n_out + row] = hi;
-                        args.hh[((size_t) args.hh_rows + slot) * args.n_out + row] = lo;
+                        const int col = (row & ~63) + tc_kpos(row & 63);
+                        args.hh[(size_t) slot * args.n_out + col] = hi;
+                        args.hh[((size_t) args.hh_rows + slot) * args.n_out + col] = lo;
                     } else {
-                        args.parts[(size_t) slot * args.n_out + row] = __uint_as_float(g8[i]);
+                        args.parts[(size_t) slot * args.n_out + row] =
+                            __fadd_rn(__uint_as_float(g8[i]), __uint_as_float(gl8[i]));
                     }
                 }
             }
@@ -401,7 +427,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
     }
 }
 
-// q8_1 image of x as hi/lo fp16 halves: xh[t][i] = hi, xh[T + t][i] = lo, hi + lo = q * fp16(d) exactly.
+// q8_1 image of x as hi/lo fp16 halves, in the K order of tc_kpos: value i of token t goes to column
+// c = (i & ~63) + tc_kpos(i & 63), xh[t][c] = hi, xh[T + t][c] = lo, hi + lo = q * fp16(d) exactly.
 // One warp per 32-value block, the q8_1 rule of quant_q8_1_warp.
 __global__ void quant_xh_kernel(const float* __restrict__ x, int T, int H, __half* __restrict__ xh) {
     const int lane = threadIdx.x & 31;
@@ -419,8 +446,9 @@ __global__ void quant_xh_kernel(const float* __restrict__ x, int T, int H, __hal
         if (amax != 0.f) qv = fminf(fmaxf(roundf(__fdiv_rn(xi, d)), -127.f), 127.f);
         const float v = __fmul_rn(qv, f16_to_f32(f16_bits(d)));
         const __half hi = __float2half_rn(v);
-        xh[i] = hi;
-        xh[(int64_t) T * H + i] = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+        const int64_t c = (i & ~(int64_t) 63) + tc_kpos((int) (i & 63));
+        xh[c] = hi;
+        xh[(int64_t) T * H + c] = __float2half_rn(__fsub_rn(v, __half2float(hi)));
     }
 }
 
@@ -518,7 +546,7 @@ cudaError_t launch_tc_down(Matrix down, Matrix sdown, Work w, int n_expert, cons
     const bool ok = weight_map(&maps[0], down.base, routed_rows, rb) && weight_map(&maps[1], down.base, routed_rows, rb) &&
                     weight_map(&maps[2], sd, n_embd, rb) && weight_map(&maps[3], sd, n_embd, rb) &&
                     make_map(&maps[4], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, hh, (uint64_t) n_ff, (uint64_t) 2 * R,
-                             (uint64_t) n_ff * 2, kTcK, kTcChunk, CU_TENSOR_MAP_SWIZZLE_128B);
+                             (uint64_t) n_ff * 2, kTcK, 16, CU_TENSOR_MAP_SWIZZLE_128B);
     if (!ok) return cudaErrorInvalidValue;
     TcArgs a{};
     a.w = w;
