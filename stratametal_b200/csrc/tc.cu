@@ -1,8 +1,8 @@
 // tc.cu - grouped expert GEMMs on the 5th-generation tensor cores (tcgen05.mma kind::f16, f32 accumulators in
 // tensor memory) for work entries with many tokens: the prefill path.
 //
-// Shapes (swap-AB): M = 128 weight rows per tile (tensor-memory lanes), N = 2 x the entry's tokens (hi and lo
-// halves of <= 64 tokens each, padded to a multiple of 16), K streamed in 64-wide stages (one Q2_0 block per row).
+// Shapes (swap-AB): M = 128 weight rows per tile (tensor-memory lanes), N = the entry's tokens (<= 64, padded to a
+// multiple of 16), K streamed in 64-wide stages (one Q2_0 block per row).
 //
 //   gate/up item (MODE 0): 128 rows of gate and of up (two accumulators, so the thread that owns row r holds
 //                g_r and u_r), epilogue SwiGLU and the q8_1 rule over each warp's 32 rows (one block of h),
@@ -10,22 +10,27 @@
 //   down item (MODE 1):    128 output rows, K = n_ff, epilogue stores f32 per (slot, row).
 //
 // Operands.  Weights: Q2_0 blocks are TMA-loaded raw (2D boxes of 144 B x 128 rows = 8 blocks per row) and
-// decoded by eight warps to fp16 (code - 1) * d, exact in fp16, into a K-major unswizzled shared-memory tile.
-// The decode ORs a code pair straight into the mantissas of an fp16 pair of power-of-two magnitude 2^E (the code
-// lands at the mantissa bit of weight 1), so one HADD2 of -(2^E + 1) gives code - 1 exactly and one HMUL2 by d
-// gives the weight.  That fixes the K order inside each 64-value block (tc_kpos): the activation images are
-// written in the same order, and a dot product does not depend on it.
+// decoded by eight warps to fp16 (code - 1) * d, exact in fp16, straight into tensor memory (tcgen05.st; the
+// thread that owns tensor-memory lane r decodes weight row r), where the MMA reads A: the decoded tile never
+// touches shared memory, which is left to the activation tiles.  The decode ORs a code pair straight into the
+// mantissas of an fp16 pair of power-of-two magnitude 2^E (the code lands at the mantissa bit of weight 1), so
+// one HADD2 of -(2^E + 1) gives code - 1 exactly and one HMUL2 by d gives the weight.  That fixes the K order
+// inside each 64-value block (tc_kpos): the activation images are written in the same order, and a dot product
+// does not depend on it.
 // Activations: the q8_1 image x~ = q * d (q the int8 code, d the fp16 scale) is exact in f32 but not in fp16, so
 // it is carried as two fp16 halves, hi = fp16(x~) and lo = fp16(x~ - hi), which together are exact.  The B
-// tile stacks them, hi in rows [0, npad) and lo in rows [npad, 2 npad), so one MMA per K step yields both
-// partial products in adjacent accumulator columns and the epilogue adds them: the result is the integer
-// contract's dot product up to the order of the f32 additions.  Activation rows are gathered per token by TMA
-// (tile::gather4) into a 128-byte-swizzled tile.
+// tile stacks them, hi in rows [0, npad) and lo in rows [npad, 2 npad), so one MMA of N = 2 npad per K step
+// yields both partial products in adjacent accumulator columns and the epilogue adds them: the result is the
+// integer contract's dot product up to the order of the f32 additions.  Gate/up gathers its rows per token with
+// 16-byte cp.async copies into a 128-byte-swizzled tile; down reads consecutive slots with TMA boxes.
 //
-// Warps: 0 producer (TMA; also allocates tensor memory), 1 MMA issuer (lane 0), 4-11 decoders, 12-15 epilogue
-// (warp 12 + q reads tensor-memory lanes 32q..32q+31).  Rings: raw weight quarters (2), A/B stages (3),
-// accumulators (2).  Every wait is bounded; on a timeout the kernel records kDevTimeout, drains the copies and
-// MMAs it issued (bounded), frees tensor memory and returns.
+// Warps: 0 raw weight producer (TMA; also allocates tensor memory), 1 MMA issuer (lane 0), 2-3 activation
+// producers, 4-11 decoders, 12-19 epilogue (warp 12 + 4h + q reads tensor-memory lanes 32q..32q+31, token groups
+// h, h + 2, ...).  Rings: raw weight quarters (2 or 4), decoded A stages (3, tensor memory), activation stages
+// (4 or 6), accumulators (1 for gate/up, whose epilogue frees it after copying g and u to shared memory; 2 for
+// down), each with its own full/empty barriers, so weight prefetch runs ahead of the activations.
+// Every wait is bounded; on a timeout the kernel records kDevTimeout, drains the copies and MMAs it issued
+// (bounded), frees tensor memory and returns.
 #include "common.cuh"
 #include "kernels.cuh"
 #include "q8.cuh"
@@ -39,19 +44,20 @@
 
 namespace smoe {
 
-constexpr int kTcThreads = 512;
-constexpr int kTcDecWarps = 8;
+constexpr int kTcDecWarps = 8;                    // warps 4..11
+constexpr int kTcEpiWarp0 = 4 + kTcDecWarps;      // warps 12..19
+constexpr int kTcEpiWarps = 8;
+constexpr int kTcThreads = 32 * (kTcEpiWarp0 + kTcEpiWarps);
 constexpr int kTcM = 128;
 constexpr int kTcK = 64;                          // K per A/B stage: one Q2_0 block per row
 constexpr int kTcQ = 512;                         // K per raw quarter: 8 blocks = 144 bytes per row
-constexpr int kTcAB = 3;                          // A/B stages
-constexpr int kTcRaw = 2;                         // raw weight stages
 constexpr uint32_t kRawMat = kTcM * 144;          // 18,432 B: one matrix quarter
-constexpr uint32_t kAMat = kTcM * kTcK * 2;       // 16,384 B: one fp16 A tile
 constexpr uint32_t kBTile = 2 * kTcChunk * kTcK * 2;  // 16,384 B: up to 64 hi + 64 lo activation rows
+constexpr int kBRowsPerThread = 2 * kTcChunk / 8;     // tile rows per activation-producer thread
 
 struct TcArgs {
     Work w;
+    const __half* act;  // activation image: hi rows [0, act_rows), lo rows [act_rows, 2 act_rows), K columns
     int K;          // n_embd (gate/up) or n_ff (down)
     int m_tiles;    // row tiles per expert matrix
     int act_rows;   // rows of one activation half: T (gate/up, per token) or R (down, per slot)
@@ -69,14 +75,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
         : "memory");
 }
 
-__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, int x, int y0, int y1, int y2, int y3,
-                                            uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-        "%3, %4, %5, %6}], [%7];" ::"r"(smem_addr(dst)),
-        "l"(map), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(smem_addr(bar))
-        : "memory");
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
+
+// One arrival on `bar` once every cp.async this thread issued before has completed (counted in the barrier's
+// expected arrivals).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // K-major 128-byte-swizzled descriptor (a TMA-written activation tile, 128 B per row): 1024 B between 8-row groups.
 __device__ __forceinline__ uint64_t umma_desc_sw128(const void* smem_ptr) {
@@ -119,6 +128,26 @@ __device__ __forceinline__ void drain_ring(uint64_t* bars, int n, int count) {
         mbar_wait_sleep(&bars[i % n], (uint32_t) ((i / n) & 1), kWaitLimitNs);
 }
 
+// Ring depths, shared memory and tensor memory per mode (gate/up holds two matrices per stage).
+// Gate/up keeps one accumulator buffer (gate and up, hi and lo columns: 256) beside three A stages; its epilogue
+// frees the buffer as soon as g and u sit in a shared-memory staging area.  Down keeps two buffers.
+template <int MODE> struct TcCfg {
+    static constexpr int NMAT = MODE == 0 ? 2 : 1;
+    static constexpr int kRaw = MODE == 0 ? 2 : 4;                // raw weight quarters (shared memory)
+    static constexpr int kA = 3;                                  // decoded A stages (tensor memory)
+    static constexpr int kB = MODE == 0 ? 4 : 6;                  // activation stages (shared memory)
+    static constexpr int kAccBufs = MODE == 0 ? 1 : 2;
+    static constexpr uint32_t kMatCols = 2 * kTcChunk;            // one matrix: hi [0, npad), lo [npad, 2 npad)
+    static constexpr uint32_t kAccCols = NMAT * kMatCols;         // one accumulator buffer
+    static constexpr uint32_t kAOff = kAccBufs * kAccCols;        // A stages follow the accumulator buffers
+    static constexpr uint32_t kACols = NMAT * kTcK / 2;           // one A stage: 64 fp16 per row per matrix
+    static constexpr uint32_t kTmemCols = 512;
+    static_assert(kAOff + kA * kACols <= kTmemCols, "tensor memory budget");
+    static constexpr size_t kStage = MODE == 0 ? (size_t) kTcEpiWarps * 2 * 32 * (kTcChunk / 2) * 4 : 0;  // g, u
+    static constexpr size_t smem =
+        (size_t) kB * kBTile + (size_t) kRaw * NMAT * kRawMat + kStage + 64 * 8 + 1024;
+};
+
 template <int MODE>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_constant__ CUtensorMap mw0,
                                                                   const __grid_constant__ CUtensorMap mw1,
@@ -126,25 +155,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                                                                   const __grid_constant__ CUtensorMap sw1,
                                                                   const __grid_constant__ CUtensorMap mact,
                                                                   TcArgs args) {
-    constexpr int NMAT = MODE == 0 ? 2 : 1;
-    constexpr uint32_t kMatCols = 2 * kTcChunk;     // one matrix: hi columns [0, npad), lo [npad, 2 npad)
-    constexpr uint32_t kAccCols = NMAT * kMatCols;  // one accumulator buffer
-    constexpr uint32_t kTmemCols = 2 * kAccCols;    // two buffers: 512 (gate/up) or 256 (down)
+    using Cfg = TcCfg<MODE>;
+    constexpr int NMAT = Cfg::NMAT, kRaw = Cfg::kRaw, kA = Cfg::kA, kB = Cfg::kB, kAccBufs = Cfg::kAccBufs;
+    constexpr uint32_t kMatCols = Cfg::kMatCols, kAccCols = Cfg::kAccCols, kAOff = Cfg::kAOff, kACols = Cfg::kACols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    uint8_t* sB = smem;                                   // [kTcAB][hi npad rows | lo npad rows] x 128 B, swizzled
-    uint8_t* sA = sB + kTcAB * kBTile;                    // [kTcAB][NMAT] 128 x 64 fp16, core-matrix layout
-    uint8_t* sRaw = sA + kTcAB * NMAT * kAMat;            // [kTcRaw][NMAT] 128 rows x 144 B
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sRaw + kTcRaw * NMAT * kRawMat);
-    uint64_t* raw_full = bars;                 // producer arrive + tx
-    uint64_t* raw_empty = raw_full + kTcRaw;   // the decoder warps
-    uint64_t* b_full = raw_empty + kTcRaw;     // producer arrive + tx
-    uint64_t* a_full = b_full + kTcAB;         // the decoder warps
-    uint64_t* ab_empty = a_full + kTcAB;       // MMA commit
-    uint64_t* acc_full = ab_empty + kTcAB;     // MMA commit
-    uint64_t* acc_empty = acc_full + 2;        // 4 epilogue warps
-    uint64_t* mma_done = acc_empty + 2;        // MMA commit (the final drain)
+    uint8_t* sB = smem;                          // [kB][hi npad rows | lo npad rows] x 128 B, 128-byte swizzle
+    uint8_t* sRaw = sB + kB * kBTile;            // [kRaw][NMAT] 128 rows x 144 B
+    float* sStage = reinterpret_cast<float*>(sRaw + kRaw * NMAT * kRawMat);  // gate/up: per epilogue warp g, u
+    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sStage) + Cfg::kStage);
+    uint64_t* raw_full = bars;                   // raw producer arrive + tx
+    uint64_t* raw_empty = raw_full + kRaw;       // the decoder warps
+    uint64_t* a_full = raw_empty + kRaw;         // the decoder warps
+    uint64_t* a_empty = a_full + kA;             // MMA commit
+    uint64_t* b_full = a_empty + kA;             // gate/up: 64 cp.async arrivals; down: producer arrive + tx
+    uint64_t* b_empty = b_full + kB;             // MMA commit
+    uint64_t* acc_full = b_empty + kB;           // MMA commit
+    uint64_t* acc_empty = acc_full + 2;          // the epilogue warps
+    uint64_t* mma_done = acc_empty + 2;          // MMA commit (the final drain)
     __shared__ uint32_t s_tmem;
 
     const Work w = args.w;
@@ -155,24 +184,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
     const int n_items = work_entries(w) * args.m_tiles;
 
     if (tid == 0) {
-        for (int i = 0; i < kTcRaw; i++) {
+        for (int i = 0; i < kRaw; i++) {
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_empty[i], kTcDecWarps);
         }
-        for (int i = 0; i < kTcAB; i++) {
-            mbar_init(&b_full[i], 1);
+        for (int i = 0; i < kA; i++) {
             mbar_init(&a_full[i], kTcDecWarps);
-            mbar_init(&ab_empty[i], 1);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < kB; i++) {
+            mbar_init(&b_full[i], MODE == 0 ? 64 : 1);
+            mbar_init(&b_empty[i], 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 4);
+            mbar_init(&acc_empty[i], kTcEpiWarps);
         }
         mbar_init(mma_done, 1);
         fence_mbar_init();
     }
     if (warp == 0) {
-        tmem_alloc(&s_tmem, kTmemCols);
+        tmem_alloc(&s_tmem, Cfg::kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -181,30 +213,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
     const uint32_t tmem = s_tmem;
 
     if (warp == 0) {
-        // ---------------- producer warp: raw weight quarters (lane 0) and activation rows ----------------
-        int rc = 0, sc = 0;
+        // ---------------- raw weight producer: one quarter of every matrix per raw stage ----------------
+        int rc = 0;
         bool ok = true;
         for (int j = 0; ok; j++) {
             const int id = (int) blockIdx.x + j * (int) gridDim.x;
             if (id >= n_items) break;
             const Entry en = work_entry(w, id / args.m_tiles);
-            const int mt = id % args.m_tiles;
-            const int npad = (en.n + 15) & ~15;
-            // lane l < 16 gathers hi rows 4l..4l+3, lane l >= 16 the same tokens' lo rows
-            const int g = lane & 15;
-            int tk[4] = {0, 0, 0, 0};
-            if (MODE == 0) {
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int rr = min(4 * g + u, en.n - 1);  // padding rows repeat the last token
-                    tk[u] = entry_token(w, en, en.beg + rr) + (lane >= 16 ? args.act_rows : 0);
-                }
-            }
-            const bool gather_lane = 4 * g < npad;
-            const int row = (en.shared ? 0 : en.e * args.m_tiles * kTcM) + mt * kTcM;
-            for (int q = 0; q < QS && ok; q++) {
-                const int rs = rc % kTcRaw;
-                if (rc >= kTcRaw && !warp_wait(&raw_empty[rs], (uint32_t) ((rc / kTcRaw - 1) & 1))) {
+            const int row = (en.shared ? 0 : en.e * args.m_tiles * kTcM) + (id % args.m_tiles) * kTcM;
+            for (int q = 0; q < QS; q++) {
+                const int rs = rc % kRaw;
+                if (rc >= kRaw && !warp_wait(&raw_empty[rs], (uint32_t) ((rc / kRaw - 1) & 1))) {
                     ok = false;
                     break;
                 }
@@ -215,41 +234,72 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                     if (NMAT == 2) tma_load_2d(dst + kRawMat, en.shared ? &sw1 : &mw1, q * 144, row, &raw_full[rs]);
                 }
                 rc++;
-                const int k_end = min(KS, (q + 1) * kQS);
-                for (int ks = q * kQS; ks < k_end; ks++) {
-                    const int st = sc % kTcAB;
-                    if (sc >= kTcAB && !warp_wait(&ab_empty[st], (uint32_t) ((sc / kTcAB - 1) & 1))) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t* bdst = sB + (size_t) st * kBTile;
-                    if (lane == 0) mbar_expect_tx(&b_full[st], (uint32_t) (2 * npad * kTcK * 2));
-                    __syncwarp();
-                    if (MODE == 0) {
-                        // lane g < 16: hi rows 4g..4g+3; lane 16 + g: the same tokens' lo rows at npad + 4g
-                        if (gather_lane)
-                            tma_gather4(bdst + ((lane >= 16 ? npad : 0) + 4 * g) * 128, &mact, ks * kTcK, tk[0], tk[1],
-                                        tk[2], tk[3], &b_full[st]);
-                    } else {
-                        // 16-row boxes of consecutive slots: lane i < npad/16 hi rows, lane 8 + i lo rows
-                        const int i = lane & 7;
-                        if (lane < 16 && 16 * i < npad)
-                            tma_load_2d(bdst + ((lane >= 8 ? npad : 0) + 16 * i) * 128, &mact, ks * kTcK,
-                                        (lane >= 8 ? args.act_rows : 0) + en.beg + 16 * i, &b_full[st]);
-                    }
-                    sc++;
-                }
             }
         }
         if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
-        // every copy this warp issued has landed before the shared memory is released
-        if (lane == 0) {
-            drain_ring(raw_full, kTcRaw, rc);
-            drain_ring(b_full, kTcAB, sc);
-        }
+        if (lane == 0) drain_ring(raw_full, kRaw, rc);  // every copy has landed before shared memory is released
         __syncwarp();
+    } else if (warp == 2 || (MODE == 0 && warp == 3)) {
+        // ---------------- activation producers: the entry's hi and lo rows for each K stage ----------------
+        // Tile row rho < npad is the hi row of entry row rho, row npad + rho its lo row (128-byte swizzle).
+        // gate/up (rows are tokens): 16-byte cp.async copies, thread pt copying chunk pt & 7 of rows
+        // (pt >> 3) + 8i, each thread's arrival firing when its copies have landed.  down (rows are consecutive
+        // slots): TMA boxes of 16 rows.
+        const int pt = tid - 64;
+        const int ch = pt & 7;
+        int bc = 0;
+        bool ok = true;
+        for (int j = 0; ok; j++) {
+            const int id = (int) blockIdx.x + j * (int) gridDim.x;
+            if (id >= n_items) break;
+            const Entry en = work_entry(w, id / args.m_tiles);
+            const int npad = (en.n + 15) & ~15;
+            const int nrow = 2 * npad;  // tile rows, a multiple of 32
+            const __half* src[kBRowsPerThread];
+            if (MODE == 0) {
+#pragma unroll
+                for (int i = 0; i < kBRowsPerThread; i++) {
+                    const int rho = (pt >> 3) + 8 * i;
+                    const int er = min(rho < npad ? rho : rho - npad, en.n - 1);  // padding repeats the last row
+                    src[i] = args.act + (size_t) (entry_token(w, en, en.beg + er) + (rho < npad ? 0 : args.act_rows)) *
+                                            K + ch * 8;
+                }
+            }
+            for (int ks = 0; ks < KS; ks++) {
+                const int st = bc % kB;
+                if (bc >= kB && !warp_wait(&b_empty[st], (uint32_t) ((bc / kB - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* bt = sB + (size_t) st * kBTile;
+                if (MODE == 0) {
+                    const uint32_t bdst = smem_addr(bt);
+#pragma unroll
+                    for (int i = 0; i < kBRowsPerThread; i++) {
+                        const int rho = (pt >> 3) + 8 * i;
+                        if (rho < nrow) cp_async16(bdst + rho * 128 + ((ch ^ (rho & 7)) << 4), src[i] + ks * kTcK);
+                    }
+                    cp_async_arrive_noinc(&b_full[st]);
+                } else {
+                    if (lane == 0) mbar_expect_tx(&b_full[st], (uint32_t) (nrow * kTcK * 2));
+                    __syncwarp();
+                    const int i = lane & 7;  // lane i < 8: hi rows 16i.., lane 8 + i: lo rows npad + 16i..
+                    if (lane < 16 && 16 * i < npad)
+                        tma_load_2d(bt + ((lane >= 8 ? npad : 0) + 16 * i) * 128, &mact, ks * kTcK,
+                                    (lane >= 8 ? args.act_rows : 0) + en.beg + 16 * i, &b_full[st]);
+                }
+                bc++;
+            }
+        }
+        if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
+        if (MODE == 0) {
+            cp_async_wait_all();  // every copy has landed before shared memory is released
+        } else {
+            if (lane == 0) drain_ring(b_full, kB, bc);
+            __syncwarp();
+        }
     } else if (warp == 1) {
-        // ---------------- MMA issuer (lane 0) ----------------
+        // ---------------- MMA issuer (lane 0): A from tensor memory, B from shared memory ----------------
         if (lane == 0) {
             int sc = 0;
             bool ok = true, issued = false;
@@ -258,36 +308,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                 if (id >= n_items) break;
                 const Entry en = work_entry(w, id / args.m_tiles);
                 const int npad = (en.n + 15) & ~15;
-                const int a = j & 1;
-                if (j >= 2 && !mbar_wait_sleep(&acc_empty[a], (uint32_t) ((j / 2 - 1) & 1), kWaitLimitNs)) {
+                const int a = j % kAccBufs;
+                if (j >= kAccBufs &&
+                    !mbar_wait_sleep(&acc_empty[a], (uint32_t) ((j / kAccBufs - 1) & 1), kWaitLimitNs)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t idesc = umma_idesc_f16(kTcM, 2 * npad);
+                const uint32_t idesc = umma_idesc_f16(kTcM, 2 * npad);  // hi and lo rows in one MMA
                 const uint32_t d0 = tmem + (uint32_t) a * kAccCols;
-                for (int ks = 0; ks < KS; ks++) {
-                    const int st = sc % kTcAB;
-                    const uint32_t par = (uint32_t) ((sc / kTcAB) & 1);
-                    if (!mbar_wait_sleep(&b_full[st], par, kWaitLimitNs) ||
-                        !mbar_wait_sleep(&a_full[st], par, kWaitLimitNs)) {
+                for (int ks = 0; ks < KS; ks++, sc++) {
+                    const int sa = sc % kA, sb = sc % kB;
+                    if (!mbar_wait_sleep(&b_full[sb], (uint32_t) ((sc / kB) & 1), kWaitLimitNs) ||
+                        !mbar_wait_sleep(&a_full[sa], (uint32_t) ((sc / kA) & 1), kWaitLimitNs)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint8_t* bt = sB + (size_t) st * kBTile;
+                    fence_proxy_async();  // cp.async (generic proxy) writes -> the tensor core's reads
+                    // descriptors advance by constants: 16 K values = 8 A columns = 32 B of a B row (2 in the
+                    // descriptor's 16-byte address units)
+                    const uint64_t bd = umma_desc_sw128(sB + (size_t) sb * kBTile);
+                    const uint32_t at0 = tmem + kAOff + (uint32_t) sa * kACols;
+                    const uint32_t first = ks > 0 ? 1u : 0u;
 #pragma unroll
                     for (int m = 0; m < NMAT; m++) {
-                        const uint8_t* at = sA + ((size_t) st * NMAT + m) * kAMat;
                         const uint32_t d = d0 + (uint32_t) m * kMatCols;
+                        const uint32_t at = at0 + (uint32_t) m * (kTcK / 2);
 #pragma unroll
-                        for (int s = 0; s < kTcK / 16; s++)
-                            umma_f16(d, umma_desc(at + s * 256, 128, 1024), umma_desc_sw128(bt + s * 32), idesc,
-                                     (ks > 0 || s > 0) ? 1u : 0u);
+                        for (int s = 0; s < kTcK / 16; s++) umma_f16_ts(d, at + 8 * s, bd + 2 * s, idesc, s > 0 ? 1u : first);
                     }
-                    umma_commit(&ab_empty[st]);  // the stage is free once these MMAs have read it
+                    umma_commit(&a_empty[sa]);  // each stage is free once these MMAs have read it
+                    umma_commit(&b_empty[sb]);
                     issued = true;
-                    sc++;
                 }
                 if (!ok) break;
                 umma_commit(&acc_full[a]);
@@ -300,56 +353,64 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
         }
         __syncwarp();
     } else if (warp >= 4 && warp < 4 + kTcDecWarps) {
-        // ---------------- decoders: raw Q2_0 -> fp16 A tiles ----------------
-        // Pass i covers rows 8 (2 dw + i) + (lane&7), code word j = lane>>3 (chunks 2j, 2j + 1): a quarter-warp
-        // stores 128-byte runs of a core matrix, and the code reads of a warp fall in distinct banks.
-        const int dw = warp - 4;
-        const int j4 = lane >> 3;
+        // ---------------- decoders: raw Q2_0 -> fp16 A in tensor memory ----------------
+        // Warp 4 + 4 role + q decodes rows 32q + lane (its tensor-memory lanes): gate/up, matrix `role` (all 64
+        // values of the block); down, the block's code words 2 role and 2 role + 1.  Code word j, pair s lands in
+        // A column 8j + s (low half value 16j + s, high half 16j + 8 + s: the K order of tc_kpos).
+        const int q = warp & 3, role = (warp - 4) >> 2;
+        const int m = MODE == 0 ? role : 0;
+        constexpr int NW = MODE == 0 ? 4 : 2;  // code words per thread per stage
+        const int j0 = MODE == 0 ? 0 : 2 * role;
+        const int r = 32 * q + lane;
         int rc = 0, sc = 0;
         bool ok = true;
         for (int j = 0; ok; j++) {
             const int id = (int) blockIdx.x + j * (int) gridDim.x;
             if (id >= n_items) break;
-            for (int q = 0; q < QS && ok; q++) {
-                const int rs = rc % kTcRaw;
-                if (!warp_wait(&raw_full[rs], (uint32_t) ((rc / kTcRaw) & 1))) {
+            for (int qq = 0; qq < QS && ok; qq++) {
+                const int rs = rc % kRaw;
+                if (!warp_wait(&raw_full[rs], (uint32_t) ((rc / kRaw) & 1))) {
                     ok = false;
                     break;
                 }
-                const uint8_t* raw = sRaw + (size_t) rs * NMAT * kRawMat;
-                const int k_end = min(KS, (q + 1) * kQS);
-                for (int ks = q * kQS; ks < k_end; ks++) {
-                    const int st = sc % kTcAB;
-                    if (sc >= kTcAB && !warp_wait(&ab_empty[st], (uint32_t) ((sc / kTcAB - 1) & 1))) {
+                const uint8_t* rowp = sRaw + ((size_t) rs * NMAT + m) * kRawMat + r * 144;
+                const int k_end = min(KS, (qq + 1) * kQS);
+                for (int ks = qq * kQS; ks < k_end; ks++, sc++) {
+                    const int sa = sc % kA;
+                    const uint8_t* blk = rowp + (ks - qq * kQS) * 18;
+                    uint32_t wv[NW];
+#pragma unroll
+                    for (int i = 0; i < NW; i++) {
+                        const uint16_t* cw = reinterpret_cast<const uint16_t*>(blk + 2 + 4 * (j0 + i));
+                        wv[i] = (uint32_t) cw[0] | ((uint32_t) cw[1] << 16);
+                    }
+                    const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
+                    uint32_t col[8 * NW];
+#pragma unroll
+                    for (int i = 0; i < NW; i++) {
+                        const uint32_t wq = wv[i], w10 = wq >> 10;
+                        col[8 * i + 0] = dec_pair<0>(wq, w10, d2);
+                        col[8 * i + 1] = dec_pair<1>(wq, w10, d2);
+                        col[8 * i + 2] = dec_pair<2>(wq, w10, d2);
+                        col[8 * i + 3] = dec_pair<3>(wq, w10, d2);
+                        col[8 * i + 4] = dec_pair<4>(wq, w10, d2);
+                        col[8 * i + 5] = dec_pair<5>(wq, w10, d2);
+                        col[8 * i + 6] = dec_pair<6>(wq, w10, d2);
+                        col[8 * i + 7] = dec_pair<7>(wq, w10, d2);
+                    }
+                    if (sc >= kA && !warp_wait(&a_empty[sa], (uint32_t) ((sc / kA - 1) & 1))) {
                         ok = false;
                         break;
                     }
-                    const int boff = (ks - q * kQS) * 18;
-#pragma unroll
-                    for (int m = 0; m < NMAT; m++) {
-                        uint8_t* at = sA + ((size_t) st * NMAT + m) * kAMat;
-                        const uint8_t* rm = raw + m * kRawMat;
-#pragma unroll
-                        for (int i = 0; i < 16 / kTcDecWarps; i++) {
-                            const int r = (2 * dw + i) * 8 + (lane & 7);
-                            const uint8_t* blk = rm + r * 144 + boff;
-                            const uint16_t* cw = reinterpret_cast<const uint16_t*>(blk + 2 + 4 * j4);
-                            const uint32_t w = (uint32_t) cw[0] | ((uint32_t) cw[1] << 16);
-                            const uint32_t w10 = w >> 10;
-                            const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
-                            uint8_t* dst = at + (2 * j4) * 128 + (r >> 3) * 1024 + (r & 7) * 16;
-                            *reinterpret_cast<uint4*>(dst) =
-                                make_uint4(dec_pair<0>(w, w10, d2), dec_pair<1>(w, w10, d2), dec_pair<2>(w, w10, d2),
-                                           dec_pair<3>(w, w10, d2));
-                            *reinterpret_cast<uint4*>(dst + 128) =
-                                make_uint4(dec_pair<4>(w, w10, d2), dec_pair<5>(w, w10, d2), dec_pair<6>(w, w10, d2),
-                                           dec_pair<7>(w, w10, d2));
-                        }
-                    }
-                    fence_proxy_async();  // generic-proxy stores -> the tensor core's reads
+                    tc_fence_after();
+                    const uint32_t ta = tmem + ((uint32_t) (32 * q) << 16) + kAOff + (uint32_t) sa * kACols +
+                                        (uint32_t) m * (kTcK / 2) + (uint32_t) (8 * j0);
+                    tmem_st16(ta, col);
+                    if (NW == 4) tmem_st16(ta + 16, col + 16);
+                    tmem_wait_st();
+                    tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&a_full[st]);
-                    sc++;
+                    if (lane == 0) mbar_arrive(&a_full[sa]);
                 }
                 if (!ok) break;
                 __syncwarp();
@@ -358,9 +419,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
             }
         }
         if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
-    } else if (warp >= 4 + kTcDecWarps) {
+    } else if (warp >= kTcEpiWarp0) {
         // ---------------- epilogue: tensor memory -> h (gate/up) or the slot rows (down) ----------------
-        const int wq = warp & 3;  // tensor-memory lanes 32 wq .. 32 wq + 31
+        // Warp kTcEpiWarp0 + 4 hf + q reads tensor-memory lanes 32q..32q+31 (its rows) and the 8-token column
+        // groups hf, hf + 2, hf + 4, ...
+        const int wq = warp & 3;
+        const int hf = (warp - kTcEpiWarp0) >> 2;
+        // gate/up staging of this warp: g and u of its 32 rows for its tokens, [token][row]
+        float* sg = sStage + (size_t) (warp - kTcEpiWarp0) * 2 * 32 * (kTcChunk / 2);
+        float* su = sg + 32 * (kTcChunk / 2);
         bool ok = true;
         for (int j = 0; ok; j++) {
             const int id = (int) blockIdx.x + j * (int) gridDim.x;
@@ -368,15 +435,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
             const Entry en = work_entry(w, id / args.m_tiles);
             const int mt = id % args.m_tiles;
             const int npad = (en.n + 15) & ~15;
-            const int a = j & 1;
-            if (!warp_wait(&acc_full[a], (uint32_t) ((j / 2) & 1))) {
+            const int a = j % kAccBufs;
+            if (!warp_wait(&acc_full[a], (uint32_t) ((j / kAccBufs) & 1))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const uint32_t tbase = tmem + ((uint32_t) (32 * wq) << 16) + (uint32_t) a * kAccCols;
             const int row = mt * kTcM + 32 * wq + lane;  // this thread's output row
-            for (int c0 = 0; c0 < en.n; c0 += 8) {
+            // pass 1: accumulators (hi + lo columns) out of tensor memory
+            for (int c0 = 8 * hf, tt = 0; c0 < en.n; c0 += 16, tt += 8) {
                 uint32_t g8[8], gl8[8], u8[8], ul8[8];
                 tmem_ld8(tbase + (uint32_t) c0, g8);
                 tmem_ld8(tbase + (uint32_t) (npad + c0), gl8);
@@ -387,13 +455,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
-                    const int t = c0 + i;
-                    if (t >= en.n) break;  // uniform across the warp
-                    const int slot = en.beg + t;
+                    const float g = __fadd_rn(__uint_as_float(g8[i]), __uint_as_float(gl8[i]));
                     if (MODE == 0) {
-                        // SwiGLU, then the q8_1 rule over the warp's 32 rows (one block of h), stored as hi/lo
-                        const float h = silu_mul(__fadd_rn(__uint_as_float(g8[i]), __uint_as_float(gl8[i])),
-                                                 __fadd_rn(__uint_as_float(u8[i]), __uint_as_float(ul8[i])));
+                        sg[(tt + i) * 32 + lane] = g;
+                        su[(tt + i) * 32 + lane] = __fadd_rn(__uint_as_float(u8[i]), __uint_as_float(ul8[i]));
+                    } else if (c0 + i < en.n) {
+                        args.parts[(size_t) (en.beg + c0 + i) * args.n_out + row] = g;
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[a]);  // the MMA may overwrite the buffer from here on
+            if (MODE == 0) {
+                // pass 2: SwiGLU, then the q8_1 rule over the warp's 32 rows (one block of h), stored as hi/lo
+                const int col = (row & ~63) + tc_kpos(row & 63);
+                for (int c0 = 8 * hf, tt = 0; c0 < en.n; c0 += 16, tt += 8) {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int t = c0 + i;
+                        if (t >= en.n) break;  // uniform across the warp
+                        const int slot = en.beg + t;
+                        const float h = silu_mul(sg[(tt + i) * 32 + lane], su[(tt + i) * 32 + lane]);
                         float amax = fabsf(h);
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -401,21 +484,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                         if (fabsf(d) > 65504.f) d = copysignf(65504.f, d);
                         float qv = 0.f;
                         if (amax != 0.f) qv = fminf(fmaxf(roundf(__fdiv_rn(h, d)), -127.f), 127.f);
-                        const float v = __fmul_rn(qv, f16_to_f32(f16_bits(d)));
+                        const float v = __fmul_rn(qv, __half2float(__float2half_rn(d)));
                         const __half hi = __float2half_rn(v);
                         const __half lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
-                        const int col = (row & ~63) + tc_kpos(row & 63);
                         args.hh[(size_t) slot * args.n_out + col] = hi;
                         args.hh[((size_t) args.hh_rows + slot) * args.n_out + col] = lo;
-                    } else {
-                        args.parts[(size_t) slot * args.n_out + row] =
-                            __fadd_rn(__uint_as_float(g8[i]), __uint_as_float(gl8[i]));
                     }
                 }
+                __syncwarp();  // the staging area is rewritten by this warp's next item
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[a]);
         }
         if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
     }
@@ -423,7 +500,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        tmem_dealloc(tmem, Cfg::kTmemCols);
     }
 }
 
@@ -488,14 +565,9 @@ bool weight_map(CUtensorMap* m, const uint8_t* base, int64_t rows, int row_bytes
                     (uint64_t) row_bytes, 144, kTcM, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
-size_t tc_smem_bytes(int nmat) {
-    return (size_t) kTcAB * kBTile + (size_t) kTcAB * nmat * kAMat + (size_t) kTcRaw * nmat * kRawMat + 32 * 8 +
-           1024;
-}
-
 template <int MODE>
 cudaError_t launch_tc(const CUtensorMap* maps, const TcArgs& a, cudaStream_t s) {
-    const size_t smem = tc_smem_bytes(MODE == 0 ? 2 : 1);
+    const size_t smem = TcCfg<MODE>::smem;
     cudaError_t err =
         cudaFuncSetAttribute(tc_expert_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     if (err != cudaSuccess) return err;
@@ -522,12 +594,12 @@ cudaError_t launch_tc_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, 
     CUtensorMap maps[5];
     const bool ok = weight_map(&maps[0], gate.base, routed_rows, rb) && weight_map(&maps[1], up.base, routed_rows, rb) &&
                     weight_map(&maps[2], sgate.base ? sgate.base : gate.base, n_ff, rb) &&
-                    weight_map(&maps[3], sup.base ? sup.base : up.base, n_ff, rb) &&
-                    make_map(&maps[4], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, (uint64_t) n_embd, (uint64_t) 2 * T,
-                             (uint64_t) n_embd * 2, kTcK, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+                    weight_map(&maps[3], sup.base ? sup.base : up.base, n_ff, rb);
     if (!ok) return cudaErrorInvalidValue;
+    maps[4] = maps[0];  // gate/up gathers its activation rows with cp.async: no activation tensor map
     TcArgs a{};
     a.w = w;
+    a.act = xh;
     a.K = n_embd;
     a.m_tiles = n_ff / kTcM;
     a.act_rows = T;
@@ -550,6 +622,7 @@ cudaError_t launch_tc_down(Matrix down, Matrix sdown, Work w, int n_expert, cons
     if (!ok) return cudaErrorInvalidValue;
     TcArgs a{};
     a.w = w;
+    a.act = hh;
     a.K = n_ff;
     a.m_tiles = n_embd / kTcM;
     a.act_rows = R;
