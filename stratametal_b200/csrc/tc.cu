@@ -377,14 +377,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                 const int k_end = min(KS, (qq + 1) * kQS);
                 for (int ks = qq * kQS; ks < k_end; ks++, sc++) {
                     const int sa = sc % kA;
-                    const uint8_t* blk = rowp + (ks - qq * kQS) * 18;
+                    // the block's 18 bytes from aligned 4-byte words: rows are 144 B apart, so a block starts on a
+                    // 4-byte boundary for even b (d and the first code pair share a word) and 2 bytes past one
+                    // for odd b (d ends a word, the codes are aligned)
+                    const int b = ks - qq * kQS;
+                    const uint32_t* wp = reinterpret_cast<const uint32_t*>(rowp + ((b * 18) & ~3));
                     uint32_t wv[NW];
+                    uint16_t dbits;
+                    if ((b & 1) == 0) {
+                        uint32_t raw5[NW + 1];
 #pragma unroll
-                    for (int i = 0; i < NW; i++) {
-                        const uint16_t* cw = reinterpret_cast<const uint16_t*>(blk + 2 + 4 * (j0 + i));
-                        wv[i] = (uint32_t) cw[0] | ((uint32_t) cw[1] << 16);
+                        for (int i = 0; i <= NW; i++) raw5[i] = wp[j0 + i];
+                        dbits = (uint16_t) raw5[0];  // only meaningful when j0 == 0 (see below)
+#pragma unroll
+                        for (int i = 0; i < NW; i++) wv[i] = __funnelshift_r(raw5[i], raw5[i + 1], 16);
+                        if (j0 != 0) dbits = (uint16_t) wp[0];
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < NW; i++) wv[i] = wp[1 + j0 + i];
+                        dbits = (uint16_t) (wp[0] >> 16);
                     }
-                    const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const uint16_t*>(blk)));
+                    const __half2 d2 = __half2half2(__ushort_as_half(dbits));
                     uint32_t col[8 * NW];
 #pragma unroll
                     for (int i = 0; i < NW; i++) {
@@ -476,10 +489,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                         const int t = c0 + i;
                         if (t >= en.n) break;  // uniform across the warp
                         const int slot = en.beg + t;
-                        const float h = silu_mul(sg[(tt + i) * 32 + lane], su[(tt + i) * 32 + lane]);
-                        float amax = fabsf(h);
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                        // SwiGLU with the library expf (within 2 ulp; the dot products here already differ from
+                        // the reference in f32 summation order), block max by one warp reduction (the order of
+                        // non-negative floats is the order of their bit patterns)
+                        const float gg = sg[(tt + i) * 32 + lane];
+                        const float h = __fmul_rn(__fdiv_rn(gg, __fadd_rn(1.f, expf(-gg))), su[(tt + i) * 32 + lane]);
+                        const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(h))));
                         float d = __fdiv_rn(amax, 127.f);
                         if (fabsf(d) > 65504.f) d = copysignf(65504.f, d);
                         float qv = 0.f;
