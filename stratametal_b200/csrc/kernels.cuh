@@ -8,6 +8,7 @@
 namespace smoe {
 
 constexpr int kRouterTokTile = 16;  // tokens per CTA in the router GEMV (x staged as bf16: 16 x n_embd x 2 bytes)
+constexpr int kRouterGemmMinTokens = 64;  // above this the router logits use the tiled fp64 GEMM
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxK = 64;
 

@@ -13,6 +13,7 @@
 #include "kernels.cuh"
 #include "q8.cuh"
 
+#include <algorithm>
 #include <cfloat>
 
 namespace smoe {
@@ -120,6 +121,87 @@ __global__ void __launch_bounds__(256) bf16_gemv_kernel(const void* __restrict__
     }
 }
 
+// ------------------------------------------------------------------------------------------------
+// a1 + a2 for many tokens: the same products as tiles of a GEMM.  A CTA computes 64 rows x 64 tokens over
+// K chunks of 32: each chunk is staged once in shared memory already converted to fp64 (weights bf16 -> f64,
+// activations f32 -> bf16 RNE -> f64), and each thread accumulates a 4 x 4 register tile with DFMA.  The
+// next chunk is loaded into registers while the current one is multiplied.
+// ------------------------------------------------------------------------------------------------
+constexpr int kRgRows = 64, kRgToks = 64, kRgK = 32;
+
+__global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restrict__ x, const uint16_t* __restrict__ w,
+                                                          const uint16_t* __restrict__ extra, float* __restrict__ y,
+                                                          float* __restrict__ y_extra, int T, int H, int n_out) {
+    __shared__ __align__(16) double ws[kRgK][kRgRows];
+    __shared__ __align__(16) double xs[kRgK][kRgToks];
+    const int tid = threadIdx.x;
+    const int o0 = blockIdx.x * kRgRows, t0 = blockIdx.y * kRgToks;
+    const int n_rows = n_out + (extra ? 1 : 0);
+    // loader roles: thread tid stages 8 consecutive k of row (and token) tid >> 2, k offset (tid & 3) * 8
+    const int lr = tid >> 2, lk = (tid & 3) * 8;
+    const int wo = min(o0 + lr, n_rows - 1);
+    const uint16_t* wrow = wo < n_out ? w + (size_t) wo * H : extra;
+    const int xt = min(t0 + lr, T - 1);
+    const float* xrow = x + (size_t) xt * H;
+    uint4 wreg;
+    float4 xreg0, xreg1;
+    auto load = [&](int kc) {
+        wreg = __ldg(reinterpret_cast<const uint4*>(wrow + kc + lk));
+        xreg0 = __ldg(reinterpret_cast<const float4*>(xrow + kc + lk));
+        xreg1 = __ldg(reinterpret_cast<const float4*>(xrow + kc + lk + 4));
+    };
+    auto stage = [&]() {
+        const uint32_t wu[4] = {wreg.x, wreg.y, wreg.z, wreg.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            ws[lk + 2 * q][lr] = (double) __uint_as_float(wu[q] << 16);
+            ws[lk + 2 * q + 1][lr] = (double) __uint_as_float(wu[q] & 0xFFFF0000u);
+        }
+        const float xv[8] = {xreg0.x, xreg0.y, xreg0.z, xreg0.w, xreg1.x, xreg1.y, xreg1.z, xreg1.w};
+#pragma unroll
+        for (int q = 0; q < 8; q++) xs[lk + q][lr] = (double) bf16_round(xv[q]);
+    };
+    // compute roles: rows 4 ty .. 4 ty + 3, tokens 4 tx .. 4 tx + 3
+    const int ty = tid >> 4, tx = tid & 15;
+    double acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
+    load(0);
+    for (int kc = 0; kc < H; kc += kRgK) {
+        __syncthreads();  // the previous chunk is consumed
+        stage();
+        __syncthreads();
+        if (kc + kRgK < H) load(kc + kRgK);
+#pragma unroll 8
+        for (int k = 0; k < kRgK; k++) {
+            const double2 w01 = *reinterpret_cast<const double2*>(&ws[k][4 * ty]);
+            const double2 w23 = *reinterpret_cast<const double2*>(&ws[k][4 * ty + 2]);
+            const double2 x01 = *reinterpret_cast<const double2*>(&xs[k][4 * tx]);
+            const double2 x23 = *reinterpret_cast<const double2*>(&xs[k][4 * tx + 2]);
+            const double wv[4] = {w01.x, w01.y, w23.x, w23.y};
+            const double xv[4] = {x01.x, x01.y, x23.x, x23.y};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fma(wv[i], xv[j], acc[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int o = o0 + 4 * ty + i;
+        if (o >= n_rows) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int t = t0 + 4 * tx + j;
+            if (t >= T) continue;
+            if (o < n_out) y[(size_t) t * n_out + o] = (float) acc[i][j];
+            else y_extra[t] = (float) acc[i][j];
+        }
+    }
+}
+
 __global__ void quant_q8_1_kernel(const float* __restrict__ x, uint8_t* __restrict__ y, int64_t n_blocks) {
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t) gridDim.x * (blockDim.x >> 5);
@@ -161,10 +243,10 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const floa
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int route_blocks = (T + kTopkWarps - 1) / kTopkWarps;
     if ((int) blockIdx.x >= route_blocks) {
-        // the remaining CTAs write the q8_1 image of x: one 32-value block per warp
-        const int nb = H / 32;
-        const int64_t q = (int64_t) (blockIdx.x - route_blocks) * kTopkWarps + warp;
-        if (q < (int64_t) T * nb) {
+        // the remaining CTAs write the q8_1 image of x: one 32-value block per warp, grid-stride
+        const int64_t nq = (int64_t) T * (H / 32);
+        const int64_t stride = (int64_t) (gridDim.x - route_blocks) * kTopkWarps;
+        for (int64_t q = (int64_t) (blockIdx.x - route_blocks) * kTopkWarps + warp; q < nq; q += stride) {
             const float xi = x[q * 32 + lane];
             quant_q8_1_warp(xi, xq + q * kQ8Block, lane);
             if (xa.base) quant_ka_warp(xi, xa.base + q * kKaBlock, lane, xa_q2 != 0);
@@ -248,6 +330,11 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const floa
 cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, const uint16_t* extra, float* y,
                              float* y_extra, int T, int H, int n_out, cudaStream_t s) {
     const int n_rows = n_out + (extra ? 1 : 0);
+    if (f32_in && T > kRouterGemmMinTokens && H % kRgK == 0) {
+        const dim3 grid((n_rows + kRgRows - 1) / kRgRows, (T + kRgToks - 1) / kRgToks);
+        router_gemm_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(x), w, extra, y, y_extra, T, H, n_out);
+        return cudaGetLastError();
+    }
     const size_t smem = (size_t) kRouterTokTile * H * 2;
     // few tokens: one row per warp spreads the weight stream over more SMs; many tokens: two rows per warp
     // reuse each staged token twice while 8 warps per CTA keep the fp64 pipe fed
@@ -275,7 +362,7 @@ cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, cons
 cudaError_t launch_router_topk(const float* logits, int T, int E, int k, int32_t* ids, float* w, const float* x,
                                uint8_t* xq, int H, cudaStream_t s, const KAct* xa, int xa_q2) {
     int blocks = (T + kTopkWarps - 1) / kTopkWarps;
-    if (xq) blocks += (int) (((int64_t) T * (H / 32) + kTopkWarps - 1) / kTopkWarps);
+    if (xq) blocks += (int) std::min<int64_t>(((int64_t) T * (H / 32) + kTopkWarps - 1) / kTopkWarps, 148 * 8);
     const KAct a = xa ? *xa : KAct{};
     if (E <= 256) router_topk_kernel<8><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);
     else if (E <= 512) router_topk_kernel<16><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);

@@ -99,21 +99,22 @@ def test_router_zero_tokens_leaves_outputs(cuda):
     assert ids.cpu().tolist() == [7, 7, 7, 7]
 
 
-def test_router_fused_logits_bitwise(cuda):
+@pytest.mark.parametrize("T", [33, 200])  # 200 tokens take the tiled fp64 GEMM (partial tiles included)
+def test_router_fused_logits_bitwise(cuda, T):
     from stratametal_b200 import synth
     sp = synth.LayerSpec(n_embd=2048, n_ff=64, n_expert=512, k=10, seed=8)
     lay = synth.make_layer(sp, 0, cuda)
-    x = synth.make_x(5, 33, 2048, cuda)
+    x = synth.make_x(5, T, 2048, cuda)
     wr = lay["ffn_gate_inp.weight"]
-    logits = torch.empty(33, 512, device=cuda)
-    ids = torch.empty(33, 10, dtype=torch.int32, device=cuda)
-    w = torch.empty(33, 10, device=cuda)
-    api.router(x, wr, 33, 2048, 512, 10, logits, ids, w)
+    logits = torch.empty(T, 512, device=cuda)
+    ids = torch.empty(T, 10, dtype=torch.int32, device=cuda)
+    w = torch.empty(T, 10, device=cuda)
+    api.router(x, wr, T, 2048, 512, 10, logits, ids, w)
     xh = x.cpu().numpy()
     wh = wr.cpu().numpy().view(np.uint16)
     L = O.lib()
-    lg_ref = np.empty((33, 512), np.float32)
-    for t in range(33):
+    lg_ref = np.empty((T, 512), np.float32)
+    for t in range(T):
         xr = np.array([L.orc_bf16_from_f32(float(v)) for v in xh[t]], np.uint16)
         xr = (xr.astype(np.uint32) << 16).view(np.float32)
         for e in range(512):
