@@ -46,6 +46,7 @@ size_t up256(size_t n) { return (n + 255) & ~(size_t) 255; }
 struct Layout {
     size_t xq, xa, xa2, logits, sh_logit, ids, w, slot, slot_token, tables, sched, gu, ha, parts;
     size_t sched_tc, xh, hh;  // the tensor-core path (0 bytes when the layer does not qualify)
+    size_t chunk;             // per-(64-token chunk, expert) counts of the many-CTA grouping
     size_t total;
 };
 
@@ -87,6 +88,7 @@ Layout layout_of(const smoe_layer* L, int T) {
     o.gu = at; at += up256(rows * 2 * F * 4);
     o.ha = at; at += up256(ka_bytes((int64_t) rows, (int) (F / 32)));
     o.parts = at; at += up256(rows * H * 4);
+    o.chunk = at; at += group_chunk_bytes(T, (int) E);
     o.sched_tc = o.xh = o.hh = at;
     if (tc_qualifies(L)) {
         o.sched_tc = at; at += sched_bytes((int) E, T, (int) K, kTcChunk);
@@ -353,7 +355,7 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     if (e == cudaSuccess) e = mark(1, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: top-k");
     const Sched sct = tc ? sched_at(base + lo.sched_tc, E, T, K, kTcChunk) : sc;
-    e = launch_group(ids, T, K, E, tabs, slot, slot_tok, s, &sct);
+    e = launch_group(ids, T, K, E, tabs, slot, slot_tok, s, &sct, reinterpret_cast<int32_t*>(base + lo.chunk));
     if (e == cudaSuccess) e = mark(2, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: dispatch");
 

@@ -71,6 +71,63 @@ __device__ __forceinline__ int block_excl_scan(int v, int* warp_sums, int* total
     return before + x - v;
 }
 
+// The work list from the grouping tables (one CTA of 1024 threads, thread e = expert e): experts bucketed by
+// min(count, 63), heaviest bucket first, ascending id inside a bucket (per-warp bucket counts, scanned
+// bucket-major then warp-minor, plus the rank among same-bucket lanes), then each expert cut into chunks of at
+// most sched.chunk slots.
+__device__ void build_sched(GroupTables g, Sched sched, int E, int* warp_sums) {
+    __shared__ int whist[32][64];
+    __shared__ int bucket_off[64];
+    __shared__ int sorted[kMaxExperts];
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    for (int i = tid; i < 32 * 64; i += blockDim.x) whist[i / 64][i % 64] = 0;
+    __syncthreads();
+    const int e = tid;
+    const int cnt = e < E ? g.counts[e] : 0;
+    const int b = cnt > 0 ? 63 - min(cnt, 63) : -1;
+    if (b >= 0) atomicAdd(&whist[warp][b], 1);
+    __syncthreads();
+    if (tid < 64) {
+        int acc = 0;
+        for (int w = 0; w < 32; w++) {
+            const int t = whist[w][tid];
+            whist[w][tid] = acc;
+            acc += t;
+        }
+        bucket_off[tid] = acc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int off = 0;
+        for (int i = 0; i < 64; i++) {
+            const int t = bucket_off[i];
+            bucket_off[i] = off;
+            off += t;
+        }
+    }
+    __syncthreads();
+    const uint32_t same = __match_any_sync(0xffffffffu, b);
+    if (b >= 0) sorted[bucket_off[b] + whist[warp][b] + __popc(same & lanemask_lt())] = e;
+    __syncthreads();
+    const int n_active = g.n_active[0];
+    const int ej = tid < n_active ? sorted[tid] : -1;
+    const int cj = ej >= 0 ? g.counts[ej] : 0;
+    const int chunk = sched.chunk;
+    const int nch = (cj + chunk - 1) / chunk;
+    int total = 0;
+    const int off = block_excl_scan(nch, warp_sums, &total);
+    if (ej >= 0) {
+        const int base = g.offsets[ej];
+        for (int c = 0; c < nch; c++) {
+            sched.e[off + c] = ej;
+            sched.beg[off + c] = base + c * chunk;
+            sched.n[off + c] = min(chunk, cj - c * chunk);
+        }
+    }
+    if (tid == 0) sched.count[0] = total;
+}
+
 __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__ ids, int T, int k, int E,
                                                      GroupTables g, int32_t* __restrict__ slot,
                                                      int32_t* __restrict__ src, Sched sched, int with_sched) {
@@ -138,64 +195,96 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__
             __syncthreads();
         }
     }
-    if (!with_sched) return;
-
-    // The work list: experts bucketed by min(count, 63), heaviest bucket first, ascending id inside a bucket
-    // (per-warp bucket counts, scanned bucket-major then warp-minor, plus the rank among same-bucket lanes),
-    // then each expert cut into chunks of at most sched.chunk slots.
-    __shared__ int whist[32][64];
-    __shared__ int bucket_off[64];
-    __shared__ int sorted[kMaxExperts];
-    const int warp = tid >> 5;
-    for (int i = tid; i < 32 * 64; i += blockDim.x) whist[i / 64][i % 64] = 0;
-    __syncthreads();
-    const int e = tid;
-    const int cnt = e < E ? g.counts[e] : 0;
-    const int b = cnt > 0 ? 63 - min(cnt, 63) : -1;
-    if (b >= 0) atomicAdd(&whist[warp][b], 1);
-    __syncthreads();
-    if (tid < 64) {
-        int acc = 0;
-        for (int w = 0; w < 32; w++) {
-            const int t = whist[w][tid];
-            whist[w][tid] = acc;
-            acc += t;
-        }
-        bucket_off[tid] = acc;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        int off = 0;
-        for (int i = 0; i < 64; i++) {
-            const int t = bucket_off[i];
-            bucket_off[i] = off;
-            off += t;
-        }
-    }
-    __syncthreads();
-    const uint32_t same = __match_any_sync(0xffffffffu, b);
-    if (b >= 0) sorted[bucket_off[b] + whist[warp][b] + __popc(same & lanemask_lt())] = e;
-    __syncthreads();
-    const int n_active = g.n_active[0];
-    const int ej = tid < n_active ? sorted[tid] : -1;
-    const int cj = ej >= 0 ? g.counts[ej] : 0;
-    const int chunk = sched.chunk;
-    const int nch = (cj + chunk - 1) / chunk;
-    int total = 0;
-    const int off = block_excl_scan(nch, warp_sums, &total);
-    if (ej >= 0) {
-        const int base = g.offsets[ej];
-        for (int c = 0; c < nch; c++) {
-            sched.e[off + c] = ej;
-            sched.beg[off + c] = base + c * chunk;
-            sched.n[off + c] = min(chunk, cj - c * chunk);
-        }
-    }
-    if (tid == 0) sched.count[0] = total;
+    if (with_sched) build_sched(g, sched, E, warp_sums);
 }
 
+// ------------------------------------------------------------------------------------------------
+// The same grouping for many tokens, over CTAs of 64-token chunks: (1) per-chunk expert counts, (2) one CTA
+// turns them into per-(chunk, expert) base slots, the tables and the work list, (3) each chunk places its pairs
+// at base + rank among the chunk's pairs of that expert (token order).  The slots equal group_kernel's.
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) group_count_kernel(const int32_t* __restrict__ ids, int T, int k, int E,
+                                                          int32_t* __restrict__ cc) {
+    __shared__ int cnt[kMaxExperts];
+    const int c = blockIdx.x, t0 = c * 64, nt = min(64, T - t0);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int p = threadIdx.x; p < nt * k; p += blockDim.x) {
+        const int e = ids[(size_t) t0 * k + p];
+        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cc[(size_t) c * E + e] = cnt[e];
+}
+
+__global__ void __launch_bounds__(1024) group_scan_kernel(int E, int nchunks, int32_t* __restrict__ cc,
+                                                          GroupTables g, Sched sched, int with_sched) {
+    __shared__ int warp_sums[32];
+    const int e = threadIdx.x;
+    int run = 0;
+    if (e < E)
+        for (int c = 0; c < nchunks; c++) {
+            const int v = cc[(size_t) c * E + e];
+            cc[(size_t) c * E + e] = run;
+            run += v;
+        }
+    const int cnt = e < E ? run : 0;
+    int tot, tot_act;
+    const int off = block_excl_scan(cnt, warp_sums, &tot);
+    const int act = block_excl_scan(cnt > 0 ? 1 : 0, warp_sums, &tot_act);
+    if (e < E) {
+        g.counts[e] = cnt;
+        g.offsets[e] = off;
+        if (cnt > 0) g.active[act] = e;
+        for (int c = 0; c < nchunks; c++) cc[(size_t) c * E + e] += off;
+    }
+    if (e == 0) {
+        g.offsets[E] = tot;
+        g.n_active[0] = tot_act;
+        g.work[0] = g.work[1] = g.work[2] = g.work[3] = 0;
+    }
+    __syncthreads();
+    if (with_sched) build_sched(g, sched, E, warp_sums);
+}
+
+__global__ void __launch_bounds__(256) group_assign_kernel(const int32_t* __restrict__ ids, int T, int k, int E,
+                                                           const int32_t* __restrict__ cc, int32_t* __restrict__ slot,
+                                                           int32_t* __restrict__ src) {
+    __shared__ unsigned long long mask[kMaxExperts];
+    const int c = blockIdx.x, t0 = c * 64, nt = min(64, T - t0);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) mask[e] = 0ull;
+    __syncthreads();
+    for (int p = threadIdx.x; p < nt * k; p += blockDim.x) {
+        const int e = ids[(size_t) t0 * k + p];
+        if (e >= 0 && e < E) atomicOr(&mask[e], 1ull << (p / k));
+    }
+    __syncthreads();
+    for (int p = threadIdx.x; p < nt * k; p += blockDim.x) {
+        const int tl = p / k;
+        const size_t i = (size_t) t0 * k + p;
+        const int e = ids[i];
+        if (e < 0 || e >= E) {
+            slot[i] = -1;
+            atomicOr(&g_smoe_status, kDevBadId);
+            continue;
+        }
+        const int pos = cc[(size_t) c * E + e] + __popcll(mask[e] & ((1ull << tl) - 1ull));
+        slot[i] = pos;
+        if (src) src[pos] = t0 + tl;
+    }
+}
+
+size_t group_chunk_bytes(int T, int E) { return (((size_t) (T + 63) / 64) * E * 4 + 255) & ~(size_t) 255; }
+
 cudaError_t launch_group(const int32_t* ids, int T, int k, int E, GroupTables g, int32_t* slot, int32_t* src,
-                         cudaStream_t s, const Sched* sched) {
+                         cudaStream_t s, const Sched* sched, int32_t* chunk_counts) {
+    if (chunk_counts && T > kGroupWideMinTokens) {
+        const int nchunks = (T + 63) / 64;
+        group_count_kernel<<<nchunks, 256, 0, s>>>(ids, T, k, E, chunk_counts);
+        group_scan_kernel<<<1, 1024, 0, s>>>(E, nchunks, chunk_counts, g, sched ? *sched : Sched{}, sched ? 1 : 0);
+        group_assign_kernel<<<nchunks, 256, 0, s>>>(ids, T, k, E, chunk_counts, slot, src);
+        return cudaGetLastError();
+    }
     group_kernel<<<1, 1024, 0, s>>>(ids, T, k, E, g, slot, src, sched ? *sched : Sched{}, sched ? 1 : 0);
     return cudaGetLastError();
 }

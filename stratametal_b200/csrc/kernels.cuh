@@ -68,8 +68,12 @@ size_t sched_bytes(int E, int T, int k, int chunk = kChunk);
 Sched sched_at(void* base, int E, int T, int k, int chunk = kChunk);
 
 // `sched` may be null (the stage entry points): then only the grouping tables are written.
+// With chunk_counts (group_chunk_bytes(T, E) of scratch) and more than kGroupWideMinTokens tokens the grouping
+// runs over many CTAs (three launches) instead of one; the result is the same.
+constexpr int kGroupWideMinTokens = 256;
+size_t group_chunk_bytes(int T, int E);
 cudaError_t launch_group(const int32_t* ids, int T, int k, int E, GroupTables g, int32_t* slot, int32_t* src,
-                         cudaStream_t s, const Sched* sched = nullptr);
+                         cudaStream_t s, const Sched* sched = nullptr, int32_t* chunk_counts = nullptr);
 
 
 // ---- expert.cu ----

@@ -122,70 +122,81 @@ __global__ void __launch_bounds__(256) bf16_gemv_kernel(const void* __restrict__
 }
 
 // ------------------------------------------------------------------------------------------------
-// a1 + a2 for many tokens: the same products as tiles of a GEMM.  A CTA computes 64 rows x 64 tokens over
+// a1 + a2 for many tokens: the same products as tiles of a GEMM.  A CTA computes 64 rows x 128 tokens over
 // K chunks of 32: each chunk is staged once in shared memory already converted to fp64 (weights bf16 -> f64,
-// activations f32 -> bf16 RNE -> f64), and each thread accumulates a 4 x 4 register tile with DFMA.  The
-// next chunk is loaded into registers while the current one is multiplied.
+// activations f32 -> bf16 RNE -> f64), and each thread accumulates a 4-row x 8-token register tile with DFMA.
+// Thread (ty, tx) owns rows 4ty..4ty+3 and tokens 2tx, 2tx+1 (+32, +64, +96), so a warp's activation reads
+// are 256 contiguous bytes per 16-byte load and its weight reads are broadcasts; the staging stores run along
+// rows (tokens), so they are contiguous too.  The next chunk is loaded into registers while the current one
+// is multiplied.
 // ------------------------------------------------------------------------------------------------
-constexpr int kRgRows = 64, kRgToks = 64, kRgK = 32;
+constexpr int kRgRows = 64, kRgToks = 128, kRgK = 32;
 
-__global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restrict__ x, const uint16_t* __restrict__ w,
+__global__ void __launch_bounds__(256, 2) router_gemm_kernel(const float* __restrict__ x, const uint16_t* __restrict__ w,
                                                           const uint16_t* __restrict__ extra, float* __restrict__ y,
                                                           float* __restrict__ y_extra, int T, int H, int n_out) {
-    __shared__ __align__(16) double ws[kRgK][kRgRows];
-    __shared__ __align__(16) double xs[kRgK][kRgToks];
+    __shared__ __align__(16) double ws[kRgK][kRgRows];   // 16 KB
+    __shared__ __align__(16) double xs[kRgK][kRgToks];   // 32 KB
     const int tid = threadIdx.x;
     const int o0 = blockIdx.x * kRgRows, t0 = blockIdx.y * kRgToks;
     const int n_rows = n_out + (extra ? 1 : 0);
-    // loader roles: thread tid stages 8 consecutive k of row (and token) tid >> 2, k offset (tid & 3) * 8
-    const int lr = tid >> 2, lk = (tid & 3) * 8;
-    const int wo = min(o0 + lr, n_rows - 1);
-    const uint16_t* wrow = wo < n_out ? w + (size_t) wo * H : extra;
-    const int xt = min(t0 + lr, T - 1);
-    const float* xrow = x + (size_t) xt * H;
+    // loaders: weights, thread -> row tid % 64, k segment (tid / 64) * 8; activations, thread -> token tid % 128,
+    // k segment (tid / 128) * 16
+    const int wr = tid & 63, wk = (tid >> 6) * 8;
+    const int wo = min(o0 + wr, n_rows - 1);
+    const uint16_t* wrow = (wo < n_out ? w + (size_t) wo * H : extra) + wk;
+    const int xr = tid & 127, xk = (tid >> 7) * 16;
+    const float* xrow = x + (size_t) min(t0 + xr, T - 1) * H + xk;
     uint4 wreg;
-    float4 xreg0, xreg1;
+    float4 xreg[4];
     auto load = [&](int kc) {
-        wreg = __ldg(reinterpret_cast<const uint4*>(wrow + kc + lk));
-        xreg0 = __ldg(reinterpret_cast<const float4*>(xrow + kc + lk));
-        xreg1 = __ldg(reinterpret_cast<const float4*>(xrow + kc + lk + 4));
+        wreg = __ldg(reinterpret_cast<const uint4*>(wrow + kc));
+#pragma unroll
+        for (int q = 0; q < 4; q++) xreg[q] = __ldg(reinterpret_cast<const float4*>(xrow + kc) + q);
     };
     auto stage = [&]() {
         const uint32_t wu[4] = {wreg.x, wreg.y, wreg.z, wreg.w};
 #pragma unroll
         for (int q = 0; q < 4; q++) {
-            ws[lk + 2 * q][lr] = (double) __uint_as_float(wu[q] << 16);
-            ws[lk + 2 * q + 1][lr] = (double) __uint_as_float(wu[q] & 0xFFFF0000u);
+            ws[wk + 2 * q][wr] = (double) __uint_as_float(wu[q] << 16);
+            ws[wk + 2 * q + 1][wr] = (double) __uint_as_float(wu[q] & 0xFFFF0000u);
         }
-        const float xv[8] = {xreg0.x, xreg0.y, xreg0.z, xreg0.w, xreg1.x, xreg1.y, xreg1.z, xreg1.w};
 #pragma unroll
-        for (int q = 0; q < 8; q++) xs[lk + q][lr] = (double) bf16_round(xv[q]);
+        for (int q = 0; q < 4; q++) {
+            xs[xk + 4 * q + 0][xr] = (double) bf16_round(xreg[q].x);
+            xs[xk + 4 * q + 1][xr] = (double) bf16_round(xreg[q].y);
+            xs[xk + 4 * q + 2][xr] = (double) bf16_round(xreg[q].z);
+            xs[xk + 4 * q + 3][xr] = (double) bf16_round(xreg[q].w);
+        }
     };
-    // compute roles: rows 4 ty .. 4 ty + 3, tokens 4 tx .. 4 tx + 3
     const int ty = tid >> 4, tx = tid & 15;
-    double acc[4][4];
+    double acc[4][8];
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.0;
     load(0);
     for (int kc = 0; kc < H; kc += kRgK) {
         __syncthreads();  // the previous chunk is consumed
         stage();
         __syncthreads();
         if (kc + kRgK < H) load(kc + kRgK);
-#pragma unroll 8
+#pragma unroll 4
         for (int k = 0; k < kRgK; k++) {
             const double2 w01 = *reinterpret_cast<const double2*>(&ws[k][4 * ty]);
             const double2 w23 = *reinterpret_cast<const double2*>(&ws[k][4 * ty + 2]);
-            const double2 x01 = *reinterpret_cast<const double2*>(&xs[k][4 * tx]);
-            const double2 x23 = *reinterpret_cast<const double2*>(&xs[k][4 * tx + 2]);
+            double xv[8];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const double2 v = *reinterpret_cast<const double2*>(&xs[k][32 * q + 2 * tx]);
+                xv[2 * q] = v.x;
+                xv[2 * q + 1] = v.y;
+            }
             const double wv[4] = {w01.x, w01.y, w23.x, w23.y};
-            const double xv[4] = {x01.x, x01.y, x23.x, x23.y};
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int j = 0; j < 4; j++) acc[i][j] = fma(wv[i], xv[j], acc[i][j]);
+                for (int j = 0; j < 8; j++) acc[i][j] = fma(wv[i], xv[j], acc[i][j]);
         }
     }
 #pragma unroll
@@ -193,8 +204,8 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restric
         const int o = o0 + 4 * ty + i;
         if (o >= n_rows) continue;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int t = t0 + 4 * tx + j;
+        for (int j = 0; j < 8; j++) {
+            const int t = t0 + 32 * (j >> 1) + 2 * tx + (j & 1);
             if (t >= T) continue;
             if (o < n_out) y[(size_t) t * n_out + o] = (float) acc[i][j];
             else y_extra[t] = (float) acc[i][j];

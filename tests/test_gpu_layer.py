@@ -116,3 +116,13 @@ def test_zero_tokens_is_a_no_op(cuda):
     m.forward(torch.zeros(0, 256, device=cuda), out[:0])
     torch.cuda.synchronize()
     assert torch.all(out == 7.0)
+
+
+def test_many_tokens_wide_grouping(cuda):
+    # 600 tokens: the grouping runs over 64-token chunks on many CTAs; the SIMT experts keep the q8_1 contract,
+    # so every stage is held to the single-CTA bar
+    spec = synth.LayerSpec(n_embd=512, n_ff=128, n_expert=64, k=6, seed=21)
+    got, want, tr, otr, hl, x = run_case(cuda, spec, 600)
+    assert np.array_equal(tr.ids.cpu().numpy(), otr["ids"])
+    assert O.rel_l1(otr["parts"], tr.parts.cpu().numpy()) <= 1e-5
+    assert O.rel_l1(want, got) <= 1e-5
