@@ -349,7 +349,11 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     if (e == cudaSuccess) e = mark(0, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: router");
     const bool tc = use_tc(L, T);
-    e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, tc ? nullptr : &xa, L->gu_type == kQ2_0);
+    // the q8_1 image of x in the reference's block format is only an output of the trace: the expert kernels
+    // read their own layouts (xa for the SIMT kernels, xh for the tensor-core kernels)
+    const bool want_xq = trace && trace->xq;
+    e = launch_router_topk(logits, T, E, K, ids, w, x, want_xq ? xq : nullptr, H, s, tc ? nullptr : &xa,
+                           L->gu_type == kQ2_0);
     __half* xh = reinterpret_cast<__half*>(base + lo.xh);
     if (e == cudaSuccess && tc) e = launch_quant_xh(x, T, H, xh, s);
     if (e == cudaSuccess) e = mark(1, s);

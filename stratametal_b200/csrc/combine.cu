@@ -38,6 +38,54 @@ __global__ void combine_kernel(const float* __restrict__ parts, const int32_t* _
     out[(int64_t) t * H + j] = (float) acc;
 }
 
+// The same sum, four outputs per thread with 16-byte loads (H a multiple of 4, 16-byte aligned rows); the token's
+// slots and weights are read once per CTA.
+__global__ void combine4_kernel(const float* __restrict__ parts, const int32_t* __restrict__ slot,
+                                const float* __restrict__ w, const float* __restrict__ shared,
+                                const float* __restrict__ shared_logit, float* __restrict__ out,
+                                float* __restrict__ shared_out, int64_t H, int k, int64_t shared_stride) {
+    __shared__ int64_t s_row[kMaxK];
+    __shared__ double s_w[kMaxK];
+    const int t = blockIdx.y;
+    for (int i = threadIdx.x; i < k; i += blockDim.x) {
+        const int64_t pi = (int64_t) t * k + i;
+        const int64_t sl = slot ? (int64_t) slot[pi] : pi;
+        s_row[i] = sl;  // an id outside the pool (slot -1, recorded by the dispatch) contributes nothing
+        s_w[i] = (double) w[pi];
+    }
+    __syncthreads();
+    const int64_t j = 4 * ((int64_t) blockIdx.x * blockDim.x + threadIdx.x);
+    if (j >= H) return;
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    for (int i = 0; i < k; i++) {
+        const int64_t sl = s_row[i];
+        if (sl < 0) continue;
+        const float4 p = __ldg(reinterpret_cast<const float4*>(parts + sl * H + j));
+        const double wi = s_w[i];
+        a0 += wi * (double) p.x;
+        a1 += wi * (double) p.y;
+        a2 += wi * (double) p.z;
+        a3 += wi * (double) p.w;
+    }
+    if (shared) {
+        float4 sh = *reinterpret_cast<const float4*>(shared + (int64_t) t * shared_stride + j);
+        if (shared_logit) {
+            const float e = (float) exp(-(double) shared_logit[t]);
+            const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+            sh.x = __fmul_rn(sh.x, sig);
+            sh.y = __fmul_rn(sh.y, sig);
+            sh.z = __fmul_rn(sh.z, sig);
+            sh.w = __fmul_rn(sh.w, sig);
+        }
+        if (shared_out) *reinterpret_cast<float4*>(shared_out + (int64_t) t * H + j) = sh;
+        a0 += (double) sh.x;
+        a1 += (double) sh.y;
+        a2 += (double) sh.z;
+        a3 += (double) sh.w;
+    }
+    *reinterpret_cast<float4*>(out + (int64_t) t * H + j) = make_float4((float) a0, (float) a1, (float) a2, (float) a3);
+}
+
 __global__ void gather_parts_kernel(const float* __restrict__ parts, const int32_t* __restrict__ slot,
                                     float* __restrict__ dst, int64_t H, int k) {
     const int ti = blockIdx.y;  // t * k + i
@@ -50,6 +98,15 @@ __global__ void gather_parts_kernel(const float* __restrict__ parts, const int32
 cudaError_t launch_combine(const float* parts, const int32_t* slot, const float* w, const float* shared,
                            const float* shared_logit, float* out, float* shared_out, int64_t H, int k, int T,
                            int64_t shared_stride, cudaStream_t s) {
+    const bool vec = T >= 128 && H % 4 == 0 && shared_stride % 4 == 0 && k <= kMaxK &&
+                     (reinterpret_cast<uintptr_t>(parts) | reinterpret_cast<uintptr_t>(out) |
+                      reinterpret_cast<uintptr_t>(shared) | reinterpret_cast<uintptr_t>(shared_out)) % 16 == 0;
+    if (vec) {
+        const dim3 grid((unsigned) ((H / 4 + 255) / 256), (unsigned) T);
+        combine4_kernel<<<grid, 256, 0, s>>>(parts, slot, w, shared, shared_logit, out, shared_out, H, k,
+                                             shared_stride);
+        return cudaGetLastError();
+    }
     const dim3 grid((unsigned) ((H + 255) / 256), (unsigned) T);
     combine_kernel<<<grid, 256, 0, s>>>(parts, slot, w, shared, shared_logit, out, shared_out, H, k, shared_stride);
     return cudaGetLastError();

@@ -122,22 +122,28 @@ __global__ void __launch_bounds__(256) bf16_gemv_kernel(const void* __restrict__
 }
 
 // ------------------------------------------------------------------------------------------------
-// a1 + a2 for many tokens: the same products as tiles of a GEMM.  A CTA computes 64 rows x 128 tokens over
-// K chunks of 32: each chunk is staged once in shared memory already converted to fp64 (weights bf16 -> f64,
-// activations f32 -> bf16 RNE -> f64), and each thread accumulates a 4-row x 8-token register tile with DFMA.
-// Thread (ty, tx) owns rows 4ty..4ty+3 and tokens 2tx, 2tx+1 (+32, +64, +96), so a warp's activation reads
-// are 256 contiguous bytes per 16-byte load and its weight reads are broadcasts; the staging stores run along
-// rows (tokens), so they are contiguous too.  The next chunk is loaded into registers while the current one
-// is multiplied.
+// a1 + a2 for many tokens: the same products as tiles of a GEMM on the fp64 tensor path
+// (mma.sync.m8n8k4.f64: exact products, fp64 sums, like the DFMA form).  A CTA computes 64 rows x 128 tokens
+// over K chunks of 32, staged once in shared memory already converted to fp64 (weights bf16 -> f64,
+// activations f32 -> bf16 RNE -> f64); each of the 8 warps owns a 32-row x 32-token tile, 4 x 4 MMA tiles of
+// 8 x 8.  The rows of the staged tiles are padded by 8 doubles so a fragment load touches both bank halves.
+// The next chunk is loaded into registers while the current one is multiplied.
 // ------------------------------------------------------------------------------------------------
-constexpr int kRgRows = 64, kRgToks = 128, kRgK = 32;
+constexpr int kRgRows = 64, kRgToks = 128, kRgK = 32, kRgPad = 8;
 
-__global__ void __launch_bounds__(256, 2) router_gemm_kernel(const float* __restrict__ x, const uint16_t* __restrict__ w,
+__device__ __forceinline__ void dmma_8x8x4(double (&d)[2], double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(d[0]), "+d"(d[1])
+                 : "d"(a), "d"(b));
+}
+
+__global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restrict__ x, const uint16_t* __restrict__ w,
                                                           const uint16_t* __restrict__ extra, float* __restrict__ y,
                                                           float* __restrict__ y_extra, int T, int H, int n_out) {
-    __shared__ __align__(16) double ws[kRgK][kRgRows];   // 16 KB
-    __shared__ __align__(16) double xs[kRgK][kRgToks];   // 32 KB
-    const int tid = threadIdx.x;
+    extern __shared__ __align__(16) double rg_smem[];
+    double (*ws)[kRgRows + kRgPad] = reinterpret_cast<double (*)[kRgRows + kRgPad]>(rg_smem);
+    double (*xs)[kRgToks + kRgPad] = reinterpret_cast<double (*)[kRgToks + kRgPad]>(rg_smem + kRgK * (kRgRows + kRgPad));
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int o0 = blockIdx.x * kRgRows, t0 = blockIdx.y * kRgToks;
     const int n_rows = n_out + (extra ? 1 : 0);
     // loaders: weights, thread -> row tid % 64, k segment (tid / 64) * 8; activations, thread -> token tid % 128,
@@ -169,49 +175,51 @@ __global__ void __launch_bounds__(256, 2) router_gemm_kernel(const float* __rest
             xs[xk + 4 * q + 3][xr] = (double) bf16_round(xreg[q].w);
         }
     };
-    const int ty = tid >> 4, tx = tid & 15;
-    double acc[4][8];
+    // warp tile: rows 32 (warp & 1) .., tokens 32 (warp >> 1) ..; fragment roles gid = lane / 4, tig = lane % 4
+    const int wro = 32 * (warp & 1), wto = 32 * (warp >> 1);
+    const int gid = lane >> 2, tig = lane & 3;
+    double acc[4][4][2];
 #pragma unroll
     for (int i = 0; i < 4; i++)
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[i][j] = 0.0;
+        for (int j = 0; j < 4; j++) acc[i][j][0] = acc[i][j][1] = 0.0;
     load(0);
     for (int kc = 0; kc < H; kc += kRgK) {
         __syncthreads();  // the previous chunk is consumed
         stage();
         __syncthreads();
         if (kc + kRgK < H) load(kc + kRgK);
-#pragma unroll 4
-        for (int k = 0; k < kRgK; k++) {
-            const double2 w01 = *reinterpret_cast<const double2*>(&ws[k][4 * ty]);
-            const double2 w23 = *reinterpret_cast<const double2*>(&ws[k][4 * ty + 2]);
-            double xv[8];
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const double2 v = *reinterpret_cast<const double2*>(&xs[k][32 * q + 2 * tx]);
-                xv[2 * q] = v.x;
-                xv[2 * q + 1] = v.y;
-            }
-            const double wv[4] = {w01.x, w01.y, w23.x, w23.y};
+        for (int k = 0; k < kRgK; k += 4) {
+            double a[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) a[i] = ws[k + tig][wro + 8 * i + gid];   // A[row gid][k tig]
+#pragma unroll
+            for (int j = 0; j < 4; j++) bv[j] = xs[k + tig][wto + 8 * j + gid];  // B[k tig][token gid]
 #pragma unroll
             for (int i = 0; i < 4; i++)
 #pragma unroll
-                for (int j = 0; j < 8; j++) acc[i][j] = fma(wv[i], xv[j], acc[i][j]);
+                for (int j = 0; j < 4; j++) dmma_8x8x4(acc[i][j], a[i], bv[j]);
         }
     }
+    // D[row gid][token 2 tig + c]
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const int o = o0 + 4 * ty + i;
+        const int o = o0 + wro + 8 * i + gid;
         if (o >= n_rows) continue;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int t = t0 + 32 * (j >> 1) + 2 * tx + (j & 1);
-            if (t >= T) continue;
-            if (o < n_out) y[(size_t) t * n_out + o] = (float) acc[i][j];
-            else y_extra[t] = (float) acc[i][j];
-        }
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                const int t = t0 + wto + 8 * j + 2 * tig + c;
+                if (t >= T) continue;
+                if (o < n_out) y[(size_t) t * n_out + o] = (float) acc[i][j][c];
+                else y_extra[t] = (float) acc[i][j][c];
+            }
     }
 }
+
+constexpr size_t kRgSmem = (size_t) kRgK * (kRgRows + kRgPad + kRgToks + kRgPad) * sizeof(double);
 
 __global__ void quant_q8_1_kernel(const float* __restrict__ x, uint8_t* __restrict__ y, int64_t n_blocks) {
     const int lane = threadIdx.x & 31;
@@ -259,7 +267,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const floa
         const int64_t stride = (int64_t) (gridDim.x - route_blocks) * kTopkWarps;
         for (int64_t q = (int64_t) (blockIdx.x - route_blocks) * kTopkWarps + warp; q < nq; q += stride) {
             const float xi = x[q * 32 + lane];
-            quant_q8_1_warp(xi, xq + q * kQ8Block, lane);
+            if (xq) quant_q8_1_warp(xi, xq + q * kQ8Block, lane);
             if (xa.base) quant_ka_warp(xi, xa.base + q * kKaBlock, lane, xa_q2 != 0);
         }
         return;
@@ -343,7 +351,11 @@ cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, cons
     const int n_rows = n_out + (extra ? 1 : 0);
     if (f32_in && T > kRouterGemmMinTokens && H % kRgK == 0) {
         const dim3 grid((n_rows + kRgRows - 1) / kRgRows, (T + kRgToks - 1) / kRgToks);
-        router_gemm_kernel<<<grid, 256, 0, s>>>(static_cast<const float*>(x), w, extra, y, y_extra, T, H, n_out);
+        cudaError_t err = cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int) kRgSmem);
+        if (err != cudaSuccess) return err;
+        router_gemm_kernel<<<grid, 256, kRgSmem, s>>>(static_cast<const float*>(x), w, extra, y, y_extra, T, H,
+                                                      n_out);
         return cudaGetLastError();
     }
     const size_t smem = (size_t) kRouterTokTile * H * 2;
@@ -373,7 +385,7 @@ cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, cons
 cudaError_t launch_router_topk(const float* logits, int T, int E, int k, int32_t* ids, float* w, const float* x,
                                uint8_t* xq, int H, cudaStream_t s, const KAct* xa, int xa_q2) {
     int blocks = (T + kTopkWarps - 1) / kTopkWarps;
-    if (xq) blocks += (int) std::min<int64_t>(((int64_t) T * (H / 32) + kTopkWarps - 1) / kTopkWarps, 148 * 8);
+    if (xq || xa) blocks += (int) std::min<int64_t>(((int64_t) T * (H / 32) + kTopkWarps - 1) / kTopkWarps, 148 * 8);
     const KAct a = xa ? *xa : KAct{};
     if (E <= 256) router_topk_kernel<8><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);
     else if (E <= 512) router_topk_kernel<16><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);
