@@ -7,10 +7,16 @@ A step is one smoe_moe_forward over one batch: router, dispatch, expert products
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C]
 
-Timing: W untimed steps, then exactly K steps between CUDA events on the launching stream, bracketed by a
-barrier and a synchronize, max over ranks.  Each step's expert bytes (~200 MB) exceed the 126 MB L2 and the
-steps rotate over --layers distinct seeded layers, so weights stream from HBM.  Rank 0 prints one JSON line.
-N > 1 runs independent replicas (decode does not shard: "replicas only"), value = all ranks' tokens / time.
+Timing: each step's smoe_moe_forward calls are captured once as a CUDA graph (one graph per (layer, batch)
+forward; for configs[3] one graph for the whole 48-layer stack with its residual add + RMSNorm); W untimed
+replays, then exactly K replays between CUDA events on the replay stream, bracketed by a barrier and a
+synchronize, max over ranks.  Per-stage times come from a separate eager pass with stage events.  Each step's
+expert bytes (~200 MB at 64 tokens) exceed the 126 MB L2 and the steps rotate over --layers distinct seeded
+layers, so weights stream from HBM.  Rank 0 prints one JSON line.  N > 1 runs independent replicas (decode
+does not shard: "replicas only"), value = all ranks' tokens / time.
+
+  python bench.py --config 3 [--tokens 16]    # the 48-layer stack at batch 1 (or 16)
+  python bench.py --config 2                  # 4096-token prefill (tensor-core expert kernels)
 """
 from __future__ import annotations
 
@@ -26,6 +32,8 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+STACK_LAYERS = 48
+RMS_EPS = 1e-6
 METRIC = "MoE-layer tokens/s (decode b1/b64, prefill 4k); expert-weight HBM GB/s vs peak"
 UNIT = "tokens/s"
 STAGES = ["router_gemv", "router_topk_q8", "dispatch", "expert_gate_up", "expert_down", "combine"]
@@ -45,6 +53,7 @@ def parse():
     ap.add_argument("--expert-path", type=int, default=0, choices=[0, 1, 2],
                     help="0 automatic, 1 SIMT expert kernels, 2 tensor-core expert kernels")
     ap.add_argument("--layers", type=int, default=4, help="distinct layers rotated through the steps")
+    ap.add_argument("--tokens", type=int, default=0, help="override the config's tokens per step (configs[3]: 1 or 16)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -159,7 +168,9 @@ def cpu_layer_runner(lay):
     return (lambda x: O.moe_layer(hl, x, n_threads=threads)), "port", threads
 
 
-def cpu_baseline(lay, x_host, seconds: float):
+def cpu_baseline(lay, x_host, seconds: float, n_layers: int = 1):
+    """The reference's CPU path on this host: layer 0 on the step's tokens, repeated within the time budget.  For
+    the stack the per-layer time is multiplied by the layer count (every layer has the same shape)."""
     run, kind, threads = cpu_layer_runner(lay)
     T = x_host.shape[0]
     run(x_host[:1])
@@ -170,8 +181,11 @@ def cpu_baseline(lay, x_host, seconds: float):
         el = time.perf_counter() - t0
         if el > seconds or n >= 50:
             break
-    return {"value": n * T / el, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{n} full steps of the bench workload ({T} tokens each, layer 0), {el:.1f} s"}
+    per_step = el / n * n_layers
+    sample = f"{n} layer calls of the bench workload ({T} tokens each, layer 0), {el:.1f} s"
+    if n_layers > 1:
+        sample += f"; tokens/s for the stack = T / ({n_layers} x the per-layer time)"
+    return {"value": T / per_step, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample}
 
 
 # ---------------------------------------------------------------------------------------------------
@@ -208,7 +222,15 @@ def max_over_ranks(v: float, ws: int) -> float:
     return float(t.item())
 
 
-def config_dict(args, spec, T, D_mean):
+def config_dict(args, spec, T, D_mean, n_layers=None, stack=False):
+    if stack:
+        return {"workload": f"configs[3]: stack of {n_layers} MoE layers (residual add + RMSNorm between them), "
+                            f"{T} decode tokens/step",
+                "tokens_per_step": T, "layers": n_layers, "n_embd": spec.n_embd, "n_ff": spec.n_ff,
+                "n_expert": spec.n_expert, "top_k": spec.k, "expert_format": "Q2_0", "shared_expert": True,
+                "distinct_experts_per_layer": D_mean, "rms_eps": RMS_EPS,
+                "l2": "inputs larger than L2: one step streams every layer's routed experts (> 400 MB)",
+                "parallelism": f"replicas x{args.gpus}", "seed": spec.seed}
     return {"workload": f"configs[{args.config}]: one MoE layer, {T} {'decode' if T <= 64 else 'prefill'} tokens/step"
                         + (", Zipf(1.1) expert popularity" if spec.zipf else "")
                         + (", IQ2_S gate/up" if spec.gu_type == 22 else ""),
@@ -227,6 +249,9 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return
     spec, T = synth.config_spec(args.config)
+    if args.tokens:
+        T = args.tokens
+    stack = args.config == 3
     lay = synth.make_layer(spec, 0, "cpu")
     x = synth.make_x(spec.seed, T, spec.n_embd).numpy()
     run, kind, threads = cpu_layer_runner(lay)
@@ -244,10 +269,13 @@ def run_reference(args, ws, rank):
     el = time.perf_counter() - t0
     value = args.steps * s / el
     sample = f"{s} of the {T} tokens per step (layer 0 of configs[{args.config}]), {args.steps} steps, {el:.1f} s"
+    if stack:  # the stack's layers share one shape: tokens/s through all of them
+        value /= STACK_LAYERS
+        sample += f"; stack tokens/s = layer tokens/s / {STACK_LAYERS}"
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int2 dot, f32/f64 sums", "data": "synthetic",
-            "config": config_dict(args, spec, T, None), "impl": "reference",
+            "config": config_dict(args, spec, T, None, STACK_LAYERS, stack), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -265,126 +293,184 @@ def run_ours(args, ws, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_stream(torch.cuda.Stream(dev))  # the C ABI wants an explicit non-null stream
     spec, T = synth.config_spec(args.config)
+    if args.tokens:
+        T = args.tokens
+    H = spec.n_embd
+    stack = args.config == 3
+    n_layers = STACK_LAYERS if stack else args.layers
     api.set_expert_path(args.expert_path)
-    layers = [api.MoeLayer(synth.make_layer(spec, li, dev), T, dev) for li in range(args.layers)]
+    layers = [api.MoeLayer(synth.make_layer(spec, li, dev), T, dev) for li in range(n_layers)]
     tc = lib().smoe_expert_path_for(C.byref(layers[0].c), T) == 2
-    n_batches = 4
-    xs = [synth.make_x(spec.seed + 1000 * local, T, spec.n_embd, dev, stream=b) for b in range(n_batches)]
-    out = torch.empty(T, spec.n_embd, device=dev)
+    n_batches = 1 if stack else 4
+    xs = [synth.make_x(spec.seed + 1000 * local, T, H, dev, stream=b) for b in range(n_batches)]
+    out = torch.empty(T, H, device=dev)
     stream = torch.cuda.current_stream()
+    # the stack ping-pongs between two buffers: layer l reads cur, writes MoE(cur) to nxt, then
+    # nxt = rms_norm(nxt + cur)
+    sbuf = [torch.empty(T, H, device=dev) for _ in range(2)]
 
-    # distinct experts per (layer, batch), for the algorithmic bytes
+    def forward_once(li, b, dst):
+        layers[li].forward(xs[b], dst)
+
+    def stack_once():
+        cur = xs[0]
+        for li in range(n_layers):
+            nxt = sbuf[li & 1]
+            layers[li].forward(cur, nxt)
+            api.add_rms_norm(nxt, cur, None, T, H, RMS_EPS)
+            cur = nxt
+        return cur
+
+    # distinct experts per (layer, batch), for the algorithmic bytes (eager, with a trace)
     D = {}
+    cur = xs[0]
     for li, m in enumerate(layers):
-        for b, x in enumerate(xs):
+        for b in range(n_batches):
             tr = m.make_trace(T)
-            m.forward(x, out, tr)
+            xin = cur if stack else xs[b]
+            m.forward(xin, out, tr)
             D[(li, b)] = int(torch.unique(tr.ids).numel())
+            if stack:  # follow the stack's own activations
+                api.add_rms_norm(out, xin, None, T, H, RMS_EPS)
+                cur = out.clone()
     torch.cuda.synchronize()
     assert api.device_status() == 0
 
-    def step(i):
-        layers[i % args.layers].forward(xs[(i // args.layers) % n_batches], out)
+    # one CUDA graph per step kind: every (layer, batch) forward, or the whole stack
+    G = 1 if stack else n_layers * n_batches
+    graphs = []
+    for gi in range(G):
+        g = torch.cuda.CUDAGraph()
+        for _ in range(2):  # warm the allocator and any first-call set-up outside the capture
+            stack_once() if stack else forward_once(gi % n_layers, (gi // n_layers) % n_batches, out)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, capture_error_mode="relaxed"):
+            stack_once() if stack else forward_once(gi % n_layers, (gi // n_layers) % n_batches, out)
+        graphs.append(g)
+    torch.cuda.synchronize()
+    gstream = torch.cuda.current_stream()
 
     K, W = args.steps, args.warmup
     for i in range(W):
-        step(i)
-    # stage events for every timed step
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)] for _ in range(K)]
-    for row in ev:  # torch creates the CUDA event on its first record
-        for e in row:
-            e.record(stream)
-    handles = [(C.c_void_p * len(STAGES))(*[e.cuda_event for e in row[1:]]) for row in ev]
+        graphs[i % G].replay()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        start.record(stream)
+        start.record(gstream)
         for i in range(K):
-            ev[i][0].record(stream)
-            lib().smoe_set_stage_events(handles[i], len(STAGES))
-            step(i)
-        end.record(stream)
-        lib().smoe_set_stage_events(None, 0)
+            graphs[i % G].replay()
+        end.record(gstream)
         torch.cuda.synchronize()
     barrier(ws)
-    el_ms = start.elapsed_time(end)
-    el_ms = max_over_ranks(el_ms, ws)
+    el_ms = max_over_ranks(start.elapsed_time(end), ws)
     ms_step = el_ms / K
     value = ws * T / (ms_step * 1e-3)
-    # per-stage device time
-    stage_ms = {s: 0.0 for s in STAGES}
-    for i in range(K):
-        for j, s in enumerate(STAGES):
-            stage_ms[s] += ev[i][j].elapsed_time(ev[i][j + 1])
-    dominant = max(stage_ms, key=stage_ms.get)
+    assert api.device_status() == 0
+
+    # per-stage device time: an eager pass with stage events (single layers only)
+    stage_ms = None
+    if not stack:
+        Ks = min(K, 500)
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)] for _ in range(Ks)]
+        for row in ev:  # torch creates the CUDA event on its first record
+            for e in row:
+                e.record(stream)
+        handles = [(C.c_void_p * len(STAGES))(*[e.cuda_event for e in row[1:]]) for row in ev]
+        torch.cuda.synchronize()
+        for i in range(Ks):
+            ev[i][0].record(stream)
+            lib().smoe_set_stage_events(handles[i], len(STAGES))
+            forward_once(i % n_layers, (i // n_layers) % n_batches, out)
+        lib().smoe_set_stage_events(None, 0)
+        torch.cuda.synchronize()
+        stage_ms = {s: 0.0 for s in STAGES}
+        for i in range(Ks):
+            for j, s in enumerate(STAGES):
+                stage_ms[s] += ev[i][j].elapsed_time(ev[i][j + 1]) / Ks
+
     hbm_peak, peak_kind = peaks()
     E_BYTES = spec.expert_bytes()
     rbg = synth.row_bytes(spec.gu_type, spec.n_embd) * spec.n_ff
     rbd = synth.row_bytes(spec.d_type, spec.n_ff) * spec.n_embd
-    Ds = [D[(i % args.layers, (i // args.layers) % n_batches)] for i in range(K)]
-    D_mean = float(np.mean(Ds))
     q8x, q8h = (spec.n_embd // 32) * 36, (spec.n_ff // 32) * 36
     rows = T * spec.k + T
-    alg = {"expert_gate_up": lambda d: (d + 1) * 2 * rbg + T * q8x + rows * q8h,
-           "expert_down": lambda d: (d + 1) * rbd + rows * q8h + rows * spec.n_embd * 4,
-           "router_gemv": lambda d: spec.n_expert * spec.n_embd * 2 + T * spec.n_embd * 4 + T * spec.n_expert * 4,
-           "combine": lambda d: rows * spec.n_embd * 4 + T * spec.n_embd * 4}
-    dom_bytes = float(np.mean([alg[dominant](d) for d in Ds])) if dominant in alg else None
-    dom_ms = stage_ms[dominant] / K
-    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_bytes else None
-    tpu = traffic_per_unit()
-    traffic = None
-    if dominant == "expert_gate_up" and "expert_gate_up_per_expert" in tpu:
-        traffic = tpu["expert_gate_up_per_expert"] * (D_mean + 1)
-    expert_gbs = (D_mean + 1) * E_BYTES / (ms_step * 1e-3) / 1e9
+    if stack:
+        Ds = [D[(li, 0)] for li in range(n_layers)]
+        step_bytes = float(sum((d + 1) * E_BYTES for d in Ds))
+        D_mean = float(np.mean(Ds))
+        expert_gbs = step_bytes / (ms_step * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": "whole 48-layer stack (CUDA graph)", "achieved": expert_gbs,
+                "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": expert_gbs / hbm_peak,
+                "traffic": None, "algorithmic_bytes_per_launch": step_bytes, "ms_per_launch": ms_step}
+    else:
+        Ds = [D[(i % n_layers, (i // n_layers) % n_batches)] for i in range(K)]
+        D_mean = float(np.mean(Ds))
+        alg = {"expert_gate_up": lambda d: (d + 1) * 2 * rbg + T * q8x + rows * q8h,
+               "expert_down": lambda d: (d + 1) * rbd + rows * q8h + rows * spec.n_embd * 4,
+               "router_gemv": lambda d: spec.n_expert * spec.n_embd * 2 + T * spec.n_embd * 4 + T * spec.n_expert * 4,
+               "combine": lambda d: rows * spec.n_embd * 4 + T * spec.n_embd * 4}
+        dominant = max(stage_ms, key=stage_ms.get)
+        dom_bytes = float(np.mean([alg[dominant](d) for d in Ds])) if dominant in alg else None
+        dom_ms = stage_ms[dominant]
+        achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_bytes else None
+        tpu = traffic_per_unit()
+        traffic = None
+        if dominant == "expert_gate_up" and not tc and "expert_gate_up_per_expert" in tpu:
+            traffic = tpu["expert_gate_up_per_expert"] * (D_mean + 1)
+        expert_gbs = (D_mean + 1) * E_BYTES / (ms_step * 1e-3) / 1e9
+        roof = {"bound": "hbm", "kernel": (KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE)[dominant],
+                "achieved": achieved, "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": achieved / hbm_peak if achieved else None, "traffic": traffic,
+                "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms}
 
-    # end to end through the public API with host buffers
+    # end to end: every step copies its input from pinned host memory, replays the captured API calls and
+    # reads the result back
     x_host = [x.cpu().pin_memory() for x in xs]
-    out_host = torch.empty(T, spec.n_embd).pin_memory()
-    x_dev = torch.empty(T, spec.n_embd, device=dev)
+    out_host = torch.empty(T, H).pin_memory()
+    res = sbuf[(n_layers - 1) & 1] if stack else out
     Ke = min(K, 1000)
     torch.cuda.synchronize()
     barrier(ws)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    e0.record(gstream)
     for i in range(Ke):
-        x_dev.copy_(x_host[(i // args.layers) % n_batches], non_blocking=True)
-        layers[i % args.layers].forward(x_dev, out)
-        out_host.copy_(out, non_blocking=True)
-    e1.record(stream)
+        b = 0 if stack else (i // n_layers) % n_batches
+        xs[b].copy_(x_host[b], non_blocking=True)
+        graphs[i % G].replay()
+        out_host.copy_(res, non_blocking=True)
+    e1.record(gstream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), ws) / Ke
-    e2e = {"value": ws * T / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": T * spec.n_embd * 4,
-           "d2h_bytes_per_step": T * spec.n_embd * 4, "ms_per_step": e2e_ms}
+    e2e = {"value": ws * T / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": T * H * 4,
+           "d2h_bytes_per_step": T * H * 4, "ms_per_step": e2e_ms,
+           "how": "per step: H2D of the input from pinned memory, replay of the captured smoe_moe_forward calls, "
+                  "D2H of the output"}
     assert api.device_status() == 0
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(synth.make_layer(spec, 0, "cpu"), xs[0].cpu().numpy(), args.cpu_seconds)
+        cpu = cpu_baseline(synth.make_layer(spec, 0, "cpu"), xs[0].cpu().numpy(), args.cpu_seconds,
+                           n_layers if stack else 1)
 
     if rank == 0:
         # router GEMV, top-k (+ q8_1), dispatch, gate/up, [SwiGLU], down, combine; the tensor-core path adds the
-        # hi/lo activation image and fuses SwiGLU into gate/up
-        if tc:
-            launches_per_step = 7
-        else:
-            launches_per_step = 7 + (0 if spec.sg_type == spec.gu_type else 2) + \
-                (0 if spec.sd_type == spec.d_type else 2)
+        # hi/lo activation image and fuses SwiGLU into gate/up; grouping above 256 tokens takes three launches
+        per_fwd = 7 if tc else 7 + (0 if spec.sg_type == spec.gu_type else 2) + (0 if spec.sd_type == spec.d_type else 2)
+        if T > 256:
+            per_fwd += 2
+        launches_per_step = n_layers * (per_fwd + 1) if stack else per_fwd
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
                 "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": ("fp16 x fp16 tcgen05 (exact hi/lo q8_1 image), f32 accumulate" if tc
                           else "int8 x int2 dot (q8_1 contract), f32/f64 sums"), "data": "synthetic",
                 "expert_path": "tensor cores (tcgen05)" if tc else "SIMT",
-                "config": config_dict(args, spec, T, D_mean),
+                "config": config_dict(args, spec, T, D_mean, n_layers, stack),
+                "timing": "CUDA events around CUDA-graph replays (one captured forward per step"
+                          + (", the whole 48-layer stack" if stack else "") + ")",
                 "expert_weight_gbs": expert_gbs, "expert_weight_frac_of_peak": expert_gbs / hbm_peak,
-                "roofline": {"bound": "hbm", "kernel": (KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE)[dominant],
-                             "achieved": achieved,
-                             "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
-                             "frac": achieved / hbm_peak if achieved else None, "traffic": traffic,
-                             "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms},
-                "stage_ms_per_step": {s: v / K for s, v in stage_ms.items()},
+                "roofline": roof, "stage_ms_per_step": stage_ms,
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": K * launches_per_step,
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)

@@ -153,6 +153,15 @@ typedef struct smoe_trace {
 enum { SMOE_STAGES = 6 };
 void smoe_set_stage_events(void** events, int n);
 
+/* The glue of the layer stack.  rms_norm_weighted (include/strata/kernels/elementwise.hpp:82, host rule
+ * metal/src/elementwise_parity.cpp:84-100): in place, per row of cols values, x = (x / sqrt(mean(x^2) + eps)) * w
+ * with the mean and the division in fp64 and w[cols] (NULL: unit weight, an extension).  smoe_add_rms_norm fuses
+ * the reference's add_inplace (elementwise.hpp:52) before it: x = rms_norm(x + residual) * w, the step between
+ * two MoE blocks of the stack (residual NULL: plain rms_norm_weighted).  Zero sizes return SMOE_OK untouched. */
+smoe_status smoe_rms_norm_weighted(float* x, const float* w, int64_t rows, int64_t cols, float eps, void* stream);
+smoe_status smoe_add_rms_norm(float* x, const float* residual, const float* w, int64_t rows, int64_t cols, float eps,
+                              void* stream);
+
 /* Expert-kernel path of smoe_moe_forward (no reference counterpart: the reference has one GPU path).
  * 0 (default) automatic: the tensor-core kernels for batches of 512 tokens or more when the layer qualifies,
  * the SIMT kernels otherwise; 1 the SIMT kernels always; 2 the tensor-core kernels whenever the layer

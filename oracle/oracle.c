@@ -541,3 +541,23 @@ done:
     free(J.g); free(J.u); free(J.hq); free(J.h32); free(J.parts);
     return rc;
 }
+
+/* elementwise_parity.cpp:84-100 (rms_ref with use_sum = false, use_w = w != NULL); add_inplace before it. */
+void orc_add_rms_norm(const float* x, const float* residual, const float* w, int64_t rows, int64_t cols, float eps,
+                      float* out) {
+    for (int64_t r = 0; r < rows; r++) {
+        const float* xr = x + r * cols;
+        float* o = out + r * cols;
+        for (int64_t c = 0; c < cols; c++) o[c] = residual ? xr[c] + residual[r * cols + c] : xr[c];
+        double ss = 0.0;
+        for (int64_t c = 0; c < cols; c++) {
+            const double v = o[c];
+            ss += v * v;
+        }
+        const double den = sqrt(ss / (double) cols + (double) eps);
+        for (int64_t c = 0; c < cols; c++) {
+            const double v = o[c];
+            o[c] = (float) ((v / den) * (w ? (double) w[c] : 1.0));
+        }
+    }
+}

@@ -89,6 +89,12 @@ typedef struct {
 int orc_moe_layer(const orc_layer* L, const float* x, int T, float* out, const orc_trace* tr, int mode,
                   int n_threads);
 
+/* rms_norm_weighted host rule (metal/src/elementwise_parity.cpp:84-100, mean form): per row, ss = sequential
+ * fp64 sum of v^2, den = sqrt(ss / cols + eps), out = (float)((v / den) * w) (w NULL: unit weight).  With
+ * residual non-NULL the row is first (float)(x + residual), the reference's add_inplace (elementwise.hpp:52). */
+void orc_add_rms_norm(const float* x, const float* residual, const float* w, int64_t rows, int64_t cols, float eps,
+                      float* out);
+
 /* Trap variants for the tests (variant 1: Q2_0 codes without the -1, iq_parity.cpp:225-248 minus_one=false). */
 float orc_row_dot_variant(int type, const uint8_t* row, const uint8_t* col_q8, int n_in, int variant);
 

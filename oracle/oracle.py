@@ -85,6 +85,8 @@ def lib() -> C.CDLL:
         L.orc_route.argtypes = [_f32p, C.c_int, C.c_int, _i32p, _f32p]
         L.orc_combine.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_int, C.c_int]
         L.orc_dequant_row.argtypes = [C.c_int, _u8p, C.c_int, _f32p]
+        L.orc_add_rms_norm.argtypes = [_f32p, _f32p, _f32p, C.c_int64, C.c_int64, C.c_float, _f32p]
+        L.orc_add_rms_norm.restype = None
         L.orc_moe_layer.restype = C.c_int
         L.orc_moe_layer.argtypes = [C.POINTER(OrcLayer), _f32p, C.c_int, _f32p, C.POINTER(OrcTrace), C.c_int,
                                     C.c_int]
@@ -239,6 +241,26 @@ def moe_layer(layer: HostLayer, x: np.ndarray, mode: int = 0, n_threads: int | N
     if rc != 0:
         raise ValueError("oracle: bad layer geometry or routed id")
     return (out, bufs) if trace else out
+
+
+def add_rms_norm(x: np.ndarray, residual: np.ndarray | None = None, w: np.ndarray | None = None,
+                 eps: float = 1e-6) -> np.ndarray:
+    """rms_norm_weighted's host rule (elementwise_parity.cpp:84-100) after an optional residual add."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.shape
+    out = np.empty_like(x)
+    r = None if residual is None else np.ascontiguousarray(residual, np.float32)
+    ww = None if w is None else np.ascontiguousarray(w, np.float32)
+    lib().orc_add_rms_norm(_ptr(x, _f32p), None if r is None else _ptr(r, _f32p),
+                           None if ww is None else _ptr(ww, _f32p), rows, cols, eps, _ptr(out, _f32p))
+    return out
+
+
+def moe_stack(layers: list, x: np.ndarray, eps: float = 1e-6, mode: int = 0) -> np.ndarray:
+    """The configs[3] stack: per layer x = rms_norm(x + moe_layer(x)) with unit weight."""
+    for hl in layers:
+        x = add_rms_norm(moe_layer(hl, x, mode=mode), x, None, eps)
+    return x
 
 
 def rel_l1(a: np.ndarray, b: np.ndarray) -> float:

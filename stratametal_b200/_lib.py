@@ -47,6 +47,8 @@ SIGNATURES = {
     "smoe_moe_group": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp, _vp]),
     "smoe_set_stage_events": (None, [C.POINTER(_vp), C.c_int]),
     "smoe_moe_group_noalloc": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, _vp, _vp, _vp]),
+    "smoe_rms_norm_weighted": (C.c_int, [_vp, _vp, C.c_int64, C.c_int64, C.c_float, _vp]),
+    "smoe_add_rms_norm": (C.c_int, [_vp, _vp, _vp, C.c_int64, C.c_int64, C.c_float, _vp]),
     "smoe_set_expert_path": (C.c_int, [C.c_int]),
     "smoe_expert_path_for": (C.c_int, [C.POINTER(SmoeLayer), C.c_int]),
     "smoe_layer_check": (C.c_int, [C.POINTER(SmoeLayer)]),

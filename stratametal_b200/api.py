@@ -15,7 +15,7 @@ from ._lib import SmoeError, SmoeLayer, SmoeTrace, check, lib
 
 __all__ = ["SmoeError", "f32_to_bf16_bulk", "bf16_gemv", "router_top10", "router", "iq_quantize_q8_1", "iq_mmvq",
            "iq_swiglu_q8", "moe_combine", "moe_group", "row_bytes", "q8_1_bytes", "MoeLayer", "device_status",
-           "set_expert_path"]
+           "set_expert_path", "rms_norm_weighted", "add_rms_norm"]
 
 
 def _s() -> int:
@@ -38,6 +38,16 @@ def q8_1_bytes(n: int) -> int:
 
 def device_status(clear: bool = True) -> int:
     return int(lib().smoe_device_status(1 if clear else 0))
+
+
+def rms_norm_weighted(x: torch.Tensor, w: torch.Tensor | None, rows: int, cols: int, eps: float) -> None:
+    check(lib().smoe_rms_norm_weighted(_p(x), _p(w), rows, cols, eps, _s()))
+
+
+def add_rms_norm(x: torch.Tensor, residual: torch.Tensor | None, w: torch.Tensor | None, rows: int, cols: int,
+                 eps: float) -> None:
+    """x = rms_norm(x + residual) * w in place: the step between two MoE blocks of a layer stack."""
+    check(lib().smoe_add_rms_norm(_p(x), _p(residual), _p(w), rows, cols, eps, _s()))
 
 
 def set_expert_path(path: int) -> None:

@@ -303,6 +303,21 @@ smoe_status smoe_moe_group(const int32_t* ids, int n_tok, int k, int n_expert, v
     return e == cudaSuccess ? ok() : cuda_fail(e, "moe_group");
 }
 
+smoe_status smoe_rms_norm_weighted(float* x, const float* w, int64_t rows, int64_t cols, float eps, void* stream) {
+    return smoe_add_rms_norm(x, nullptr, w, rows, cols, eps, stream);
+}
+
+smoe_status smoe_add_rms_norm(float* x, const float* residual, const float* w, int64_t rows, int64_t cols, float eps,
+                              void* stream) {
+    if (rows < 0 || cols < 0) return fail(SMOE_INVALID_ARG, "rms_norm: negative size");
+    if (rows == 0 || cols == 0) return ok();
+    if (!(eps >= 0.f)) return fail(SMOE_INVALID_ARG, "rms_norm: eps must be >= 0");
+    if (!stream) return fail(SMOE_INVALID_ARG, "rms_norm: a non-null stream is required");
+    if (!x) return fail(SMOE_INVALID_ARG, "rms_norm: null buffer");
+    const cudaError_t e = launch_add_rms_norm(x, residual, w, rows, cols, eps, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "rms_norm");
+}
+
 smoe_status smoe_layer_check(const smoe_layer* L) {
     const smoe_status st = check_layer(L);
     return st == SMOE_OK ? ok() : st;

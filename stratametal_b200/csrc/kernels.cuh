@@ -132,6 +132,11 @@ cudaError_t launch_tc_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, 
 cudaError_t launch_tc_down(Matrix down, Matrix sdown, Work w, int n_expert, const __half* hh, int R, float* parts,
                            int n_ff, int n_embd, cudaStream_t s);
 
+// ---- elementwise.cu ----
+// x[r] = rms_norm(x[r] + residual[r]) * w (residual and w may be null): the host rule of rms_ref.
+cudaError_t launch_add_rms_norm(float* x, const float* residual, const float* w, int64_t rows, int64_t cols,
+                                float eps, cudaStream_t s);
+
 // ---- combine.cu ----
 // out[t][j] = sum_i w[t][i] * parts[slot(t, i)][j] (+ shared[t][j] * sigmoid(gate_logit[t]) when shared)
 // slot == nullptr means parts is [T][k][H] in router order; shared_scale == nullptr adds shared plain.

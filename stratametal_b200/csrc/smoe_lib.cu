@@ -5,5 +5,6 @@
 #include "expert.cu"
 #include "combine.cu"
 #include "tc.cu"
+#include "elementwise.cu"
 #include "api.cu"
 #include "noalloc.cu"

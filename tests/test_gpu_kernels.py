@@ -157,3 +157,19 @@ def test_group_stable(cuda, T, E, k):
     want_slot[order] = np.arange(order.size)
     assert np.array_equal(slot.cpu().numpy(), want_slot)
     assert np.array_equal(src.cpu().numpy(), order // k)
+
+
+@pytest.mark.parametrize("rows,cols,resid,weighted", [(1, 2048, True, False), (16, 2048, True, True),
+                                                      (5, 1000, False, True)])
+def test_add_rms_norm(cuda, rows, cols, resid, weighted):
+    rng = np.random.default_rng(rows * cols)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    r = rng.standard_normal((rows, cols)).astype(np.float32) if resid else None
+    w = (0.5 + rng.random(cols)).astype(np.float32) if weighted else None
+    xd = torch.tensor(np.concatenate([x.ravel(), np.full(8, 7.0, np.float32)]), device=cuda)
+    api.add_rms_norm(xd, None if r is None else dev(r, cuda), None if w is None else dev(w, cuda), rows, cols, 1e-6)
+    got = xd.cpu().numpy()
+    assert np.all(got[rows * cols:] == 7.0)
+    want = O.add_rms_norm(x, r, w, 1e-6)
+    ulp = np.abs(bits(got[:rows * cols]).astype(np.int64) - bits(want.ravel()).astype(np.int64))
+    assert ulp.max() <= 1 and (ulp == 0).mean() >= 0.999   # only the fp64 order of the sum of squares differs

@@ -193,3 +193,22 @@ def test_fp32_mode_is_close_to_contract_mode():
     f = O.moe_layer(L, x, mode=1, n_threads=2)
     # the q8_1 activation contract moves the block by about a percent, not more
     assert 1e-4 < O.rel_l1(f, c) < 0.05
+
+
+def test_rms_norm_rule():
+    # the reference's own test inputs (elementwise_parity.cpp:102-112): x = sin(0.017 i) * 1.7 + 0.4,
+    # w = 0.5 + 0.002 (c % 97); checked against an independent fp64 evaluation of the same formula
+    rows, cols = 3, 2048
+    i = np.arange(rows * cols, dtype=np.float64)
+    x = (np.sin(i * 0.017).astype(np.float32) * np.float32(1.7) + np.float32(0.4)).reshape(rows, cols)
+    w = (np.float32(0.5) + np.float32(0.002) * (np.arange(cols) % 97).astype(np.float32)).astype(np.float32)
+    got = O.add_rms_norm(x, None, w, 1e-6)
+    xd = x.astype(np.float64)
+    den = np.sqrt((xd * xd).sum(axis=1, keepdims=True) / cols + np.float64(np.float32(1e-6)))
+    want = ((xd / den) * w.astype(np.float64)).astype(np.float32)
+    assert np.array_equal(got, want)
+    # unit weight: mean of squares 1; the residual is added in f32 first
+    r = np.ones_like(x)
+    g2 = O.add_rms_norm(x, r, None, 1e-6)
+    assert np.allclose((g2.astype(np.float64) ** 2).mean(axis=1), 1.0, atol=1e-5)
+    assert np.array_equal(g2, O.add_rms_norm((x + r).astype(np.float32), None, None, 1e-6))
