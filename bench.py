@@ -300,7 +300,8 @@ def run_ours(args, ws, rank, local):
     n_layers = STACK_LAYERS if stack else args.layers
     api.set_expert_path(args.expert_path)
     layers = [api.MoeLayer(synth.make_layer(spec, li, dev), T, dev) for li in range(n_layers)]
-    tc = lib().smoe_expert_path_for(C.byref(layers[0].c), T) == 2
+    path = lib().smoe_expert_path_for(C.byref(layers[0].c), T)
+    tc, fused = path == 2, path == 3
     n_batches = 1 if stack else 4
     xs = [synth.make_x(spec.seed + 1000 * local, T, H, dev, stream=b) for b in range(n_batches)]
     out = torch.empty(T, H, device=dev)
@@ -411,16 +412,23 @@ def run_ours(args, ws, rank, local):
                "expert_down": lambda d: (d + 1) * rbd + rows * q8h + rows * spec.n_embd * 4,
                "router_gemv": lambda d: spec.n_expert * spec.n_embd * 2 + T * spec.n_embd * 4 + T * spec.n_expert * 4,
                "combine": lambda d: rows * spec.n_embd * 4 + T * spec.n_embd * 4}
-        dominant = max(stage_ms, key=stage_ms.get)
+        if fused:  # one kernel for the whole block: its bytes are the router's and the experts'
+            dominant = "fused"
+            alg["fused"] = lambda d: (d + 1) * E_BYTES + spec.n_expert * spec.n_embd * 2
+            stage_ms = {"fused_block": sum(stage_ms.values())}
+            dom_ms = stage_ms["fused_block"]
+        else:
+            dominant = max(stage_ms, key=stage_ms.get)
+            dom_ms = stage_ms[dominant]
         dom_bytes = float(np.mean([alg[dominant](d) for d in Ds])) if dominant in alg else None
-        dom_ms = stage_ms[dominant]
         achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_bytes else None
         tpu = traffic_per_unit()
         traffic = None
         if dominant == "expert_gate_up" and not tc and "expert_gate_up_per_expert" in tpu:
             traffic = tpu["expert_gate_up_per_expert"] * (D_mean + 1)
         expert_gbs = (D_mean + 1) * E_BYTES / (ms_step * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": (KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE)[dominant],
+        roof = {"bound": "hbm", "kernel": "decode_layer_kernel" if fused else
+                (KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE)[dominant],
                 "achieved": achieved, "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
                 "frac": achieved / hbm_peak if achieved else None, "traffic": traffic,
                 "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms}
@@ -460,12 +468,15 @@ def run_ours(args, ws, rank, local):
         per_fwd = 7 if tc else 7 + (0 if spec.sg_type == spec.gu_type else 2) + (0 if spec.sd_type == spec.d_type else 2)
         if T > 256:
             per_fwd += 2
+        if fused:
+            per_fwd = 1
         launches_per_step = n_layers * (per_fwd + 1) if stack else per_fwd
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
                 "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": ("fp16 x fp16 tcgen05 (exact hi/lo q8_1 image), f32 accumulate" if tc
                           else "int8 x int2 dot (q8_1 contract), f32/f64 sums"), "data": "synthetic",
-                "expert_path": "tensor cores (tcgen05)" if tc else "SIMT",
+                "expert_path": ("tensor cores (tcgen05)" if tc else "fused single-token kernel (one cooperative launch)"
+                                if fused else "SIMT"),
                 "config": config_dict(args, spec, T, D_mean, n_layers, stack),
                 "timing": "CUDA events around CUDA-graph replays (one captured forward per step"
                           + (", the whole 48-layer stack" if stack else "") + ")",

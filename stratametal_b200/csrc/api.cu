@@ -47,11 +47,13 @@ struct Layout {
     size_t xq, xa, xa2, logits, sh_logit, ids, w, slot, slot_token, tables, sched, gu, ha, parts;
     size_t sched_tc, xh, hh;  // the tensor-core path (0 bytes when the layer does not qualify)
     size_t chunk;             // per-(64-token chunk, expert) counts of the many-CTA grouping
+    size_t bar;               // grid barrier words of the single-token fused kernel
     size_t total;
 };
 
-// Expert path: 0 automatic (tensor cores from kTcAutoTokens tokens on), 1 the SIMT kernels, 2 tensor cores
-// whenever the layer qualifies.
+// Expert path: 0 automatic (the fused single-token kernel at one token, tensor cores from kTcAutoTokens tokens
+// on, the SIMT kernels between), 1 the SIMT kernels, 2 tensor cores whenever the layer qualifies, 3 the fused
+// single-token kernel whenever the batch is one token and the layer qualifies.
 std::atomic<int> g_expert_path{0};
 constexpr int kTcAutoTokens = 512;
 
@@ -63,9 +65,16 @@ bool tc_qualifies(const smoe_layer* L) {
     return q2 && L->n_embd % 512 == 0 && L->n_ff % 512 == 0;
 }
 
+bool use_decode(const smoe_layer* L, int T) {
+    const int p = g_expert_path.load(std::memory_order_relaxed);
+    return T == 1 && (p == 0 || p == 3) &&
+           decode_qualifies(L->n_embd, L->n_ff, L->n_expert, L->k, L->gu_type, L->d_type, L->has_shared, L->sg_type,
+                            L->su_type, L->sd_type);
+}
+
 bool use_tc(const smoe_layer* L, int T) {
     const int p = g_expert_path.load(std::memory_order_relaxed);
-    if (p == 1 || !tc_qualifies(L)) return false;
+    if (p == 1 || p == 3 || !tc_qualifies(L)) return false;
     return p == 2 || T >= kTcAutoTokens;
 }
 
@@ -89,6 +98,7 @@ Layout layout_of(const smoe_layer* L, int T) {
     o.ha = at; at += up256(ka_bytes((int64_t) rows, (int) (F / 32)));
     o.parts = at; at += up256(rows * H * 4);
     o.chunk = at; at += group_chunk_bytes(T, (int) E);
+    o.bar = at; at += 256;
     o.sched_tc = o.xh = o.hh = at;
     if (tc_qualifies(L)) {
         o.sched_tc = at; at += sched_bytes((int) E, T, (int) K, kTcChunk);
@@ -136,14 +146,14 @@ extern "C" {
 const char* smoe_last_error(void) { return g_err.c_str(); }
 
 smoe_status smoe_set_expert_path(int path) {
-    if (path < 0 || path > 2) return fail(SMOE_INVALID_ARG, "set_expert_path: path must be 0, 1 or 2");
+    if (path < 0 || path > 3) return fail(SMOE_INVALID_ARG, "set_expert_path: path must be 0, 1, 2 or 3");
     g_expert_path.store(path);
     return ok();
 }
 
 int smoe_expert_path_for(const smoe_layer* L, int n_tokens) {
     if (check_layer(L) != SMOE_OK || n_tokens <= 0) return -1;
-    return use_tc(L, n_tokens) ? 2 : 1;
+    return use_decode(L, n_tokens) ? 3 : use_tc(L, n_tokens) ? 2 : 1;
 }
 
 void smoe_set_stage_events(void** events, int n) {
@@ -358,6 +368,47 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     const KAct ha = ka_at(base + lo.ha, rows, F / 32);
     float* gu = reinterpret_cast<float*>(base + lo.gu);
     float* parts = reinterpret_cast<float*>(base + lo.parts);
+
+    if (use_decode(L, T)) {
+        // one token: the whole block in one cooperative launch
+        DecodeArgs da{};
+        da.x = x;
+        da.out = out;
+        da.router = L->router;
+        da.ginp = sh ? L->gate_inp_shexp : nullptr;
+        da.gate = Matrix{L->gate, (int64_t) F * (int64_t) row_bytes(L->gu_type, H), L->gu_type};
+        da.up = Matrix{L->up, da.gate.expert_stride, L->gu_type};
+        da.down = Matrix{L->down, (int64_t) H * (int64_t) row_bytes(L->d_type, F), L->d_type};
+        da.sgate = Matrix{L->sgate, 0, L->sg_type};
+        da.sup = Matrix{L->sup, 0, L->su_type};
+        da.sdown = Matrix{L->sdown, 0, L->sd_type};
+        da.H = H;
+        da.F = F;
+        da.E = E;
+        da.k = K;
+        da.has_shared = sh ? 1 : 0;
+        da.logits = logits;
+        da.sh_logit = sh_logit;
+        da.ids = ids;
+        da.w = w;
+        da.xa = xa.base;
+        da.ha = ha.base;
+        da.xq = trace && trace->xq ? trace->xq : nullptr;
+        da.parts = trace ? trace->parts : nullptr;
+        da.shared_out = trace ? trace->shared : nullptr;
+        da.bar = reinterpret_cast<unsigned*>(base + lo.bar);
+        cudaError_t e = launch_decode_layer(da, s);
+        for (int st = 0; st < SMOE_STAGES && e == cudaSuccess; st++) e = mark(st, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: fused single-token kernel");
+        if (trace) {
+            if (trace->logits) e = cudaMemcpyAsync(trace->logits, logits, (size_t) E * 4, cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && trace->ids) e = cudaMemcpyAsync(trace->ids, ids, (size_t) K * 4, cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && trace->weights)
+                e = cudaMemcpyAsync(trace->weights, w, (size_t) K * 4, cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(e, "moe_forward: trace");
+        }
+        return ok();
+    }
 
     cudaError_t e = launch_bf16_gemv(x, true, L->router, sh ? L->gate_inp_shexp : nullptr, logits, sh_logit, T, H,
                                      E, s);

@@ -1,0 +1,259 @@
+// decode.cu - one token through one MoE layer in a single cooperative launch (batch-1 decode, configs[0] and the
+// configs[3] stack at batch 1).  At one token every stage of the block is a few microseconds of latency and a
+// few megabytes of bytes, so the seven launches of the general path cost more than their work; here the whole
+// block is three phases of one persistent kernel separated by two grid barriers:
+//
+//   phase 0  router logits (warp per expert row, fp64 accumulation) and the activation's q8_1 image
+//   phase 1  every CTA ranks the logits itself (route_warp), then CTAs take (expert slot, 32-row block) items:
+//            32 gate and 32 up row dots, SwiGLU and the q8_1 rule of that block of h
+//   phase 2  CTAs take ranges of output rows: for each row the down dot of every slot (two per warp, one per
+//            half-warp), then the combine of the row in router order (fp64) plus the gated shared expert
+//
+// Every dot follows the reference's order (partial k of 32 values to lane k & 31, in-lane sums in k order, xor
+// butterfly 16..1), the activations use the q8_1 rule and the combine the host's fp64 router-order sum, so the
+// output equals the general path's bit for bit.  The grid barriers are a counter and a generation word in the
+// caller's scratch, zeroed by the host before the launch; every wait is bounded (kWaitLimitNs) and a timeout
+// records kDevTimeout and ends the CTA.  The launch is cooperative, so every CTA is resident.
+#include "common.cuh"
+#include "kernels.cuh"
+#include "q8.cuh"
+
+namespace smoe {
+
+constexpr int kDecThreads = 512;  // 16 warps
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kDecMaxRows = 32;   // output rows per CTA in phase 2 (n_embd <= 4096 over >= 128 CTAs)
+
+struct DecodeArgs {
+    const float* x;
+    float* out;
+    const uint16_t* router;
+    const uint16_t* ginp;  // shared-expert gate vector (null without a shared expert)
+    Matrix gate, up, down, sgate, sup, sdown;
+    int H, F, E, k, has_shared;
+    float* logits;       // [E]
+    float* sh_logit;     // [1]
+    int32_t* ids;        // [k]
+    float* w;            // [k]
+    uint8_t* xa;         // H / 32 activation blocks (KAct layout, Q2_0 order)
+    uint8_t* ha;         // (k + 1) x F / 32 blocks of h
+    uint8_t* xq;         // optional q8_1 image of x (trace)
+    float* parts;        // optional [k][H] routed outputs in router order (trace)
+    float* shared_out;   // optional [H] gated shared expert (trace)
+    unsigned* bar;       // [2] arrival count, generation: zero before the launch
+};
+
+// All CTAs meet; false when the wait ran out (the caller then ends the CTA).
+__device__ __forceinline__ bool grid_barrier(unsigned* bar) {
+    __syncthreads();
+    int ok = 1;
+    if (threadIdx.x == 0) {
+        volatile unsigned* gen = bar + 1;
+        const unsigned g = *gen;  // cannot advance before this CTA arrives
+        __threadfence();
+        if (atomicAdd(bar, 1u) + 1u == gridDim.x) {
+            bar[0] = 0;
+            __threadfence();
+            atomicAdd(bar + 1, 1u);
+        } else {
+            const uint64_t t0 = global_timer_ns();
+            while (*gen == g) {
+                if (global_timer_ns() - t0 > kWaitLimitNs) {
+                    ok = 0;
+                    atomicOr(&g_smoe_status, kDevTimeout);
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        __threadfence();
+    }
+    return __syncthreads_and(ok) != 0;
+}
+
+// decode_q2 for a row in global memory: the code words come from 2-byte loads inside the 18-byte block (the
+// shared-memory version reads whole aligned words, which can reach 4 bytes past the last row of a plane).
+__device__ __forceinline__ void decode_q2_global(const uint8_t* __restrict__ row, int k, Dec& w) {
+    const uint8_t* blk = row + (k >> 1) * 18;
+    w.d = f16_to_f32(*reinterpret_cast<const uint16_t*>(blk));
+    const uint16_t* q = reinterpret_cast<const uint16_t*>(blk + 2 + 8 * (k & 1));
+    const uint32_t w0 = (uint32_t) q[0] | ((uint32_t) q[1] << 16);
+    const uint32_t w1 = (uint32_t) q[2] | ((uint32_t) q[3] << 16);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        w.c[j] = (w0 >> (2 * j)) & 0x03030303u;
+        w.c[4 + j] = (w1 >> (2 * j)) & 0x03030303u;
+    }
+    w.ls = 0;
+}
+
+// Row dot of n_in values against n_in / 32 activation blocks: partial kk on lane kk & 31, then the butterfly.
+// Every lane returns the sum.
+__device__ __forceinline__ float row_dot_warp(const uint8_t* __restrict__ row, const uint8_t* __restrict__ act,
+                                              int n_in, int lane) {
+    float v = 0.f;
+    for (int kk = lane; kk < n_in / 32; kk += 32) {
+        Dec d;
+        decode_q2_global(row, kk, d);
+        v = __fadd_rn(v, partial_layer<kQ2_0>(d, load_act(act + (size_t) kk * kKaBlock)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// The same for n_in <= 512 on one half-warp (hl = lane & 15): lanes 16..31 of a full warp would hold zeros,
+// so the xor-16 level adds 0 and the 16-lane butterfly gives the same bits.
+__device__ __forceinline__ float row_dot_half(const uint8_t* __restrict__ row, const uint8_t* __restrict__ act,
+                                              int n_in, int hl) {
+    float v = 0.f;
+    if (hl < n_in / 32) {
+        Dec d;
+        decode_q2_global(row, hl, d);
+        v = partial_layer<kQ2_0>(d, load_act(act + (size_t) hl * kKaBlock));
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <int PER_LANE>
+__global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs a) {
+    __shared__ int32_t s_ids[kMaxK];
+    __shared__ float s_w[kMaxK];
+    __shared__ float s_g[32], s_u[32];
+    __shared__ float s_parts[kDecMaxRows][kMaxK + 1];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int gw = blockIdx.x * kDecWarps + warp, nw = gridDim.x * kDecWarps;
+    const int H = a.H, F = a.F, E = a.E, K = a.k;
+    const int nslot = K + (a.has_shared ? 1 : 0);
+
+    // ---- phase 0: router logits (fp64), activation q8_1 ----
+    for (int r = gw; r < E + (a.has_shared ? 1 : 0); r += nw) {
+        const uint16_t* wr = r < E ? a.router + (size_t) r * H : a.ginp;
+        double acc = 0.0;
+        for (int c = lane * 8; c < H; c += 256) {
+            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + c));
+            const float4 x0 = __ldg(reinterpret_cast<const float4*>(a.x + c));
+            const float4 x1 = __ldg(reinterpret_cast<const float4*>(a.x + c + 4));
+            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                acc = fma((double) bf16_round(xv[2 * q]), (double) __uint_as_float(wu[q] << 16), acc);
+                acc = fma((double) bf16_round(xv[2 * q + 1]), (double) __uint_as_float(wu[q] & 0xFFFF0000u), acc);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+            if (r < E) a.logits[r] = (float) acc;
+            else a.sh_logit[0] = (float) acc;
+        }
+    }
+    for (int b = nw - 1 - gw; b < H / 32 && b >= 0; b += nw) {  // the last warps quantize the activation
+        const float xi = a.x[b * 32 + lane];
+        quant_ka_warp(xi, a.xa + (size_t) b * kKaBlock, lane, true);
+        if (a.xq) quant_q8_1_warp(xi, a.xq + (size_t) b * kQ8Block, lane);
+    }
+    if (!grid_barrier(a.bar)) return;
+
+    // ---- phase 1: routing (every CTA), gate/up + SwiGLU + q8_1 per (slot, 32-row block) ----
+    if (warp == 0) {
+        route_warp<PER_LANE>(a.logits, E, K, s_ids, s_w, lane);
+        __syncwarp();
+        if (blockIdx.x == 0)
+            for (int i = lane; i < K; i += 32) {
+                a.ids[i] = s_ids[i];
+                a.w[i] = s_w[i];
+            }
+    }
+    __syncthreads();
+    const int nb = F / 32;
+    const int rbg = (H / 64) * 18;
+    for (int item = blockIdx.x; item < nslot * nb; item += gridDim.x) {
+        const int s = item / nb, b = item % nb;
+        const bool sh = s >= K;
+        const uint8_t* gb = sh ? a.sgate.base : a.gate.base + (int64_t) s_ids[s] * a.gate.expert_stride;
+        const uint8_t* ub = sh ? a.sup.base : a.up.base + (int64_t) s_ids[s] * a.up.expert_stride;
+        // warp w: rows 2w, 2w + 1 of the block, gate then up
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int rl = 2 * warp + (q & 1);
+            const uint8_t* row = (q < 2 ? gb : ub) + (size_t) (b * 32 + rl) * rbg;
+            const float v = row_dot_warp(row, a.xa, H, lane);
+            if (lane == 0) (q < 2 ? s_g : s_u)[rl] = v;
+        }
+        __syncthreads();
+        if (warp == 0)
+            quant_ka_warp(silu_mul(s_g[lane], s_u[lane]), a.ha + ((size_t) s * nb + b) * kKaBlock, lane, true);
+        __syncthreads();
+    }
+    if (!grid_barrier(a.bar)) return;
+
+    // ---- phase 2: down dots by output row range, then the combine of each row ----
+    const int rows_per = (H + gridDim.x - 1) / gridDim.x;
+    const int j0 = blockIdx.x * rows_per, nj = max(0, min(rows_per, H - j0));
+    const int rbd = (F / 64) * 18;
+    const int hl = lane & 15, half = lane >> 4;
+    const int n_dots = nj * nslot;
+    for (int u2 = warp; 2 * u2 < n_dots; u2 += kDecWarps) {  // warp-uniform trip count; a half may idle
+        const int u = 2 * u2 + half;
+        const bool valid = u < n_dots;
+        const int jl = valid ? u / nslot : 0, s = valid ? u % nslot : 0;
+        const bool sh = s >= K;
+        const uint8_t* row = (sh ? a.sdown.base : a.down.base + (int64_t) s_ids[s] * a.down.expert_stride) +
+                             (size_t) (j0 + jl) * rbd;
+        const float v = row_dot_half(row, a.ha + (size_t) s * nb * kKaBlock, valid ? F : 0, hl);
+        if (valid && hl == 0) s_parts[jl][s] = v;
+    }
+    __syncthreads();
+    if ((int) threadIdx.x < nj) {
+        const int jl = threadIdx.x, j = j0 + jl;
+        double acc = 0.0;
+        for (int i = 0; i < K; i++) {
+            acc += (double) s_w[i] * (double) s_parts[jl][i];
+            if (a.parts) a.parts[(size_t) i * H + j] = s_parts[jl][i];
+        }
+        if (a.has_shared) {
+            const float e = (float) exp(-(double) a.sh_logit[0]);
+            const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+            const float shv = __fmul_rn(s_parts[jl][K], sig);
+            if (a.shared_out) a.shared_out[j] = shv;
+            acc += (double) shv;
+        }
+        a.out[j] = (float) acc;
+    }
+}
+
+// The fused path needs every matrix in Q2_0, n_embd a multiple of 256 (the router's 8-value lanes) and at most
+// 512 intermediate values (one half-warp per down dot).
+bool decode_qualifies(int H, int F, int E, int k, int gu_type, int d_type, int has_shared, int sg, int su, int sd) {
+    const bool q2 = gu_type == kQ2_0 && d_type == kQ2_0 &&
+                    (!has_shared || (sg == kQ2_0 && su == kQ2_0 && sd == kQ2_0));
+    return q2 && H % 256 == 0 && F % 32 == 0 && F <= 512 && E <= kMaxExperts && k <= kMaxK && k <= E;
+}
+
+cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t s) {
+    cudaError_t e = cudaMemsetAsync(a.bar, 0, 2 * sizeof(unsigned), s);
+    if (e != cudaSuccess) return e;
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    if ((a.H + nsm - 1) / nsm > kDecMaxRows) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) nsm);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (a.E <= 256) return cudaLaunchKernelEx(&cfg, decode_layer_kernel<8>, a);
+    if (a.E <= 512) return cudaLaunchKernelEx(&cfg, decode_layer_kernel<16>, a);
+    return cudaLaunchKernelEx(&cfg, decode_layer_kernel<32>, a);
+}
+
+}  // namespace smoe

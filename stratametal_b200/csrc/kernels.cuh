@@ -137,6 +137,11 @@ cudaError_t launch_tc_down(Matrix down, Matrix sdown, Work w, int n_expert, cons
 cudaError_t launch_add_rms_norm(float* x, const float* residual, const float* w, int64_t rows, int64_t cols,
                                 float eps, cudaStream_t s);
 
+// ---- decode.cu ---- (one token through the whole block in one cooperative launch)
+struct DecodeArgs;
+bool decode_qualifies(int H, int F, int E, int k, int gu_type, int d_type, int has_shared, int sg, int su, int sd);
+cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t s);
+
 // ---- combine.cu ----
 // out[t][j] = sum_i w[t][i] * parts[slot(t, i)][j] (+ shared[t][j] * sigmoid(gate_logit[t]) when shared)
 // slot == nullptr means parts is [T][k][H] in router order; shared_scale == nullptr adds shared plain.

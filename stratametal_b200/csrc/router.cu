@@ -252,6 +252,77 @@ __device__ __forceinline__ bool better(double v, int i, double bv, int bi) { ret
 
 constexpr int kTopkWarps = 8;
 
+// The routing of one token by one warp (route_ref, pack_parity.cpp:5144-5165): ids[0..k) and the renormalised
+// weights wout[0..k) (global or shared memory).
+template <int PER_LANE>
+__device__ __forceinline__ void route_warp(const float* __restrict__ l, int E, int k, int32_t* ids, float* wout,
+                                           int lane) {
+    float lv[PER_LANE];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < PER_LANE; j++) {
+        const int e = lane + 32 * j;
+        lv[j] = e < E ? l[e] : -INFINITY;
+        mx = fmaxf(mx, lv[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    double pv[PER_LANE];
+    double part = 0.0;
+#pragma unroll
+    for (int j = 0; j < PER_LANE; j++) {
+        const int e = lane + 32 * j;
+        pv[j] = e < E ? exp((double) lv[j] - (double) mx) : -1.0;
+        if (e < E) part += pv[j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    const double sum = part;
+    uint32_t taken = 0;
+    double bv = -1.0;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < PER_LANE; j++)
+        if (better(pv[j], lane + 32 * j, bv, bi)) { bv = pv[j]; bi = lane + 32 * j; }
+    double chosen = 0.0, my_p = 0.0;
+    int my_id = 0;
+    for (int i = 0; i < k; i++) {
+        double v = bv;
+        int ix = bi;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const double ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
+            if (better(ov, oi, v, ix)) { v = ov; ix = oi; }
+        }
+        const double pn = v / sum;
+        chosen += pn;
+        if (lane == (i & 31)) { my_p = pn; my_id = ix; }  // lane i keeps rank i (k <= 64: two rounds)
+        if (i == 31 || i == k - 1) {
+            // flush ranks [i & ~31, i] written so far by their lanes
+            const int r = (i & ~31) + lane;
+            if (lane <= (i & 31)) {
+                ids[r] = my_id;
+                wout[r] = (float) my_p;  // raw (float) p; renormalised below
+            }
+        }
+        if ((ix & 31) == lane) {
+            taken |= 1u << (ix >> 5);
+            bv = -1.0;
+            bi = 0x7fffffff;
+#pragma unroll
+            for (int j = 0; j < PER_LANE; j++)
+                if (!((taken >> j) & 1u) && better(pv[j], lane + 32 * j, bv, bi)) { bv = pv[j]; bi = lane + 32 * j; }
+        }
+    }
+    chosen = fmax(chosen, 6.103515625e-05);
+    __syncwarp();
+    for (int r = lane; r < k; r += 32) {
+        float* wp = wout + r;
+        *wp = (float) ((double) *wp / chosen);
+    }
+}
+
 template <int PER_LANE>
 __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const float* __restrict__ logits, int T, int E,
                                                                       int k, int32_t* __restrict__ ids,
@@ -273,73 +344,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const floa
         return;
     }
     const int t = blockIdx.x * kTopkWarps + warp;
-    if (t < T) {
-        const float* l = logits + (size_t) t * E;
-        float lv[PER_LANE];
-        float mx = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < PER_LANE; j++) {
-            const int e = lane + 32 * j;
-            lv[j] = e < E ? l[e] : -INFINITY;
-            mx = fmaxf(mx, lv[j]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        double pv[PER_LANE];
-        double part = 0.0;
-#pragma unroll
-        for (int j = 0; j < PER_LANE; j++) {
-            const int e = lane + 32 * j;
-            pv[j] = e < E ? exp((double) lv[j] - (double) mx) : -1.0;
-            if (e < E) part += pv[j];
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        const double sum = part;
-        uint32_t taken = 0;
-        double bv = -1.0;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < PER_LANE; j++)
-            if (better(pv[j], lane + 32 * j, bv, bi)) { bv = pv[j]; bi = lane + 32 * j; }
-        double chosen = 0.0, my_p = 0.0;
-        int my_id = 0;
-        for (int i = 0; i < k; i++) {
-            double v = bv;
-            int ix = bi;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const double ov = __shfl_xor_sync(0xffffffffu, v, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
-                if (better(ov, oi, v, ix)) { v = ov; ix = oi; }
-            }
-            const double pn = v / sum;
-            chosen += pn;
-            if (lane == (i & 31)) { my_p = pn; my_id = ix; }  // lane i keeps rank i (k <= 64: two rounds)
-            if (i == 31 || i == k - 1) {
-                // flush ranks [i & ~31, i] written so far by their lanes
-                const int r = (i & ~31) + lane;
-                if (lane <= (i & 31)) {
-                    ids[(size_t) t * k + r] = my_id;
-                    wout[(size_t) t * k + r] = (float) my_p;  // raw (float) p; renormalised below
-                }
-            }
-            if ((ix & 31) == lane) {
-                taken |= 1u << (ix >> 5);
-                bv = -1.0;
-                bi = 0x7fffffff;
-#pragma unroll
-                for (int j = 0; j < PER_LANE; j++)
-                    if (!((taken >> j) & 1u) && better(pv[j], lane + 32 * j, bv, bi)) { bv = pv[j]; bi = lane + 32 * j; }
-            }
-        }
-        chosen = fmax(chosen, 6.103515625e-05);
-        __syncwarp();
-        for (int r = lane; r < k; r += 32) {
-            float* wp = wout + (size_t) t * k + r;
-            *wp = (float) ((double) *wp / chosen);
-        }
-    }
+    if (t < T) route_warp<PER_LANE>(logits + (size_t) t * E, E, k, ids + (size_t) t * k, wout + (size_t) t * k, lane);
 }
 
 // ------------------------------------------------------------------------------------------------

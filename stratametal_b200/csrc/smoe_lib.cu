@@ -6,5 +6,6 @@
 #include "combine.cu"
 #include "tc.cu"
 #include "elementwise.cu"
+#include "decode.cu"
 #include "api.cu"
 #include "noalloc.cu"

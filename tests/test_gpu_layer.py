@@ -126,3 +126,32 @@ def test_many_tokens_wide_grouping(cuda):
     assert np.array_equal(tr.ids.cpu().numpy(), otr["ids"])
     assert O.rel_l1(otr["parts"], tr.parts.cpu().numpy()) <= 1e-5
     assert O.rel_l1(want, got) <= 1e-5
+
+
+@pytest.mark.parametrize("shared", [True, False])
+def test_fused_single_token_equals_simt(cuda, shared):
+    # one token: the fused cooperative kernel (path 3) and the seven-launch SIMT path give the same bits
+    import ctypes as C
+
+    from stratametal_b200 import _lib
+    spec = synth.LayerSpec(n_embd=2048, n_ff=512, n_expert=512, k=10, has_shared=shared, seed=51)
+    lay = synth.make_layer(spec, 0, cuda)
+    x = synth.make_x(4, 1, 2048, cuda)
+    outs = []
+    try:
+        for path in (3, 1):
+            api.set_expert_path(path)
+            m = api.MoeLayer(lay, 1, cuda)
+            assert _lib.lib().smoe_expert_path_for(C.byref(m.c), 1) == path
+            tr = m.make_trace(1)
+            api.device_status(clear=True)
+            o = m.forward(x, None, tr)
+            torch.cuda.synchronize()
+            assert api.device_status() == 0
+            outs.append((o.cpu().numpy(), tr.parts.cpu().numpy(), tr.ids.cpu().numpy(), tr.weights.cpu().numpy()))
+    finally:
+        api.set_expert_path(0)
+    (a, pa, ia, wa), (b, pb, ib, wb) = outs
+    assert np.array_equal(ia, ib) and np.array_equal(bits(wa), bits(wb))
+    assert np.array_equal(bits(pa), bits(pb))
+    assert np.array_equal(bits(a), bits(b))

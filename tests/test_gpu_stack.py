@@ -40,7 +40,7 @@ def test_stack_vs_oracle(cuda):
     assert np.allclose((got.astype(np.float64) ** 2).mean(axis=1), 1.0, atol=1e-4)
 
 
-@pytest.mark.parametrize("path,T", [(1, 8), (2, 64)])
+@pytest.mark.parametrize("path,T", [(1, 8), (2, 64), (0, 1)])  # SIMT, tensor cores, fused single token
 def test_graph_replay_matches_eager(cuda, path, T):
     spec = synth.LayerSpec(n_embd=2048, n_ff=512, n_expert=64, k=10, seed=41)
     api.set_expert_path(path)
