@@ -6,8 +6,10 @@
 //   phase 0  router logits (warp per expert row, fp64 accumulation) and the activation's q8_1 image
 //   phase 1  every CTA ranks the logits itself (route_warp), then CTAs take (expert slot, 32-row block) items:
 //            32 gate and 32 up row dots, SwiGLU and the q8_1 rule of that block of h
-//   phase 2  CTAs take ranges of output rows: for each row the down dot of every slot (two per warp, one per
-//            half-warp), then the combine of the row in router order (fp64) plus the gated shared expert
+//   phase 2  CTAs take ranges of output rows: for each row the down dot of every slot (one per half-warp: at
+//            n_ff <= 512 the partials fill lanes 0..15, so the xor-16 level of the reference's butterfly adds
+//            zeros and the 16-lane butterfly gives the same bits), then the combine of the row in router order
+//            (fp64) plus the gated shared expert
 //
 // Every dot follows the reference's order (partial k of 32 values to lane k & 31, in-lane sums in k order, xor
 // butterfly 16..1), the activations use the q8_1 rule and the combine the host's fp64 router-order sum, so the
@@ -87,34 +89,25 @@ __device__ __forceinline__ void decode_q2_global(const uint8_t* __restrict__ row
     w.ls = 0;
 }
 
-// Row dot of n_in values against n_in / 32 activation blocks: partial kk on lane kk & 31, then the butterfly.
-// Every lane returns the sum.
-__device__ __forceinline__ float row_dot_warp(const uint8_t* __restrict__ row, const uint8_t* __restrict__ act,
-                                              int n_in, int lane) {
-    float v = 0.f;
+// Four row dots of n_in values against the same n_in / 32 activation blocks, in the reference's order (partial
+// kk on lane kk & 31, in-lane sums in kk order, xor butterfly 16..1; every lane returns the sums).  All loads of
+// a partial position are issued before its math, so a warp keeps more of them in flight.
+__device__ __forceinline__ void row_dot4_warp(const uint8_t* const (&rows)[4], const uint8_t* __restrict__ act,
+                                              int n_in, int lane, float (&v)[4]) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) v[q] = 0.f;
     for (int kk = lane; kk < n_in / 32; kk += 32) {
-        Dec d;
-        decode_q2_global(row, kk, d);
-        v = __fadd_rn(v, partial_layer<kQ2_0>(d, load_act(act + (size_t) kk * kKaBlock)));
+        Dec d[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) decode_q2_global(rows[q], kk, d[q]);
+        const ActRegs ar = load_act(act + (size_t) kk * kKaBlock);
+#pragma unroll
+        for (int q = 0; q < 4; q++) v[q] = __fadd_rn(v[q], partial_layer<kQ2_0>(d[q], ar));
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-
-// The same for n_in <= 512 on one half-warp (hl = lane & 15): lanes 16..31 of a full warp would hold zeros,
-// so the xor-16 level adds 0 and the 16-lane butterfly gives the same bits.
-__device__ __forceinline__ float row_dot_half(const uint8_t* __restrict__ row, const uint8_t* __restrict__ act,
-                                              int n_in, int hl) {
-    float v = 0.f;
-    if (hl < n_in / 32) {
-        Dec d;
-        decode_q2_global(row, hl, d);
-        v = partial_layer<kQ2_0>(d, load_act(act + (size_t) hl * kKaBlock));
-    }
+    for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
+        for (int q = 0; q < 4; q++) v[q] = __fadd_rn(v[q], __shfl_xor_sync(0xffffffffu, v[q], o));
 }
 
 template <int PER_LANE>
@@ -132,6 +125,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs
     for (int r = gw; r < E + (a.has_shared ? 1 : 0); r += nw) {
         const uint16_t* wr = r < E ? a.router + (size_t) r * H : a.ginp;
         double acc = 0.0;
+#pragma unroll 8
         for (int c = lane * 8; c < H; c += 256) {
             const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + c));
             const float4 x0 = __ldg(reinterpret_cast<const float4*>(a.x + c));
@@ -177,12 +171,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs
         const uint8_t* gb = sh ? a.sgate.base : a.gate.base + (int64_t) s_ids[s] * a.gate.expert_stride;
         const uint8_t* ub = sh ? a.sup.base : a.up.base + (int64_t) s_ids[s] * a.up.expert_stride;
         // warp w: rows 2w, 2w + 1 of the block, gate then up
+        const uint8_t* rows[4];
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int rl = 2 * warp + (q & 1);
-            const uint8_t* row = (q < 2 ? gb : ub) + (size_t) (b * 32 + rl) * rbg;
-            const float v = row_dot_warp(row, a.xa, H, lane);
-            if (lane == 0) (q < 2 ? s_g : s_u)[rl] = v;
+        for (int q = 0; q < 4; q++) rows[q] = (q < 2 ? gb : ub) + (size_t) (b * 32 + 2 * warp + (q & 1)) * rbg;
+        float v[4];
+        row_dot4_warp(rows, a.xa, H, lane, v);
+        if (lane == 0) {
+            s_g[2 * warp] = v[0];
+            s_g[2 * warp + 1] = v[1];
+            s_u[2 * warp] = v[2];
+            s_u[2 * warp + 1] = v[3];
         }
         __syncthreads();
         if (warp == 0)
@@ -197,15 +195,35 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs
     const int rbd = (F / 64) * 18;
     const int hl = lane & 15, half = lane >> 4;
     const int n_dots = nj * nslot;
-    for (int u2 = warp; 2 * u2 < n_dots; u2 += kDecWarps) {  // warp-uniform trip count; a half may idle
-        const int u = 2 * u2 + half;
-        const bool valid = u < n_dots;
-        const int jl = valid ? u / nslot : 0, s = valid ? u % nslot : 0;
-        const bool sh = s >= K;
-        const uint8_t* row = (sh ? a.sdown.base : a.down.base + (int64_t) s_ids[s] * a.down.expert_stride) +
-                             (size_t) (j0 + jl) * rbd;
-        const float v = row_dot_half(row, a.ha + (size_t) s * nb * kKaBlock, valid ? F : 0, hl);
-        if (valid && hl == 0) s_parts[jl][s] = v;
+    constexpr int kBatch = 3;  // dots per half-warp with their loads in flight together
+    for (int u2 = warp; 2 * u2 < n_dots; u2 += kDecWarps * kBatch) {  // warp-uniform trip count
+        Dec d[kBatch];
+        ActRegs ar[kBatch];
+        bool act[kBatch];
+        int jl[kBatch], sl[kBatch];
+#pragma unroll
+        for (int i = 0; i < kBatch; i++) {
+            const int u = 2 * (u2 + i * kDecWarps) + half;
+            const bool valid = u < n_dots;
+            jl[i] = valid ? u / nslot : 0;
+            sl[i] = valid ? u % nslot : 0;
+            act[i] = valid && hl < F / 32;  // partial hl of this dot (lanes past the partials hold zero)
+            if (act[i]) {
+                const uint8_t* row = (sl[i] >= K ? a.sdown.base
+                                                 : a.down.base + (int64_t) s_ids[sl[i]] * a.down.expert_stride) +
+                                     (size_t) (j0 + jl[i]) * rbd;
+                decode_q2_global(row, hl, d[i]);
+                ar[i] = load_act(a.ha + ((size_t) sl[i] * nb + hl) * kKaBlock);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; i++) {
+            float v = act[i] ? partial_layer<kQ2_0>(d[i], ar[i]) : 0.f;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+            const int u = 2 * (u2 + i * kDecWarps) + half;
+            if (u < n_dots && hl == 0) s_parts[jl[i]][sl[i]] = v;
+        }
     }
     __syncthreads();
     if ((int) threadIdx.x < nj) {

@@ -248,12 +248,18 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, uint16_t* __rest
 // route_ref does: w = (float)(p / sum), chosen = sum of those quotients in rank order, clamped at 2^-14,
 // final (float)((double) w / chosen).  With xq the CTA then writes the q8_1 image of its 8 tokens.
 // ------------------------------------------------------------------------------------------------
-__device__ __forceinline__ bool better(double v, int i, double bv, int bi) { return v > bv || (v == bv && i < bi); }
 
 constexpr int kTopkWarps = 8;
 
 // The routing of one token by one warp (route_ref, pack_parity.cpp:5144-5165): ids[0..k) and the renormalised
-// weights wout[0..k) (global or shared memory).
+// weights wout[0..k) (global or shared memory).  p_e = exp(l_e - max) in fp64 and its sum (per-lane partial sums,
+// then the xor butterfly).  The ranking by p descending with the lower index on a tie is the ranking by the f32
+// logit descending with the same tie rule: exp is increasing, equal logits give equal p, and distinct f32
+// logits (at least one f32 ulp apart) give distinct fp64 p in the same order.  So the selection rounds compare
+// floats; p is evaluated again, by the same expression, for the k chosen.  Then w = (float)(p / sum), chosen =
+// the sum of those quotients in rank order, clamped at 2^-14, and the final weight (float)((double) w / chosen).
+__device__ __forceinline__ bool better_f(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+
 template <int PER_LANE>
 __device__ __forceinline__ void route_warp(const float* __restrict__ l, int E, int k, int32_t* ids, float* wout,
                                            int lane) {
@@ -267,59 +273,59 @@ __device__ __forceinline__ void route_warp(const float* __restrict__ l, int E, i
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    double pv[PER_LANE];
     double part = 0.0;
 #pragma unroll
-    for (int j = 0; j < PER_LANE; j++) {
-        const int e = lane + 32 * j;
-        pv[j] = e < E ? exp((double) lv[j] - (double) mx) : -1.0;
-        if (e < E) part += pv[j];
-    }
+    for (int j = 0; j < PER_LANE; j++)
+        if (lane + 32 * j < E) part += exp((double) lv[j] - (double) mx);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
     const double sum = part;
+    // selection: each lane offers its best untaken value; k rounds of a warp argmax
     uint32_t taken = 0;
-    double bv = -1.0;
+    float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
     for (int j = 0; j < PER_LANE; j++)
-        if (better(pv[j], lane + 32 * j, bv, bi)) { bv = pv[j]; bi = lane + 32 * j; }
-    double chosen = 0.0, my_p = 0.0;
-    int my_id = 0;
+        if (lane + 32 * j < E && better_f(lv[j], lane + 32 * j, bv, bi)) { bv = lv[j]; bi = lane + 32 * j; }
+    int id0 = 0, id1 = 0;  // ranks lane and 32 + lane (k <= 64)
     for (int i = 0; i < k; i++) {
-        double v = bv;
+        float v = bv;
         int ix = bi;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            const double ov = __shfl_xor_sync(0xffffffffu, v, o);
+            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
             const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
-            if (better(ov, oi, v, ix)) { v = ov; ix = oi; }
+            if (better_f(ov, oi, v, ix)) { v = ov; ix = oi; }
         }
-        const double pn = v / sum;
-        chosen += pn;
-        if (lane == (i & 31)) { my_p = pn; my_id = ix; }  // lane i keeps rank i (k <= 64: two rounds)
-        if (i == 31 || i == k - 1) {
-            // flush ranks [i & ~31, i] written so far by their lanes
-            const int r = (i & ~31) + lane;
-            if (lane <= (i & 31)) {
-                ids[r] = my_id;
-                wout[r] = (float) my_p;  // raw (float) p; renormalised below
-            }
+        if (lane == (i & 31)) {
+            if (i < 32) id0 = ix;
+            else id1 = ix;
         }
         if ((ix & 31) == lane) {
             taken |= 1u << (ix >> 5);
-            bv = -1.0;
+            bv = -INFINITY;
             bi = 0x7fffffff;
 #pragma unroll
             for (int j = 0; j < PER_LANE; j++)
-                if (!((taken >> j) & 1u) && better(pv[j], lane + 32 * j, bv, bi)) { bv = pv[j]; bi = lane + 32 * j; }
+                if (!((taken >> j) & 1u) && lane + 32 * j < E && better_f(lv[j], lane + 32 * j, bv, bi)) {
+                    bv = lv[j];
+                    bi = lane + 32 * j;
+                }
         }
     }
+    // weights of the chosen, the chosen sum in rank order
+    const double pn0 = lane < k ? exp((double) l[id0] - (double) mx) / sum : 0.0;
+    const double pn1 = 32 + lane < k ? exp((double) l[id1] - (double) mx) / sum : 0.0;
+    double chosen = 0.0;
+    for (int i = 0; i < k; i++) chosen += __shfl_sync(0xffffffffu, i < 32 ? pn0 : pn1, i & 31);
     chosen = fmax(chosen, 6.103515625e-05);
-    __syncwarp();
-    for (int r = lane; r < k; r += 32) {
-        float* wp = wout + r;
-        *wp = (float) ((double) *wp / chosen);
+    if (lane < k) {
+        ids[lane] = id0;
+        wout[lane] = (float) ((double) (float) pn0 / chosen);
+    }
+    if (32 + lane < k) {
+        ids[32 + lane] = id1;
+        wout[32 + lane] = (float) ((double) (float) pn1 / chosen);
     }
 }
 
