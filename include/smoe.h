@@ -167,7 +167,8 @@ smoe_status smoe_add_rms_norm(float* x, const float* residual, const float* w, i
  * batches of 512 tokens or more the tensor-core kernels when the layer qualifies, the SIMT kernels otherwise;
  * 1 the SIMT kernels always; 2 the tensor-core kernels whenever the layer qualifies (every routed and shared
  * matrix Q2_0, n_embd and n_ff multiples of 512); 3 the fused single-token kernel whenever the batch is one
- * token and the layer qualifies (every matrix Q2_0, n_embd a multiple of 256, n_ff at most 512).  The SIMT and
+ * token and the layer qualifies (every matrix Q2_0, n_embd a multiple of 256, n_ff and n_expert at
+ * most 512).  The SIMT and
  * fused kernels evaluate the reference's q8_1 integer contract in the reference's summation order; the
  * tensor-core kernels evaluate the same products from an exact fp16 hi/lo split of the q8_1 activation with f32
  * accumulation, so their results agree up to the order of the f32 additions.  Process-wide. */

@@ -4,7 +4,7 @@
 // block is three phases of one persistent kernel separated by two grid barriers:
 //
 //   phase 0  router logits (warp per expert row, fp64 accumulation) and the activation's q8_1 image
-//   phase 1  every CTA ranks the logits itself (route_warp), then CTAs take (expert slot, 32-row block) items:
+//   phase 1  every CTA ranks the logits itself (route_cta), then CTAs take (expert slot, 32-row block) items:
 //            32 gate and 32 up row dots, SwiGLU and the q8_1 rule of that block of h
 //   phase 2  CTAs take ranges of output rows: for each row the down dot of every slot (one per half-warp: at
 //            n_ff <= 512 the partials fill lanes 0..15, so the xor-16 level of the reference's butterfly adds
@@ -110,7 +110,82 @@ __device__ __forceinline__ void row_dot4_warp(const uint8_t* const (&rows)[4], c
         for (int q = 0; q < 4; q++) v[q] = __fadd_rn(v[q], __shfl_xor_sync(0xffffffffu, v[q], o));
 }
 
-template <int PER_LANE>
+// route_warp's result computed by a whole CTA of kDecThreads threads (E <= kDecThreads): thread t holds logit t.
+// The order (logit descending, lower index first) comes from a bitonic sort of (logit, index) - partners closer
+// than 32 exchange by shuffle, farther ones through shared memory.  p = exp(l - max) in fp64 is evaluated once per
+// expert; its sum is taken in route_warp's order (lane l adds p[l], p[l + 32], ... in turn, then the xor
+// butterfly), and the weights of the chosen as route_warp forms them, so the two give the same bits.
+__device__ __forceinline__ bool rank_before(float va, int ia, float vb, int ib) {
+    return va > vb || (va == vb && ia < ib);
+}
+
+__device__ __forceinline__ void route_cta(const float* __restrict__ l, int E, int k, int32_t* s_ids, float* s_w) {
+    __shared__ float sv[kDecThreads];
+    __shared__ int si[kDecThreads];
+    __shared__ double sp[kDecThreads];
+    __shared__ float s_red[kDecWarps];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    float v = t < E ? l[t] : -INFINITY;
+    int ix = t;
+    float m = v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) s_red[warp] = m;
+    __syncthreads();
+    float mx = s_red[0];
+#pragma unroll
+    for (int i = 1; i < kDecWarps; i++) mx = fmaxf(mx, s_red[i]);
+    if (t < E) sp[t] = exp((double) v - (double) mx);
+    // bitonic sort of (v, ix), final order: rank_before
+    for (int kk = 2; kk <= kDecThreads; kk <<= 1) {
+        for (int j = kk >> 1; j > 0; j >>= 1) {
+            float pv;
+            int pi;
+            if (j >= 32) {
+                __syncthreads();
+                sv[t] = v;
+                si[t] = ix;
+                __syncthreads();
+                pv = sv[t ^ j];
+                pi = si[t ^ j];
+            } else {
+                pv = __shfl_xor_sync(0xffffffffu, v, j);
+                pi = __shfl_xor_sync(0xffffffffu, ix, j);
+            }
+            const bool first = ((t & j) == 0) == ((t & kk) == 0);  // this position keeps the earlier of the two
+            const bool mine_first = rank_before(v, ix, pv, pi);
+            if (first != mine_first) {
+                v = pv;
+                ix = pi;
+            }
+        }
+    }
+    __syncthreads();
+    sv[t] = v;
+    si[t] = ix;
+    __syncthreads();
+    if (warp == 0) {
+        double part = 0.0;
+        for (int e = lane; e < E; e += 32) part += sp[e];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        const double sum = part;
+        const double pn0 = lane < k ? sp[si[lane]] / sum : 0.0;
+        const double pn1 = 32 + lane < k ? sp[si[32 + lane]] / sum : 0.0;
+        double chosen = 0.0;
+        for (int i = 0; i < k; i++) chosen += __shfl_sync(0xffffffffu, i < 32 ? pn0 : pn1, i & 31);
+        chosen = fmax(chosen, 6.103515625e-05);
+        if (lane < k) {
+            s_ids[lane] = si[lane];
+            s_w[lane] = (float) ((double) (float) pn0 / chosen);
+        }
+        if (32 + lane < k) {
+            s_ids[32 + lane] = si[32 + lane];
+            s_w[32 + lane] = (float) ((double) (float) pn1 / chosen);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs a) {
     __shared__ int32_t s_ids[kMaxK];
     __shared__ float s_w[kMaxK];
@@ -153,16 +228,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs
     if (!grid_barrier(a.bar)) return;
 
     // ---- phase 1: routing (every CTA), gate/up + SwiGLU + q8_1 per (slot, 32-row block) ----
-    if (warp == 0) {
-        route_warp<PER_LANE>(a.logits, E, K, s_ids, s_w, lane);
-        __syncwarp();
-        if (blockIdx.x == 0)
-            for (int i = lane; i < K; i += 32) {
-                a.ids[i] = s_ids[i];
-                a.w[i] = s_w[i];
-            }
-    }
+    route_cta(a.logits, E, K, s_ids, s_w);
     __syncthreads();
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+            a.ids[i] = s_ids[i];
+            a.w[i] = s_w[i];
+        }
     const int nb = F / 32;
     const int rbg = (H / 64) * 18;
     for (int item = blockIdx.x; item < nslot * nb; item += gridDim.x) {
@@ -244,12 +316,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs
     }
 }
 
-// The fused path needs every matrix in Q2_0, n_embd a multiple of 256 (the router's 8-value lanes) and at most
-// 512 intermediate values (one half-warp per down dot).
+// The fused path needs every matrix in Q2_0, n_embd a multiple of 256 (the router's 8-value lanes), at most 512
+// intermediate values (one half-warp per down dot) and at most 512 experts (one per thread in the routing).
 bool decode_qualifies(int H, int F, int E, int k, int gu_type, int d_type, int has_shared, int sg, int su, int sd) {
     const bool q2 = gu_type == kQ2_0 && d_type == kQ2_0 &&
                     (!has_shared || (sg == kQ2_0 && su == kQ2_0 && sd == kQ2_0));
-    return q2 && H % 256 == 0 && F % 32 == 0 && F <= 512 && E <= kMaxExperts && k <= kMaxK && k <= E;
+    return q2 && H % 256 == 0 && F % 32 == 0 && F <= 512 && E <= kDecThreads && k <= kMaxK && k <= E;
 }
 
 cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t s) {
@@ -269,9 +341,7 @@ cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t s) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (a.E <= 256) return cudaLaunchKernelEx(&cfg, decode_layer_kernel<8>, a);
-    if (a.E <= 512) return cudaLaunchKernelEx(&cfg, decode_layer_kernel<16>, a);
-    return cudaLaunchKernelEx(&cfg, decode_layer_kernel<32>, a);
+    return cudaLaunchKernelEx(&cfg, decode_layer_kernel, a);
 }
 
 }  // namespace smoe
