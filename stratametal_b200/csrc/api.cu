@@ -391,7 +391,6 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
         da.sh_logit = sh_logit;
         da.ids = ids;
         da.w = w;
-        da.xa = xa.base;
         da.ha = ha.base;
         da.xq = trace && trace->xq ? trace->xq : nullptr;
         da.parts = trace ? trace->parts : nullptr;

@@ -3,9 +3,12 @@
 // few megabytes of bytes, so the seven launches of the general path cost more than their work; here the whole
 // block is three phases of one persistent kernel separated by two grid barriers:
 //
-//   phase 0  router logits (warp per expert row, fp64 accumulation) and the activation's q8_1 image
-//   phase 1  every CTA ranks the logits itself (route_cta), then CTAs take (expert slot, 32-row block) items:
-//            32 gate and 32 up row dots, SwiGLU and the q8_1 rule of that block of h
+//   phase 0  router logits (warp per expert row, fp64 accumulation); every CTA writes the activation's q8_1
+//            image into its shared memory; the CTAs past the router rows take the shared expert's
+//            (32-row block) items, which need no routing: 32 gate and 32 up row dots, SwiGLU and the q8_1 rule
+//            of that block of h
+//   phase 1  every CTA ranks the logits itself (route_cta), starts its phase-2 down rows towards L2, then CTAs
+//            take the routed (expert slot, 32-row block) items
 //   phase 2  CTAs take ranges of output rows: for each row the down dot of every slot (one per half-warp: at
 //            n_ff <= 512 the partials fill lanes 0..15, so the xor-16 level of the reference's butterfly adds
 //            zeros and the 16-lane butterfly gives the same bits), then the combine of the row in router order
@@ -13,9 +16,9 @@
 //
 // Every dot follows the reference's order (partial k of 32 values to lane k & 31, in-lane sums in k order, xor
 // butterfly 16..1), the activations use the q8_1 rule and the combine the host's fp64 router-order sum, so the
-// output equals the general path's bit for bit.  The grid barriers are a counter and a generation word in the
-// caller's scratch, zeroed by the host before the launch; every wait is bounded (kWaitLimitNs) and a timeout
-// records kDevTimeout and ends the CTA.  The launch is cooperative, so every CTA is resident.
+// output equals the general path's bit for bit.  The grid barriers share an arrival counter in the caller's
+// scratch, zeroed by the host before the launch; every wait is bounded (kWaitLimitNs) and a timeout records
+// kDevTimeout and ends the CTA.  The launch is cooperative, so every CTA is resident.
 #include "common.cuh"
 #include "kernels.cuh"
 #include "q8.cuh"
@@ -25,6 +28,7 @@ namespace smoe {
 constexpr int kDecThreads = 512;  // 16 warps
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kDecMaxRows = 32;   // output rows per CTA in phase 2 (n_embd <= 4096 over >= 128 CTAs)
+constexpr int kDecMaxBlocks = 128;  // q8_1 blocks of the activation (n_embd <= 4096)
 
 struct DecodeArgs {
     const float* x;
@@ -37,7 +41,6 @@ struct DecodeArgs {
     float* sh_logit;     // [1]
     int32_t* ids;        // [k]
     float* w;            // [k]
-    uint8_t* xa;         // H / 32 activation blocks (KAct layout, Q2_0 order)
     uint8_t* ha;         // (k + 1) x F / 32 blocks of h
     uint8_t* xq;         // optional q8_1 image of x (trace)
     float* parts;        // optional [k][H] routed outputs in router order (trace)
@@ -45,30 +48,29 @@ struct DecodeArgs {
     unsigned* bar;       // [2] arrival count, generation: zero before the launch
 };
 
-// All CTAs meet; false when the wait ran out (the caller then ends the CTA).
-__device__ __forceinline__ bool grid_barrier(unsigned* bar) {
+// All CTAs meet; false when the wait ran out (the caller then ends the CTA).  bar[0] counts arrivals over the
+// whole launch (zeroed by the host before it): barrier number n of the launch completes when it reaches
+// n * gridDim.x.  One release add per CTA, acquire loads while waiting.
+__device__ __forceinline__ bool grid_barrier(unsigned* bar, unsigned n) {
     __syncthreads();
     int ok = 1;
     if (threadIdx.x == 0) {
-        volatile unsigned* gen = bar + 1;
-        const unsigned g = *gen;  // cannot advance before this CTA arrives
-        __threadfence();
-        if (atomicAdd(bar, 1u) + 1u == gridDim.x) {
-            bar[0] = 0;
-            __threadfence();
-            atomicAdd(bar + 1, 1u);
-        } else {
+        const unsigned target = n * gridDim.x;
+        unsigned v;
+        asm volatile("atom.add.release.gpu.u32 %0, [%1], 1;" : "=r"(v) : "l"(bar) : "memory");
+        v += 1;
+        if (v < target) {
             const uint64_t t0 = global_timer_ns();
-            while (*gen == g) {
+            do {
+                asm volatile("ld.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+                if (v >= target) break;
                 if (global_timer_ns() - t0 > kWaitLimitNs) {
                     ok = 0;
                     atomicOr(&g_smoe_status, kDevTimeout);
                     break;
                 }
-                __nanosleep(64);
-            }
+            } while (true);
         }
-        __threadfence();
     }
     return __syncthreads_and(ok) != 0;
 }
@@ -186,18 +188,44 @@ __device__ __forceinline__ void route_cta(const float* __restrict__ l, int E, in
     }
 }
 
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs a) {
     __shared__ int32_t s_ids[kMaxK];
     __shared__ float s_w[kMaxK];
     __shared__ float s_g[32], s_u[32];
     __shared__ float s_parts[kDecMaxRows][kMaxK + 1];
+    __shared__ __align__(16) uint8_t s_xa[kDecMaxBlocks * kKaBlock];  // this CTA's copy of the activation image
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gw = blockIdx.x * kDecWarps + warp, nw = gridDim.x * kDecWarps;
     const int H = a.H, F = a.F, E = a.E, K = a.k;
     const int nslot = K + (a.has_shared ? 1 : 0);
+    const int nb = F / 32;
+    const int rbg = (H / 64) * 18;
 
-    // ---- phase 0: router logits (fp64), activation q8_1 ----
-    for (int r = gw; r < E + (a.has_shared ? 1 : 0); r += nw) {
+    // gate and up rows of one 32-row block of slot s, SwiGLU, the q8_1 block of h (warp w: rows 2w, 2w + 1)
+    auto gate_up_item = [&](int s, int b, const uint8_t* gb, const uint8_t* ub) {
+        const uint8_t* rows[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) rows[q] = (q < 2 ? gb : ub) + (size_t) (b * 32 + 2 * warp + (q & 1)) * rbg;
+        float v[4];
+        row_dot4_warp(rows, s_xa, H, lane, v);
+        if (lane == 0) {
+            s_g[2 * warp] = v[0];
+            s_g[2 * warp + 1] = v[1];
+            s_u[2 * warp] = v[2];
+            s_u[2 * warp + 1] = v[3];
+        }
+        __syncthreads();
+        if (warp == 0)
+            quant_ka_warp(silu_mul(s_g[lane], s_u[lane]), a.ha + ((size_t) s * nb + b) * kKaBlock, lane, true);
+        __syncthreads();
+    };
+
+    // ---- phase 0: the activation image (every CTA, in shared memory), router logits (fp64), and the shared
+    // expert's gate/up, which does not depend on the routing ----
+    const int router_rows = E + (a.has_shared ? 1 : 0);
+    for (int r = gw; r < router_rows; r += nw) {
         const uint16_t* wr = r < E ? a.router + (size_t) r * H : a.ginp;
         double acc = 0.0;
 #pragma unroll 8
@@ -220,14 +248,33 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs
             else a.sh_logit[0] = (float) acc;
         }
     }
-    for (int b = nw - 1 - gw; b < H / 32 && b >= 0; b += nw) {  // the last warps quantize the activation
-        const float xi = a.x[b * 32 + lane];
-        quant_ka_warp(xi, a.xa + (size_t) b * kKaBlock, lane, true);
-        if (a.xq) quant_q8_1_warp(xi, a.xq + (size_t) b * kQ8Block, lane);
+    // the activation image of this CTA (x is read from L2 by every CTA: all loads first)
+    {
+        float xi[kDecMaxBlocks / kDecWarps];
+#pragma unroll
+        for (int i = 0; i < kDecMaxBlocks / kDecWarps; i++) {
+            const int b = warp + kDecWarps * i;
+            xi[i] = b < H / 32 ? a.x[b * 32 + lane] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < kDecMaxBlocks / kDecWarps; i++) {
+            const int b = warp + kDecWarps * i;
+            if (b < H / 32) {
+                quant_ka_warp(xi[i], s_xa + (size_t) b * kKaBlock, lane, true);
+                if (a.xq && blockIdx.x == 0) quant_q8_1_warp(xi[i], a.xq + (size_t) b * kQ8Block, lane);
+            }
+        }
     }
-    if (!grid_barrier(a.bar)) return;
+    __syncthreads();
+    // CTAs past the router rows take the shared expert's blocks (if there are enough CTAs; else phase 1 does)
+    const int r0 = (router_rows + kDecWarps - 1) / kDecWarps;
+    const bool shared_early = a.has_shared && (int) gridDim.x > r0;
+    if (shared_early)
+        for (int it = (int) blockIdx.x - r0; it >= 0 && it < nb; it += (int) gridDim.x - r0)
+            gate_up_item(K, it, a.sgate.base, a.sup.base);
+    if (!grid_barrier(a.bar, 1)) return;
 
-    // ---- phase 1: routing (every CTA), gate/up + SwiGLU + q8_1 per (slot, 32-row block) ----
+    // ---- phase 1: routing (every CTA), routed gate/up + SwiGLU + q8_1 per (slot, 32-row block) ----
     route_cta(a.logits, E, K, s_ids, s_w);
     __syncthreads();
     if (blockIdx.x == 0)
@@ -235,36 +282,26 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs
             a.ids[i] = s_ids[i];
             a.w[i] = s_w[i];
         }
-    const int nb = F / 32;
-    const int rbg = (H / 64) * 18;
-    for (int item = blockIdx.x; item < nslot * nb; item += gridDim.x) {
-        const int s = item / nb, b = item % nb;
-        const bool sh = s >= K;
-        const uint8_t* gb = sh ? a.sgate.base : a.gate.base + (int64_t) s_ids[s] * a.gate.expert_stride;
-        const uint8_t* ub = sh ? a.sup.base : a.up.base + (int64_t) s_ids[s] * a.up.expert_stride;
-        // warp w: rows 2w, 2w + 1 of the block, gate then up
-        const uint8_t* rows[4];
-#pragma unroll
-        for (int q = 0; q < 4; q++) rows[q] = (q < 2 ? gb : ub) + (size_t) (b * 32 + 2 * warp + (q & 1)) * rbg;
-        float v[4];
-        row_dot4_warp(rows, a.xa, H, lane, v);
-        if (lane == 0) {
-            s_g[2 * warp] = v[0];
-            s_g[2 * warp + 1] = v[1];
-            s_u[2 * warp] = v[2];
-            s_u[2 * warp + 1] = v[3];
-        }
-        __syncthreads();
-        if (warp == 0)
-            quant_ka_warp(silu_mul(s_g[lane], s_u[lane]), a.ha + ((size_t) s * nb + b) * kKaBlock, lane, true);
-        __syncthreads();
-    }
-    if (!grid_barrier(a.bar)) return;
-
-    // ---- phase 2: down dots by output row range, then the combine of each row ----
+    // start this CTA's phase-2 down rows on their way to L2
     const int rows_per = (H + gridDim.x - 1) / gridDim.x;
     const int j0 = blockIdx.x * rows_per, nj = max(0, min(rows_per, H - j0));
     const int rbd = (F / 64) * 18;
+    for (int u = threadIdx.x; u < nslot * nj; u += blockDim.x) {
+        const int s = u % nslot, jl = u / nslot;
+        const uint8_t* row = (s >= K ? a.sdown.base : a.down.base + (int64_t) s_ids[s] * a.down.expert_stride) +
+                             (size_t) (j0 + jl) * rbd;
+        for (int off = 0; off < rbd; off += 128) prefetch_l2(row + off);
+    }
+    const int n_items = (shared_early ? K : nslot) * nb;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const int s = item / nb, b = item % nb;
+        const bool sh = s >= K;
+        gate_up_item(s, b, sh ? a.sgate.base : a.gate.base + (int64_t) s_ids[s] * a.gate.expert_stride,
+                     sh ? a.sup.base : a.up.base + (int64_t) s_ids[s] * a.up.expert_stride);
+    }
+    if (!grid_barrier(a.bar, 2)) return;
+
+    // ---- phase 2: down dots by output row range, then the combine of each row ----
     const int hl = lane & 15, half = lane >> 4;
     const int n_dots = nj * nslot;
     constexpr int kBatch = 3;  // dots per half-warp with their loads in flight together
