@@ -12,8 +12,10 @@ forward; for configs[3] one graph for the whole 48-layer stack with its residual
 replays, then exactly K replays between CUDA events on the replay stream, bracketed by a barrier and a
 synchronize, max over ranks.  Per-stage times come from a separate eager pass with stage events.  Each step's
 expert bytes (~200 MB at 64 tokens) exceed the 126 MB L2 and the steps rotate over --layers distinct seeded
-layers, so weights stream from HBM.  Rank 0 prints one JSON line.  N > 1 runs independent replicas (decode
-does not shard: "replicas only"), value = all ranks' tokens / time.
+layers, so weights stream from HBM.  Rank 0 prints one JSON line.  N > 1 runs independent replicas for the
+decode configs (decode does not shard: "replicas only"), value = all ranks' tokens / time; configs[2] and
+configs[3] at batch 16 run expert-parallel instead: the step's tokens split over the N ranks, E / N experts per
+rank, token rows and down rows exchanged over peer memory inside smoe_ep_forward (strong scaling).
 
   python bench.py --config 3 [--tokens 16]    # the 48-layer stack at batch 1 (or 16)
   python bench.py --config 2                  # 4096-token prefill (tensor-core expert kernels)
@@ -298,12 +300,26 @@ def run_ours(args, ws, rank, local):
     H = spec.n_embd
     stack = args.config == 3
     n_layers = STACK_LAYERS if stack else args.layers
-    api.set_expert_path(args.expert_path)
-    layers = [api.MoeLayer(synth.make_layer(spec, li, dev), T, dev) for li in range(n_layers)]
-    path = lib().smoe_expert_path_for(C.byref(layers[0].c), T)
-    tc, fused = path == 2, path == 3
     n_batches = 1 if stack else 4
-    xs = [synth.make_x(spec.seed + 1000 * local, T, H, dev, stream=b) for b in range(n_batches)]
+    api.set_expert_path(args.expert_path)
+    # expert parallelism for the batched and prefill workloads on N > 1 GPUs: the step's tokens split evenly over
+    # the ranks (strong scaling), E / N routed experts per rank, the exchange inside smoe_ep_forward
+    ep_mode = ws > 1 and (args.config == 2 or (stack and T > 1))
+    if ep_mode:
+        from stratametal_b200 import ep
+        if T % ws:
+            raise SystemExit(f"{T} tokens do not split over {ws} ranks")
+        T_all, T = T, T // ws
+        areas = ep.EpAreas.distributed(spec, T)
+        layers = [ep.EpLayer(ep.shard_layer(spec, li, rank, ws, dev), areas, dev) for li in range(n_layers)]
+        path = lib().smoe_expert_path_for(C.byref(layers[0].c), T_all)
+        xs = [synth.make_x(spec.seed, T_all, H, dev, stream=b)[rank * T:(rank + 1) * T].contiguous()
+              for b in range(n_batches)]
+    else:
+        layers = [api.MoeLayer(synth.make_layer(spec, li, dev), T, dev) for li in range(n_layers)]
+        path = lib().smoe_expert_path_for(C.byref(layers[0].c), T)
+        xs = [synth.make_x(spec.seed + 1000 * local, T, H, dev, stream=b) for b in range(n_batches)]
+    tc, fused = path == 2, path == 3
     out = torch.empty(T, H, device=dev)
     stream = torch.cuda.current_stream()
     # the stack ping-pongs between two buffers: layer l reads cur, writes MoE(cur) to nxt, then
@@ -330,7 +346,15 @@ def run_ours(args, ws, rank, local):
             tr = m.make_trace(T)
             xin = cur if stack else xs[b]
             m.forward(xin, out, tr)
-            D[(li, b)] = int(torch.unique(tr.ids).numel())
+            if ep_mode:  # the experts of this rank that any rank's tokens reach
+                import torch.distributed as dist
+                allids = [torch.empty_like(tr.ids) for _ in range(ws)]
+                dist.all_gather(allids, tr.ids)
+                u = torch.unique(torch.cat(allids))
+                lo_e = rank * (spec.n_expert // ws)
+                D[(li, b)] = int(((u >= lo_e) & (u < lo_e + spec.n_expert // ws)).sum())
+            else:
+                D[(li, b)] = int(torch.unique(tr.ids).numel())
             if stack:  # follow the stack's own activations
                 api.add_rms_norm(out, xin, None, T, H, RMS_EPS)
                 cur = out.clone()
@@ -396,7 +420,7 @@ def run_ours(args, ws, rank, local):
     rbg = synth.row_bytes(spec.gu_type, spec.n_embd) * spec.n_ff
     rbd = synth.row_bytes(spec.d_type, spec.n_ff) * spec.n_embd
     q8x, q8h = (spec.n_embd // 32) * 36, (spec.n_ff // 32) * 36
-    rows = T * spec.k + T
+    rows = T * spec.k + T  # slots per rank (in expectation the same with expert parallelism)
     if stack:
         Ds = [D[(li, 0)] for li in range(n_layers)]
         step_bytes = float(sum((d + 1) * E_BYTES for d in Ds))
@@ -470,14 +494,23 @@ def run_ours(args, ws, rank, local):
             per_fwd += 2
         if fused:
             per_fwd = 1
+        if ep_mode:  # + dispatch, receive and the done-wait; grouping over the ws * T received rows
+            per_fwd = (7 if tc else 8) + 3 + (2 if ws * T > 256 else 0)
         launches_per_step = n_layers * (per_fwd + 1) if stack else per_fwd
+        cfgd = config_dict(args, spec, T_all if ep_mode else T, D_mean, n_layers, stack)
+        if ep_mode:
+            cfgd["parallelism"] = (f"expert parallel x{ws}: {spec.n_expert // ws} routed experts and {T} of the "
+                                   f"{T_all} tokens per GPU; dispatch and return over peer memory (CUDA IPC, "
+                                   f"NVLink), no collective on the data path")
+            cfgd["distinct_experts_per_step"] = f"{D_mean} on rank 0 (of its {spec.n_expert // ws})"
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
-                "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": "strong" if ep_mode else "weak", "vs_baseline": None,
                 "dtype": ("fp16 x fp16 tcgen05 (exact hi/lo q8_1 image), f32 accumulate" if tc
                           else "int8 x int2 dot (q8_1 contract), f32/f64 sums"), "data": "synthetic",
                 "expert_path": ("tensor cores (tcgen05)" if tc else "fused single-token kernel (one cooperative launch)"
                                 if fused else "SIMT"),
-                "config": config_dict(args, spec, T, D_mean, n_layers, stack),
+                "config": cfgd,
                 "timing": "CUDA events around CUDA-graph replays (one captured forward per step"
                           + (", the whole 48-layer stack" if stack else "") + ")",
                 "expert_weight_gbs": expert_gbs, "expert_weight_frac_of_peak": expert_gbs / hbm_peak,
@@ -485,6 +518,11 @@ def run_ours(args, ws, rank, local):
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": K * launches_per_step,
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
+    if ep_mode:  # every rank's kernels are done before any rank unmaps or frees an exchange area
+        del graphs
+        torch.cuda.synchronize()
+        barrier(ws)
+        areas.close()
 
 
 def main():

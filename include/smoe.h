@@ -190,6 +190,47 @@ size_t smoe_moe_scratch_bytes(const smoe_layer* L, int max_tokens);
 smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, float* out, void* scratch,
                              size_t scratch_bytes, const smoe_trace* trace, void* stream);
 
+/* ---- Expert parallelism over the GPUs of one node (no reference counterpart: the reference reaches a second
+ * GPU only through its peer / remote expert tiers, include/strata/core/peer_experts.hpp:35-104, which this
+ * replaces for the MoE block).  Rank r of `world` holds the router and the shared expert whole and the routed
+ * experts [r * E / world, (r + 1) * E / world); each rank routes its own tokens, sends each token's q8_1 row
+ * once to every rank that owns one of its experts, the owners run their experts and store every routed slot's
+ * down row straight into the token rank's exchange area, and the token's rank combines in router order.  The
+ * exchange areas are mapped into every process (CUDA IPC); the data path uses no collective library.
+ * Results equal smoe_moe_forward's on the same tokens bit for bit (the same kernels, the same orders). */
+enum { SMOE_EP_MAX_WORLD = 8, SMOE_EP_HANDLE_BYTES = 64 };
+
+typedef struct smoe_ep {
+    int rank;        /* this process's rank, 0 <= rank < world */
+    int world;       /* ranks (GPUs), 1..SMOE_EP_MAX_WORLD; n_expert % world == 0 */
+    int max_tokens;  /* tokens per rank and step, at most; the same on every rank */
+    void* areas[SMOE_EP_MAX_WORLD]; /* every rank's exchange area as this process addresses it (own at [rank]) */
+} smoe_ep;
+
+/* Bytes of one rank's exchange area (the same on every rank). */
+size_t smoe_ep_area_bytes(const smoe_layer* L, int max_tokens, int world);
+/* Set-up, not the token path: allocates a zeroed exchange area on the current device and, when ipc_handle is
+ * not NULL, writes its SMOE_EP_HANDLE_BYTES-byte IPC handle there for the other processes. */
+smoe_status smoe_ep_area_alloc(size_t bytes, void** area, void* ipc_handle);
+/* Maps another process's area from its handle (peer access over NVLink), and unmaps it. */
+smoe_status smoe_ep_area_open(const void* ipc_handle, void** area);
+smoe_status smoe_ep_area_close(void* area);
+smoe_status smoe_ep_area_free(void* area);
+/* Once per rank after every area exists (and before any rank's first step): records this rank's view of the
+ * areas in its own.  L->n_expert is the whole pool; L->gate / up / down hold this rank's experts. */
+smoe_status smoe_ep_init(const smoe_ep* ep, const smoe_layer* L);
+/* Local scratch of smoe_ep_forward. */
+size_t smoe_ep_scratch_bytes(const smoe_layer* L, const smoe_ep* ep);
+/* The MoE block of this rank's n_tokens tokens (0 <= n_tokens <= max_tokens; 0 still takes part in the
+ * exchange): every rank calls it once per step, in the same order.  phases: 1 route + dispatch, 2 receive +
+ * experts, 4 wait + combine, ORed; 7 is a whole step.  A caller that drives several ranks from one process on
+ * one device runs phase 1 of every rank, then 2 of every rank, then 4, so that no kernel ever waits for one
+ * launched after it.  Waits are bounded: a rank that does not take part makes the others record
+ * SMOE_DEVICE_TIMEOUT in the status word within seconds.  Layers whose shared expert types differ from the
+ * routed ones, and n_embd not a multiple of 128, are SMOE_UNSUPPORTED. */
+smoe_status smoe_ep_forward(const smoe_layer* L, const smoe_ep* ep, const float* x, int n_tokens, float* out,
+                            void* scratch, size_t scratch_bytes, const smoe_trace* trace, int phases, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

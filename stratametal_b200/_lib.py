@@ -29,6 +29,14 @@ class SmoeTrace(C.Structure):
     _fields_ = [("logits", _vp), ("ids", _vp), ("weights", _vp), ("xq", _vp), ("parts", _vp), ("shared", _vp)]
 
 
+EP_MAX_WORLD = 8
+EP_HANDLE_BYTES = 64
+
+
+class SmoeEp(C.Structure):
+    _fields_ = [("rank", C.c_int), ("world", C.c_int), ("max_tokens", C.c_int), ("areas", _vp * EP_MAX_WORLD)]
+
+
 # name -> (restype, argtypes); every symbol include/smoe.h declares
 SIGNATURES = {
     "smoe_last_error": (C.c_char_p, []),
@@ -55,6 +63,15 @@ SIGNATURES = {
     "smoe_moe_scratch_bytes": (C.c_size_t, [C.POINTER(SmoeLayer), C.c_int]),
     "smoe_moe_forward": (C.c_int, [C.POINTER(SmoeLayer), _vp, C.c_int, _vp, _vp, C.c_size_t,
                                    C.POINTER(SmoeTrace), _vp]),
+    "smoe_ep_area_bytes": (C.c_size_t, [C.POINTER(SmoeLayer), C.c_int, C.c_int]),
+    "smoe_ep_area_alloc": (C.c_int, [C.c_size_t, C.POINTER(_vp), _vp]),
+    "smoe_ep_area_open": (C.c_int, [_vp, C.POINTER(_vp)]),
+    "smoe_ep_area_close": (C.c_int, [_vp]),
+    "smoe_ep_area_free": (C.c_int, [_vp]),
+    "smoe_ep_init": (C.c_int, [C.POINTER(SmoeEp), C.POINTER(SmoeLayer)]),
+    "smoe_ep_scratch_bytes": (C.c_size_t, [C.POINTER(SmoeLayer), C.POINTER(SmoeEp)]),
+    "smoe_ep_forward": (C.c_int, [C.POINTER(SmoeLayer), C.POINTER(SmoeEp), _vp, C.c_int, _vp, _vp, C.c_size_t,
+                                  C.POINTER(SmoeTrace), C.c_int, _vp]),
 }
 
 _lib: C.CDLL | None = None

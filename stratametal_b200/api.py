@@ -110,6 +110,41 @@ class Trace:
     shared: torch.Tensor
 
 
+def layer_struct(t: dict, sp: synth.LayerSpec) -> SmoeLayer:
+    """The C ABI's layer descriptor over device tensors keyed by their GGUF names."""
+    c = SmoeLayer()
+    c.n_embd, c.n_ff, c.n_expert, c.k = sp.n_embd, sp.n_ff, sp.n_expert, sp.k
+    c.gu_type, c.d_type = sp.gu_type, sp.d_type
+    c.router = _p(t["ffn_gate_inp.weight"])
+    c.gate = _p(t["ffn_gate_exps.weight"])
+    c.up = _p(t["ffn_up_exps.weight"])
+    c.down = _p(t["ffn_down_exps.weight"])
+    if sp.has_shared:
+        c.has_shared = 1
+        c.sg_type, c.su_type, c.sd_type = sp.sg_type, sp.su_type, sp.sd_type
+        c.sgate = _p(t["ffn_gate_shexp.weight"])
+        c.sup = _p(t["ffn_up_shexp.weight"])
+        c.sdown = _p(t["ffn_down_shexp.weight"])
+        c.gate_inp_shexp = _p(t["ffn_gate_inp_shexp.weight"])
+    return c
+
+
+def trace_struct(trace: "Trace | None") -> SmoeTrace | None:
+    if trace is None:
+        return None
+    return SmoeTrace(_p(trace.logits), _p(trace.ids), _p(trace.weights), _p(trace.xq), _p(trace.parts),
+                     _p(trace.shared))
+
+
+def make_trace(sp: synth.LayerSpec, T: int, device) -> "Trace":
+    return Trace(logits=torch.empty(T, sp.n_expert, dtype=torch.float32, device=device),
+                 ids=torch.empty(T, sp.k, dtype=torch.int32, device=device),
+                 weights=torch.empty(T, sp.k, dtype=torch.float32, device=device),
+                 xq=torch.empty(T, q8_1_bytes(sp.n_embd), dtype=torch.uint8, device=device),
+                 parts=torch.empty(T, sp.k, sp.n_embd, dtype=torch.float32, device=device),
+                 shared=torch.zeros(T, sp.n_embd, dtype=torch.float32, device=device))
+
+
 class MoeLayer:
     """One MoE layer resident on the device plus its scratch arena; `forward` is smoe_moe_forward."""
 
@@ -118,20 +153,7 @@ class MoeLayer:
         self.spec = sp
         self.device = torch.device(device)
         self.t = {k: v.to(self.device).contiguous() for k, v in layer.tensors.items()}
-        c = SmoeLayer()
-        c.n_embd, c.n_ff, c.n_expert, c.k = sp.n_embd, sp.n_ff, sp.n_expert, sp.k
-        c.gu_type, c.d_type = sp.gu_type, sp.d_type
-        c.router = _p(self.t["ffn_gate_inp.weight"])
-        c.gate = _p(self.t["ffn_gate_exps.weight"])
-        c.up = _p(self.t["ffn_up_exps.weight"])
-        c.down = _p(self.t["ffn_down_exps.weight"])
-        if sp.has_shared:
-            c.has_shared = 1
-            c.sg_type, c.su_type, c.sd_type = sp.sg_type, sp.su_type, sp.sd_type
-            c.sgate = _p(self.t["ffn_gate_shexp.weight"])
-            c.sup = _p(self.t["ffn_up_shexp.weight"])
-            c.sdown = _p(self.t["ffn_down_shexp.weight"])
-            c.gate_inp_shexp = _p(self.t["ffn_gate_inp_shexp.weight"])
+        c = layer_struct(self.t, sp)
         self.c = c
         check(lib().smoe_layer_check(c))
         self.max_tokens = max_tokens
@@ -142,13 +164,7 @@ class MoeLayer:
         self.scratch_bytes = nbytes
 
     def make_trace(self, T: int) -> Trace:
-        sp, d = self.spec, self.device
-        return Trace(logits=torch.empty(T, sp.n_expert, dtype=torch.float32, device=d),
-                     ids=torch.empty(T, sp.k, dtype=torch.int32, device=d),
-                     weights=torch.empty(T, sp.k, dtype=torch.float32, device=d),
-                     xq=torch.empty(T, q8_1_bytes(sp.n_embd), dtype=torch.uint8, device=d),
-                     parts=torch.empty(T, sp.k, sp.n_embd, dtype=torch.float32, device=d),
-                     shared=torch.zeros(T, sp.n_embd, dtype=torch.float32, device=d))
+        return make_trace(self.spec, T, self.device)
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, trace: Trace | None = None) -> torch.Tensor:
         T = x.shape[0]
@@ -156,10 +172,7 @@ class MoeLayer:
             raise SmoeError(1, f"{T} tokens exceed the arena's {self.max_tokens}")
         if out is None:
             out = torch.empty(T, self.spec.n_embd, dtype=torch.float32, device=self.device)
-        tr = None
-        if trace is not None:
-            tr = SmoeTrace(_p(trace.logits), _p(trace.ids), _p(trace.weights), _p(trace.xq), _p(trace.parts),
-                           _p(trace.shared))
+        tr = trace_struct(trace)
         import ctypes as C
         check(lib().smoe_moe_forward(C.byref(self.c), _p(x), T, _p(out), self.scratch_ptr, self.scratch_bytes,
                                      C.byref(tr) if tr is not None else None, _s()))

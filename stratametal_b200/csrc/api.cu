@@ -5,6 +5,7 @@
 #include "kernels.cuh"
 
 #include <atomic>
+#include <cstring>
 #include <string>
 
 namespace smoe {
@@ -133,6 +134,64 @@ smoe_status check_layer(const smoe_layer* L) {
             !aligned(L->gate_inp_shexp, 16))
             return fail(SMOE_INVALID_ARG, "layer: shared planes must be 16-byte aligned");
     }
+    return SMOE_OK;
+}
+
+// Local scratch of the expert-parallel block: this rank's tokens (T = max_tokens) on the router side, the
+// received rows (R = world * max_tokens) and this rank's n_local experts on the expert side.
+struct EpLayout {
+    size_t xq, logits, sh_logit, ids, w, shared;                                       // token side
+    size_t oids, slot, slot_token, slot_pair, tables, sched, chunk, xa, gu, ha;        // expert side, SIMT
+    size_t sched_tc, xh, hh;                                                           // tensor cores
+    size_t total;
+};
+
+EpLayout ep_layout_of(const smoe_layer* L, const smoe_ep* ep) {
+    EpLayout o;
+    const size_t H = (size_t) L->n_embd, F = (size_t) L->n_ff, K = (size_t) L->k;
+    const int T = ep->max_tokens, R = ep->world * ep->max_tokens, El = L->n_expert / ep->world;
+    const size_t rows = (size_t) R * K + (L->has_shared ? (size_t) T : 0);
+    size_t at = 0;
+    o.xq = at; at += up256((size_t) T * (H / 32) * kQ8Block);
+    o.logits = at; at += up256((size_t) T * L->n_expert * 4);
+    o.sh_logit = at; at += up256((size_t) T * 4);
+    o.ids = at; at += up256((size_t) T * K * 4);
+    o.w = at; at += up256((size_t) T * K * 4);
+    o.shared = at; at += up256((size_t) T * H * 4);
+    o.oids = at; at += up256((size_t) R * K * 4);
+    o.slot = at; at += up256((size_t) R * K * 4);
+    o.slot_token = at; at += up256((size_t) R * K * 4);
+    o.slot_pair = at; at += up256((size_t) R * K * 4);
+    o.tables = at; at += group_tables_bytes(El);
+    o.sched = at; at += sched_bytes(El, R, (int) K);
+    o.chunk = at; at += group_chunk_bytes(R, El);
+    o.xa = at; at += up256(ka_bytes(R, (int) (H / 32)));
+    o.gu = at; at += up256(rows * 2 * F * 4);
+    o.ha = at; at += up256(ka_bytes((int64_t) rows, (int) (F / 32)));
+    o.sched_tc = o.xh = o.hh = at;
+    if (tc_qualifies(L)) {
+        o.sched_tc = at; at += sched_bytes(El, R, (int) K, kTcChunk);
+        o.xh = at; at += up256((size_t) 2 * R * H * 2);
+        o.hh = at; at += up256(rows * 2 * F * 2);
+    }
+    o.total = at;
+    return o;
+}
+
+smoe_status check_ep(const smoe_layer* L, const smoe_ep* ep) {
+    smoe_status st = check_layer(L);
+    if (st != SMOE_OK) return st;
+    if (!ep) return fail(SMOE_INVALID_ARG, "ep: descriptor is null");
+    if (ep->world < 1 || ep->world > SMOE_EP_MAX_WORLD || ep->rank < 0 || ep->rank >= ep->world)
+        return fail(SMOE_INVALID_ARG, "ep: need 1 <= world <= 8 and 0 <= rank < world");
+    if (ep->max_tokens < 1) return fail(SMOE_INVALID_ARG, "ep: max_tokens must be positive");
+    if (L->n_expert % ep->world) return fail(SMOE_INVALID_ARG, "ep: n_expert must be a multiple of world");
+    if (L->n_expert / ep->world < 1) return fail(SMOE_INVALID_ARG, "ep: no experts per rank");
+    if (L->n_embd % 128) return fail(SMOE_UNSUPPORTED, "ep: n_embd must be a multiple of 128");
+    if (L->has_shared && (L->sg_type != L->gu_type || L->su_type != L->gu_type || L->sd_type != L->d_type))
+        return fail(SMOE_UNSUPPORTED, "ep: the shared expert's types must equal the routed ones");
+    for (int p = 0; p < ep->world; p++)
+        if (!ep->areas[p] || !aligned(ep->areas[p], 256)) return fail(SMOE_INVALID_ARG, "ep: an area is null or unaligned");
     return SMOE_OK;
 }
 
@@ -513,6 +572,185 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
             e = cudaMemcpyAsync(trace->xq, xq, (size_t) T * (H / 32) * kQ8Block, cudaMemcpyDeviceToDevice, s);
         if (e == cudaSuccess && trace->parts) e = launch_gather_parts(parts, slot, trace->parts, H, K, T, s);
         if (e != cudaSuccess) return cuda_fail(e, "moe_forward: trace");
+    }
+    return ok();
+}
+
+size_t smoe_ep_area_bytes(const smoe_layer* L, int max_tokens, int world) {
+    // geometry only (n_embd, k): the area does not depend on the planes
+    if (!L || L->n_embd <= 0 || L->n_embd % 128 || L->k <= 0 || L->k > kMaxK || max_tokens < 1 || world < 1 ||
+        world > SMOE_EP_MAX_WORLD)
+        return 0;
+    return ep_arena_bytes(L->n_embd, L->k, max_tokens, world);
+}
+
+smoe_status smoe_ep_area_alloc(size_t bytes, void** area, void* ipc_handle) {
+    if (!area || bytes == 0) return fail(SMOE_INVALID_ARG, "ep_area_alloc: null result pointer or zero size");
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess && ipc_handle) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        return cuda_fail(e, "ep_area_alloc");
+    }
+    *area = p;
+    return ok();
+}
+
+smoe_status smoe_ep_area_open(const void* ipc_handle, void** area) {
+    if (!ipc_handle || !area) return fail(SMOE_INVALID_ARG, "ep_area_open: null argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof h);
+    const cudaError_t e = cudaIpcOpenMemHandle(area, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "ep_area_open");
+}
+
+smoe_status smoe_ep_area_close(void* area) {
+    const cudaError_t e = cudaIpcCloseMemHandle(area);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "ep_area_close");
+}
+
+smoe_status smoe_ep_area_free(void* area) {
+    const cudaError_t e = cudaFree(area);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "ep_area_free");
+}
+
+smoe_status smoe_ep_init(const smoe_ep* ep, const smoe_layer* L) {
+    const smoe_status st = check_ep(L, ep);
+    if (st != SMOE_OK) return st;
+    const cudaError_t e = ep_init(ep->areas[ep->rank], ep->areas, ep->rank, ep->world, L->n_embd, L->k, ep->max_tokens);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "ep_init");
+}
+
+size_t smoe_ep_scratch_bytes(const smoe_layer* L, const smoe_ep* ep) {
+    if (check_ep(L, ep) != SMOE_OK) return 0;
+    return ep_layout_of(L, ep).total;
+}
+
+smoe_status smoe_ep_forward(const smoe_layer* L, const smoe_ep* ep, const float* x, int n_tokens, float* out,
+                            void* scratch, size_t scratch_bytes, const smoe_trace* trace, int phases, void* stream) {
+    smoe_status st = check_ep(L, ep);
+    if (st != SMOE_OK) return st;
+    if (n_tokens < 0 || n_tokens > ep->max_tokens) return fail(SMOE_INVALID_ARG, "ep_forward: need 0 <= n_tokens <= max_tokens");
+    if (phases < 1 || phases > 7) return fail(SMOE_INVALID_ARG, "ep_forward: phases must be 1..7");
+    if (!stream) return fail(SMOE_INVALID_ARG, "ep_forward: a non-null stream is required");
+    if (!scratch || !aligned(scratch, 256)) return fail(SMOE_INVALID_ARG, "ep_forward: scratch null or not 256-byte aligned");
+    if (n_tokens > 0 && ((phases & 1) && (!x || !aligned(x, 16)))) return fail(SMOE_INVALID_ARG, "ep_forward: x null or unaligned");
+    if (n_tokens > 0 && (phases & 4) && !out) return fail(SMOE_INVALID_ARG, "ep_forward: out is null");
+    const EpLayout lo = ep_layout_of(L, ep);
+    if (scratch_bytes < lo.total) return fail(SMOE_INVALID_ARG, "ep_forward: scratch is too small");
+    cudaStream_t s = (cudaStream_t) stream;
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    void* area = ep->areas[ep->rank];
+    const int T = n_tokens, H = L->n_embd, F = L->n_ff, E = L->n_expert, K = L->k;
+    const int G = ep->world, Tm = ep->max_tokens, R = G * Tm, El = E / G;
+    const bool sh = L->has_shared != 0;
+    const int rows = R * K + (sh ? Tm : 0);
+    uint8_t* xq = base + lo.xq;
+    float* logits = reinterpret_cast<float*>(base + lo.logits);
+    float* sh_logit = reinterpret_cast<float*>(base + lo.sh_logit);
+    int32_t* ids = reinterpret_cast<int32_t*>(base + lo.ids);
+    float* w = reinterpret_cast<float*>(base + lo.w);
+    float* shared_rows = reinterpret_cast<float*>(base + lo.shared);
+    const bool tc = use_tc(L, R);
+    cudaError_t e = cudaSuccess;
+
+    if (phases & 1) {
+        if (T > 0) {
+            e = launch_bf16_gemv(x, true, L->router, sh ? L->gate_inp_shexp : nullptr, logits, sh_logit, T, H, E, s);
+            if (e == cudaSuccess) e = mark(0, s);
+            if (e == cudaSuccess) e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, nullptr, 1);
+            if (e == cudaSuccess) e = mark(1, s);
+            if (e != cudaSuccess) return cuda_fail(e, "ep_forward: router");
+        }
+        e = launch_ep_dispatch(area, ids, xq, T, K, H, El, s);
+        if (e == cudaSuccess) e = mark(2, s);
+        if (e != cudaSuccess) return cuda_fail(e, "ep_forward: dispatch");
+    }
+
+    if (phases & 2) {
+        int32_t* oids = reinterpret_cast<int32_t*>(base + lo.oids);
+        int32_t* slot = reinterpret_cast<int32_t*>(base + lo.slot);
+        int32_t* slot_tok = reinterpret_cast<int32_t*>(base + lo.slot_token);
+        int32_t* slot_pair = reinterpret_cast<int32_t*>(base + lo.slot_pair);
+        const GroupTables tabs = group_tables_at(base + lo.tables, El);
+        const KAct xa = ka_at(base + lo.xa, R, H / 32);
+        __half* xh = reinterpret_cast<__half*>(base + lo.xh);
+        e = launch_ep_receive(area, K, H, ep->rank * El, El, oids, tc ? nullptr : &xa, L->gu_type == kQ2_0,
+                              tc ? xh : nullptr, s, R);
+        if (e != cudaSuccess) return cuda_fail(e, "ep_forward: receive");
+        const Sched sc = tc ? sched_at(base + lo.sched_tc, El, R, K, kTcChunk) : sched_at(base + lo.sched, El, R, K);
+        e = launch_group(oids, R, K, El, tabs, slot, slot_tok, s, &sc, reinterpret_cast<int32_t*>(base + lo.chunk), 1,
+                         slot_pair);
+        if (e != cudaSuccess) return cuda_fail(e, "ep_forward: grouping");
+        Work wk{};
+        wk.sched = sc;
+        wk.slot_token = slot_tok;
+        wk.max_entries = tc ? sched_capacity(El, R, K, kTcChunk) : sched_capacity(El, R, K);
+        wk.shared_base = R * K;
+        wk.shared_slots = sh ? T : 0;
+        wk.slot_pair = slot_pair;
+        wk.ep_out = ep_parts_table(area);
+        wk.ep_shared = shared_rows;
+        wk.ep_rows = Tm;
+        wk.ep_k = K;
+        const int64_t gu_stride = (int64_t) F * (int64_t) row_bytes(L->gu_type, H);
+        const int64_t d_stride = (int64_t) H * (int64_t) row_bytes(L->d_type, F);
+        const Matrix mg{L->gate, gu_stride, L->gu_type}, mu{L->up, gu_stride, L->gu_type}, md{L->down, d_stride, L->d_type};
+        const Matrix sg{L->sgate, 0, L->sg_type}, su{L->sup, 0, L->su_type}, sd{L->sdown, 0, L->sd_type};
+        EpDone done;
+        done.counter = ep_done_counter(area);
+        done.flags = ep_done_table(area);
+        done.world = G;
+        if (tc) {
+            __half* hh = reinterpret_cast<__half*>(base + lo.hh);
+            e = launch_tc_gate_up(mg, mu, sg, su, wk, El, xh, R, hh, rows, H, F, s);
+            if (e == cudaSuccess) e = mark(3, s);
+            if (e != cudaSuccess) return cuda_fail(e, "ep_forward: gate/up (tensor cores)");
+            wk.ep_done = done;
+            e = launch_tc_down(md, sd, wk, El, hh, rows, nullptr, F, H, s);
+            if (e == cudaSuccess) e = mark(4, s);
+            if (e != cudaSuccess) return cuda_fail(e, "ep_forward: down (tensor cores)");
+        } else {
+            float* gu = reinterpret_cast<float*>(base + lo.gu);
+            const KAct ha = ka_at(base + lo.ha, rows, F / 32);
+            Work w1 = wk;
+            w1.counter = tabs.work + 0;
+            e = launch_layer_gate_up(mg, mu, sg, su, w1, xa, gu, H, F, s);
+            if (e == cudaSuccess) e = launch_swiglu_ka(gu, ha, rows, F, L->d_type == kQ2_0, s);
+            if (e == cudaSuccess) e = mark(3, s);
+            if (e != cudaSuccess) return cuda_fail(e, "ep_forward: gate/up");
+            Work w3 = wk;
+            w3.counter = tabs.work + 2;
+            w3.ep_done = done;
+            e = launch_layer_down(md, sd, w3, ha, nullptr, F, H, s);
+            if (e == cudaSuccess) e = mark(4, s);
+            if (e != cudaSuccess) return cuda_fail(e, "ep_forward: down");
+        }
+    }
+
+    if (phases & 4) {
+        e = launch_ep_wait_done(area, s);
+        float* parts = ep_parts(area, H, K, Tm, G);
+        if (e == cudaSuccess && T > 0)
+            e = launch_combine(parts, nullptr, w, sh ? shared_rows : nullptr, sh ? sh_logit : nullptr, out,
+                               trace ? trace->shared : nullptr, H, K, T, H, s);
+        if (e == cudaSuccess) e = mark(5, s);
+        if (e != cudaSuccess) return cuda_fail(e, "ep_forward: combine");
+        if (trace && T > 0) {
+            if (trace->logits) e = cudaMemcpyAsync(trace->logits, logits, (size_t) T * E * 4, cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && trace->ids)
+                e = cudaMemcpyAsync(trace->ids, ids, (size_t) T * K * 4, cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && trace->weights)
+                e = cudaMemcpyAsync(trace->weights, w, (size_t) T * K * 4, cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && trace->xq)
+                e = cudaMemcpyAsync(trace->xq, xq, (size_t) T * (H / 32) * kQ8Block, cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && trace->parts)
+                e = cudaMemcpyAsync(trace->parts, parts, (size_t) T * K * H * 4, cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(e, "ep_forward: trace");
+        }
     }
     return ok();
 }

@@ -130,7 +130,8 @@ __device__ void build_sched(GroupTables g, Sched sched, int E, int* warp_sums) {
 
 __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__ ids, int T, int k, int E,
                                                      GroupTables g, int32_t* __restrict__ slot,
-                                                     int32_t* __restrict__ src, Sched sched, int with_sched) {
+                                                     int32_t* __restrict__ src, Sched sched, int with_sched,
+                                                     int skip_negative, int32_t* __restrict__ pair) {
     __shared__ unsigned long long mask[kMaxExperts];
     __shared__ int run[kMaxExperts];
     __shared__ int warp_sums[32];
@@ -157,12 +158,13 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__
                     const int e = ids[i];
                     if (e < 0 || e >= E) {
                         slot[i] = -1;
-                        atomicOr(&g_smoe_status, kDevBadId);
+                        if (!(skip_negative && e < 0)) atomicOr(&g_smoe_status, kDevBadId);
                         continue;
                     }
                     const int pos = run[e] + __popcll(mask[e] & ((1ull << tl) - 1ull));
                     slot[i] = pos;
                     if (src) src[pos] = t0 + tl;
+                    if (pair) pair[pos] = (int) i;
                 }
                 __syncthreads();
             }
@@ -249,7 +251,8 @@ __global__ void __launch_bounds__(1024) group_scan_kernel(int E, int nchunks, in
 
 __global__ void __launch_bounds__(256) group_assign_kernel(const int32_t* __restrict__ ids, int T, int k, int E,
                                                            const int32_t* __restrict__ cc, int32_t* __restrict__ slot,
-                                                           int32_t* __restrict__ src) {
+                                                           int32_t* __restrict__ src, int skip_negative,
+                                                           int32_t* __restrict__ pair) {
     __shared__ unsigned long long mask[kMaxExperts];
     const int c = blockIdx.x, t0 = c * 64, nt = min(64, T - t0);
     for (int e = threadIdx.x; e < E; e += blockDim.x) mask[e] = 0ull;
@@ -265,27 +268,29 @@ __global__ void __launch_bounds__(256) group_assign_kernel(const int32_t* __rest
         const int e = ids[i];
         if (e < 0 || e >= E) {
             slot[i] = -1;
-            atomicOr(&g_smoe_status, kDevBadId);
+            if (!(skip_negative && e < 0)) atomicOr(&g_smoe_status, kDevBadId);
             continue;
         }
         const int pos = cc[(size_t) c * E + e] + __popcll(mask[e] & ((1ull << tl) - 1ull));
         slot[i] = pos;
         if (src) src[pos] = t0 + tl;
+        if (pair) pair[pos] = (int) i;
     }
 }
 
 size_t group_chunk_bytes(int T, int E) { return (((size_t) (T + 63) / 64) * E * 4 + 255) & ~(size_t) 255; }
 
 cudaError_t launch_group(const int32_t* ids, int T, int k, int E, GroupTables g, int32_t* slot, int32_t* src,
-                         cudaStream_t s, const Sched* sched, int32_t* chunk_counts) {
+                         cudaStream_t s, const Sched* sched, int32_t* chunk_counts, int skip_negative, int32_t* pair) {
     if (chunk_counts && T > kGroupWideMinTokens) {
         const int nchunks = (T + 63) / 64;
         group_count_kernel<<<nchunks, 256, 0, s>>>(ids, T, k, E, chunk_counts);
         group_scan_kernel<<<1, 1024, 0, s>>>(E, nchunks, chunk_counts, g, sched ? *sched : Sched{}, sched ? 1 : 0);
-        group_assign_kernel<<<nchunks, 256, 0, s>>>(ids, T, k, E, chunk_counts, slot, src);
+        group_assign_kernel<<<nchunks, 256, 0, s>>>(ids, T, k, E, chunk_counts, slot, src, skip_negative, pair);
         return cudaGetLastError();
     }
-    group_kernel<<<1, 1024, 0, s>>>(ids, T, k, E, g, slot, src, sched ? *sched : Sched{}, sched ? 1 : 0);
+    group_kernel<<<1, 1024, 0, s>>>(ids, T, k, E, g, slot, src, sched ? *sched : Sched{}, sched ? 1 : 0,
+                                    skip_negative, pair);
     return cudaGetLastError();
 }
 

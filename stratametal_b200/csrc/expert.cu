@@ -19,6 +19,7 @@
 // = value 4b + j of a 16-value run), so eight chained dp4a give sum code * q exactly and
 //   sum (code - 1) q = sum code * q - sum q       (exact integer arithmetic; sum q is staged per block).
 #include "common.cuh"
+#include "ep.cuh"
 #include "kernels.cuh"
 #include "q8.cuh"
 
@@ -757,7 +758,7 @@ __global__ void __launch_bounds__(kDownBlock) layer_down_kernel(Matrix wm, Matri
         if (lane == 0) ok = mbar_wait_bounded(&full[st], parity, kWaitLimitNs);
         if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
             if (lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
-            return;
+            break;
         }
         (void) mbar_try_wait(&full[st], parity);
         const int id = s_item[st];
@@ -794,11 +795,12 @@ __global__ void __launch_bounds__(kDownBlock) layer_down_kernel(Matrix wm, Matri
             tbfly<RPG, LPR / 2>(v, lane);
             constexpr int low_mask = LPR / 4 - 1;
             if ((gl & low_mask) == 0)
-                y[(int64_t) (en.beg + s) * n_out + r0 + row_base + ((gl / (LPR / 4)) & 3)] = v[0];
+                down_row(w, y, en.beg + s, n_out)[r0 + row_base + ((gl / (LPR / 4)) & 3)] = v[0];
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
     }
+    ep_signal_done(w.ep_done, gridDim.x * kDownConsumers);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -72,8 +72,11 @@ Sched sched_at(void* base, int E, int T, int k, int chunk = kChunk);
 // runs over many CTAs (three launches) instead of one; the result is the same.
 constexpr int kGroupWideMinTokens = 256;
 size_t group_chunk_bytes(int T, int E);
+// skip_negative: ids < 0 mark pairs that are not grouped (slot -1, no error); pair (optional): pair[row] = the
+// pair index t * k + j of each grouped row.
 cudaError_t launch_group(const int32_t* ids, int T, int k, int E, GroupTables g, int32_t* slot, int32_t* src,
-                         cudaStream_t s, const Sched* sched = nullptr, int32_t* chunk_counts = nullptr);
+                         cudaStream_t s, const Sched* sched = nullptr, int32_t* chunk_counts = nullptr,
+                         int skip_negative = 0, int32_t* pair = nullptr);
 
 
 // ---- expert.cu ----
@@ -104,6 +107,15 @@ struct Matrix {
 cudaError_t launch_expert_down(Matrix down, Matrix sdown, GroupView g, const uint8_t* act, int act_by_token,
                                float* y, int64_t y_stride, int n_in, int n_out, cudaStream_t s);
 
+// Expert parallelism: the warps that wrote routed rows to other ranks report here.  Each such warp fences its
+// stores system-wide and counts itself in `counter` (this rank's memory); the last of `total` warps resets the
+// counter and adds 1 to every rank's done flag for this rank (flags[p] points into rank p's exchange area).
+struct EpDone {
+    unsigned* counter = nullptr;
+    unsigned* const* flags = nullptr;
+    int world = 0;
+};
+
 // The layer path (v3): work items are (work-list entry, row tile), claimed dynamically from `counter`
 // (zeroed by the dispatch) heaviest first; the shared expert's chunks come first when shared_slots > 0.
 struct Work {
@@ -114,6 +126,16 @@ struct Work {
     int shared_slots;  // T, or 0 when the shared expert is not in this launch
     int no_routed;     // 1: the shared expert only
     int32_t* counter;
+    // Expert parallelism (null otherwise): the down output of routed slot s goes to the rank that owns its
+    // token, ep_out[p / (ep_rows * ep_k)] + (p % (ep_rows * ep_k)) * n_out with p = slot_pair[s] (received row
+    // * k + j; received rows come in blocks of ep_rows per source rank); shared slot s goes to
+    // ep_shared + (s - shared_base) * n_out.
+    const int32_t* slot_pair = nullptr;
+    float* const* ep_out = nullptr;
+    float* ep_shared = nullptr;
+    int ep_rows = 0;
+    int ep_k = 0;
+    EpDone ep_done;
 };
 // gate and up rows into gu[slot][gate n_ff | up n_ff] (f32), then SwiGLU + q8_1 of h into ha.
 cudaError_t launch_layer_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, Work w, KAct xa, float* gu,
@@ -141,6 +163,24 @@ cudaError_t launch_add_rms_norm(float* x, const float* residual, const float* w,
 struct DecodeArgs;
 bool decode_qualifies(int H, int F, int E, int k, int gu_type, int d_type, int has_shared, int sg, int su, int sd);
 cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t s);
+
+// ---- ep.cu ---- (expert parallelism over peer memory)
+size_t ep_arena_bytes(int H, int k, int max_tokens, int world);
+// Route + q8_1 done; send every token's ids to every rank and its q8_1 row to each rank that owns one of its
+// experts (and to this rank), then signal.
+cudaError_t launch_ep_dispatch(void* arena, const int32_t* ids, const uint8_t* xq, int T, int k, int H,
+                               int n_local, cudaStream_t s);
+// Wait for every rank's dispatch, then the received rows' local ids (-1: not here) and their activation image:
+// xa (the SIMT kernels' layout, q2 permuted when xa_q2) or xh (hi/lo, the tensor-core kernels).
+cudaError_t launch_ep_receive(void* arena, int k, int H, int expert_first, int n_local, int32_t* oids,
+                              const KAct* xa, int xa_q2, __half* xh, cudaStream_t s, int rows);
+// Wait for every rank's down outputs of this rank's tokens.
+cudaError_t launch_ep_wait_done(void* arena, cudaStream_t s);
+float* const* ep_parts_table(void* arena);
+unsigned* const* ep_done_table(void* arena);
+unsigned* ep_done_counter(void* arena);
+float* ep_parts(void* arena, int H, int k, int max_tokens, int world);
+cudaError_t ep_init(void* arena, void* const* peers, int rank, int world, int H, int k, int max_tokens);
 
 // ---- combine.cu ----
 // out[t][j] = sum_i w[t][i] * parts[slot(t, i)][j] (+ shared[t][j] * sigmoid(gate_logit[t]) when shared)

@@ -7,5 +7,6 @@
 #include "tc.cu"
 #include "elementwise.cu"
 #include "decode.cu"
+#include "ep.cu"
 #include "api.cu"
 #include "noalloc.cu"

@@ -32,6 +32,7 @@
 // Every wait is bounded; on a timeout the kernel records kDevTimeout, drains the copies and MMAs it issued
 // (bounded), frees tensor memory and returns.
 #include "common.cuh"
+#include "ep.cuh"
 #include "kernels.cuh"
 #include "q8.cuh"
 
@@ -473,7 +474,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                         sg[(tt + i) * 32 + lane] = g;
                         su[(tt + i) * 32 + lane] = __fadd_rn(__uint_as_float(u8[i]), __uint_as_float(ul8[i]));
                     } else if (c0 + i < en.n) {
-                        args.parts[(size_t) (en.beg + c0 + i) * args.n_out + row] = g;
+                        down_row(w, args.parts, en.beg + c0 + i, args.n_out)[row] = g;
                     }
                 }
             }
@@ -510,6 +511,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
             }
         }
         if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
+        if (MODE == 1) ep_signal_done(w.ep_done, gridDim.x * kTcEpiWarps);
     }
     tc_fence_before();
     __syncthreads();
