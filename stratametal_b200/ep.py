@@ -151,7 +151,7 @@ class EpLayer:
         self.device = torch.device(device)
         self.t = {k: v.to(self.device).contiguous() for k, v in layer.tensors.items()}
         n_local = sp.n_expert // areas.world
-        if self.t["ffn_gate_exps.weight"].shape[0] != n_local * sp.n_ff:
+        if self.t["ffn_gate_exps.weight"].numel() != n_local * sp.n_ff * synth.row_bytes(sp.gu_type, sp.n_embd):
             raise SmoeError(1, "ep: the routed planes must hold exactly this rank's experts")
         self.c = layer_struct(self.t, sp)
         self.ep = areas.desc()
