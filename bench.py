@@ -43,6 +43,7 @@ KERNEL_OF_STAGE = {"router_gemv": "bf16_gemv_kernel", "router_topk_q8": "router_
                    "dispatch": "group_kernel", "expert_gate_up": "layer_gate_up_kernel",
                    "expert_down": "layer_down_kernel", "combine": "combine_kernel"}
 KERNEL_OF_STAGE_TC = dict(KERNEL_OF_STAGE, expert_gate_up="tc_expert_kernel<0>", expert_down="tc_expert_kernel<1>")
+KERNEL_OF_STAGE_TQ = dict(KERNEL_OF_STAGE, expert_gate_up="tq_expert_kernel<0>", expert_down="tq_expert_kernel<1>")
 
 
 def parse():
@@ -52,8 +53,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
-    ap.add_argument("--expert-path", type=int, default=0, choices=[0, 1, 2],
-                    help="0 automatic, 1 SIMT expert kernels, 2 tensor-core expert kernels")
+    ap.add_argument("--expert-path", type=int, default=0, choices=[0, 1, 2, 4],
+                    help="0 automatic, 1 SIMT expert kernels, 2 fp16 tensor-core kernels, 4 int8 tensor-core kernels")
     ap.add_argument("--layers", type=int, default=4, help="distinct layers rotated through the steps")
     ap.add_argument("--tokens", type=int, default=0, help="override the config's tokens per step (configs[3]: 1 or 16)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample")
@@ -319,7 +320,7 @@ def run_ours(args, ws, rank, local):
         layers = [api.MoeLayer(synth.make_layer(spec, li, dev), T, dev) for li in range(n_layers)]
         path = lib().smoe_expert_path_for(C.byref(layers[0].c), T)
         xs = [synth.make_x(spec.seed + 1000 * local, T, H, dev, stream=b) for b in range(n_batches)]
-    tc, fused = path == 2, path == 3
+    tc, fused, tq = path == 2, path == 3, path == 4
     out = torch.empty(T, H, device=dev)
     stream = torch.cuda.current_stream()
     # the stack ping-pongs between two buffers: layer l reads cur, writes MoE(cur) to nxt, then
@@ -448,11 +449,13 @@ def run_ours(args, ws, rank, local):
         achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_bytes else None
         tpu = traffic_per_unit()
         traffic = None
-        if dominant == "expert_gate_up" and not tc and "expert_gate_up_per_expert" in tpu:
+        if dominant == "expert_gate_up" and not tc and not tq and "expert_gate_up_per_expert" in tpu:
             traffic = tpu["expert_gate_up_per_expert"] * (D_mean + 1)
         expert_gbs = (D_mean + 1) * E_BYTES / (ms_step * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "decode_layer_kernel" if fused else
-                (KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE)[dominant],
+        kos = KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE_TQ if tq else KERNEL_OF_STAGE
+        if 2 <= T <= 64:
+            kos = dict(kos, router_gemv="router_gemm_kernel + router_reduce_kernel (split K)")
+        roof = {"bound": "hbm", "kernel": "decode_layer_kernel" if fused else kos[dominant],
                 "achieved": achieved, "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
                 "frac": achieved / hbm_peak if achieved else None, "traffic": traffic,
                 "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms}
@@ -489,13 +492,21 @@ def run_ours(args, ws, rank, local):
     if rank == 0:
         # router GEMV, top-k (+ q8_1), dispatch, gate/up, [SwiGLU], down, combine; the tensor-core path adds the
         # hi/lo activation image and fuses SwiGLU into gate/up; grouping above 256 tokens takes three launches
-        per_fwd = 7 if tc else 7 + (0 if spec.sg_type == spec.gu_type else 2) + (0 if spec.sd_type == spec.d_type else 2)
-        if T > 256:
-            per_fwd += 2
+        # router (GEMV, or split-K GEMM + reduce from 2 to 64 tokens), top-k, grouping (3 launches above 256
+        # tokens), gate/up, SwiGLU (SIMT only), down, combine; the fp16 tensor-core path adds the hi/lo image
+        router_l = 2 if 2 <= T <= 64 else 1
+        group_l = 3 if T > 256 else 1
+        if tc:
+            per_fwd = router_l + 1 + 1 + group_l + 3
+        elif tq:
+            per_fwd = router_l + 1 + group_l + 3
+        else:
+            per_fwd = router_l + 1 + group_l + 4 + (0 if spec.sg_type == spec.gu_type else 2) + \
+                (0 if spec.sd_type == spec.d_type else 2)
         if fused:
             per_fwd = 1
-        if ep_mode:  # + dispatch, receive and the done-wait; grouping over the ws * T received rows
-            per_fwd = (7 if tc else 8) + 3 + (2 if ws * T > 256 else 0)
+        if ep_mode:  # router, top-k, dispatch, receive, grouping over the ws * T received rows, experts, wait, combine
+            per_fwd = router_l + 1 + 1 + 1 + (3 if ws * T > 256 else 1) + (2 if tc or tq else 3) + 1 + 1
         launches_per_step = n_layers * (per_fwd + 1) if stack else per_fwd
         cfgd = config_dict(args, spec, T_all if ep_mode else T, D_mean, n_layers, stack)
         if ep_mode:
@@ -507,9 +518,11 @@ def run_ours(args, ws, rank, local):
                 "ms_per_step": ms_step, "higher_is_better": True,
                 "scaling": "strong" if ep_mode else "weak", "vs_baseline": None,
                 "dtype": ("fp16 x fp16 tcgen05 (exact hi/lo q8_1 image), f32 accumulate" if tc
+                          else "int8 x int8 tcgen05 (q8_1 contract, s32 per 32-value partial), f32 epilogue in the "
+                               "reference's order" if tq
                           else "int8 x int2 dot (q8_1 contract), f32/f64 sums"), "data": "synthetic",
-                "expert_path": ("tensor cores (tcgen05)" if tc else "fused single-token kernel (one cooperative launch)"
-                                if fused else "SIMT"),
+                "expert_path": ("fp16 tensor cores (tcgen05)" if tc else "int8 tensor cores (tcgen05 kind::i8)" if tq
+                                else "fused single-token kernel (one cooperative launch)" if fused else "SIMT"),
                 "config": cfgd,
                 "timing": "CUDA events around CUDA-graph replays (one captured forward per step"
                           + (", the whole 48-layer stack" if stack else "") + ")",

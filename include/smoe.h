@@ -164,17 +164,19 @@ smoe_status smoe_add_rms_norm(float* x, const float* residual, const float* w, i
 
 /* Expert-kernel path of smoe_moe_forward (no reference counterpart: the reference has one GPU path).
  * 0 (default) automatic: one token takes the fused single-token kernel (path 3) when the layer qualifies,
- * batches of 512 tokens or more the tensor-core kernels when the layer qualifies, the SIMT kernels otherwise;
- * 1 the SIMT kernels always; 2 the tensor-core kernels whenever the layer qualifies (every routed and shared
- * matrix Q2_0, n_embd and n_ff multiples of 512); 3 the fused single-token kernel whenever the batch is one
- * token and the layer qualifies (every matrix Q2_0, n_embd a multiple of 256, n_ff and n_expert at
- * most 512).  The SIMT and
- * fused kernels evaluate the reference's q8_1 integer contract in the reference's summation order; the
- * tensor-core kernels evaluate the same products from an exact fp16 hi/lo split of the q8_1 activation with f32
+ * batches of 512 tokens or more the fp16 tensor-core kernels (path 2) when the layer qualifies, smaller batches
+ * the int8 tensor-core kernels (path 4) when the layer qualifies, the SIMT kernels otherwise;
+ * 1 the SIMT kernels always; 2 the fp16 tensor-core kernels whenever the layer qualifies (every routed and
+ * shared matrix Q2_0, n_embd and n_ff multiples of 512); 3 the fused single-token kernel whenever the batch is
+ * one token and the layer qualifies (every matrix Q2_0, n_embd a multiple of 256, n_ff and n_expert at most
+ * 512), automatic otherwise; 4 the int8 tensor-core kernels whenever the layer qualifies (every matrix Q2_0,
+ * n_embd and n_ff each 512, 1024 or 2048).  The SIMT, fused and int8 tensor-core kernels evaluate the
+ * reference's q8_1 integer contract in the reference's summation order (bit for bit); the fp16 tensor-core
+ * kernels evaluate the same products from an exact fp16 hi/lo split of the q8_1 activation with f32
  * accumulation, so their results agree up to the order of the f32 additions.  Process-wide. */
 smoe_status smoe_set_expert_path(int path);
-/* The path smoe_moe_forward takes for this layer and batch: 1 SIMT, 2 tensor cores, 3 fused single-token
- * kernel, -1 invalid layer. */
+/* The path smoe_moe_forward takes for this layer and batch: 1 SIMT, 2 fp16 tensor cores, 3 fused single-token
+ * kernel, 4 int8 tensor cores, -1 invalid layer. */
 int smoe_expert_path_for(const smoe_layer* L, int n_tokens);
 
 /* Validates the layer's geometry and types: SMOE_OK when smoe_moe_forward can run it. */

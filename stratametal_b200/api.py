@@ -51,8 +51,9 @@ def add_rms_norm(x: torch.Tensor, residual: torch.Tensor | None, w: torch.Tensor
 
 
 def set_expert_path(path: int) -> None:
-    """0 automatic, 1 the SIMT expert kernels, 2 the tensor-core expert kernels where the layer qualifies, 3 the
-    fused single-token kernel where the batch is one token and the layer qualifies."""
+    """0 automatic, 1 the SIMT expert kernels, 2 the fp16 tensor-core expert kernels where the layer qualifies,
+    3 the fused single-token kernel where the batch is one token and the layer qualifies, 4 the int8 tensor-core
+    kernels of the integer contract where the layer qualifies."""
     check(lib().smoe_set_expert_path(path))
 
 

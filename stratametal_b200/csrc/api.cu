@@ -4,6 +4,7 @@
 #include "common.cuh"
 #include "kernels.cuh"
 
+#include <algorithm>
 #include <atomic>
 #include <cstring>
 #include <string>
@@ -49,6 +50,7 @@ struct Layout {
     size_t sched_tc, xh, hh;  // the tensor-core path (0 bytes when the layer does not qualify)
     size_t chunk;             // per-(64-token chunk, expert) counts of the many-CTA grouping
     size_t bar;               // grid barrier words of the single-token fused kernel
+    size_t rsplit;            // fp64 partial sums of the few-token router GEMM
     size_t total;
 };
 
@@ -75,8 +77,22 @@ bool use_decode(const smoe_layer* L, int T) {
 
 bool use_tc(const smoe_layer* L, int T) {
     const int p = g_expert_path.load(std::memory_order_relaxed);
-    if (p == 1 || p == 3 || !tc_qualifies(L)) return false;
+    if (p == 1 || p == 3 || p == 4 || !tc_qualifies(L)) return false;
     return p == 2 || T >= kTcAutoTokens;
+}
+
+// The int8 tensor-core kernels of the integer contract take Q2_0 everywhere and n_embd, n_ff in {512, 1024, 2048}.
+bool tq_layer(const smoe_layer* L) {
+    const bool q2 = L->gu_type == kQ2_0 && L->d_type == kQ2_0 &&
+                    (!L->has_shared || (L->sg_type == kQ2_0 && L->su_type == kQ2_0 && L->sd_type == kQ2_0));
+    return q2 && tq_qualifies(L->n_embd, L->n_ff);
+}
+
+// Below the tensor-core (fp16) range: the int8 tensor-core kernels unless the SIMT kernels are asked for.
+bool use_tq(const smoe_layer* L, int T) {
+    const int p = g_expert_path.load(std::memory_order_relaxed);
+    if (p == 1 || p == 2 || !tq_layer(L)) return false;
+    return p == 4 || (p == 0 && T < kTcAutoTokens) || p == 3;
 }
 
 Layout layout_of(const smoe_layer* L, int T) {
@@ -100,6 +116,7 @@ Layout layout_of(const smoe_layer* L, int T) {
     o.parts = at; at += up256(rows * H * 4);
     o.chunk = at; at += group_chunk_bytes(T, (int) E);
     o.bar = at; at += 256;
+    o.rsplit = at; at += router_split_bytes(std::min(T, kRouterGemmMinTokens), (int) E + 1, (int) H);
     o.sched_tc = o.xh = o.hh = at;
     if (tc_qualifies(L)) {
         o.sched_tc = at; at += sched_bytes((int) E, T, (int) K, kTcChunk);
@@ -140,7 +157,7 @@ smoe_status check_layer(const smoe_layer* L) {
 // Local scratch of the expert-parallel block: this rank's tokens (T = max_tokens) on the router side, the
 // received rows (R = world * max_tokens) and this rank's n_local experts on the expert side.
 struct EpLayout {
-    size_t xq, logits, sh_logit, ids, w, shared;                                       // token side
+    size_t xq, logits, sh_logit, ids, w, shared, rsplit;                               // token side
     size_t oids, slot, slot_token, slot_pair, tables, sched, chunk, xa, gu, ha;        // expert side, SIMT
     size_t sched_tc, xh, hh;                                                           // tensor cores
     size_t total;
@@ -158,6 +175,7 @@ EpLayout ep_layout_of(const smoe_layer* L, const smoe_ep* ep) {
     o.ids = at; at += up256((size_t) T * K * 4);
     o.w = at; at += up256((size_t) T * K * 4);
     o.shared = at; at += up256((size_t) T * H * 4);
+    o.rsplit = at; at += router_split_bytes(std::min(T, kRouterGemmMinTokens), L->n_expert + 1, (int) H);
     o.oids = at; at += up256((size_t) R * K * 4);
     o.slot = at; at += up256((size_t) R * K * 4);
     o.slot_token = at; at += up256((size_t) R * K * 4);
@@ -205,14 +223,14 @@ extern "C" {
 const char* smoe_last_error(void) { return g_err.c_str(); }
 
 smoe_status smoe_set_expert_path(int path) {
-    if (path < 0 || path > 3) return fail(SMOE_INVALID_ARG, "set_expert_path: path must be 0, 1, 2 or 3");
+    if (path < 0 || path > 4) return fail(SMOE_INVALID_ARG, "set_expert_path: path must be 0, 1, 2, 3 or 4");
     g_expert_path.store(path);
     return ok();
 }
 
 int smoe_expert_path_for(const smoe_layer* L, int n_tokens) {
     if (check_layer(L) != SMOE_OK || n_tokens <= 0) return -1;
-    return use_decode(L, n_tokens) ? 3 : use_tc(L, n_tokens) ? 2 : 1;
+    return use_decode(L, n_tokens) ? 3 : use_tc(L, n_tokens) ? 2 : use_tq(L, n_tokens) ? 4 : 1;
 }
 
 void smoe_set_stage_events(void** events, int n) {
@@ -469,7 +487,7 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     }
 
     cudaError_t e = launch_bf16_gemv(x, true, L->router, sh ? L->gate_inp_shexp : nullptr, logits, sh_logit, T, H,
-                                     E, s);
+                                     E, s, base + lo.rsplit);
     if (e == cudaSuccess) e = mark(0, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: router");
     const bool tc = use_tc(L, T);
@@ -510,6 +528,16 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
         e = launch_tc_down(md, sd, wt, E, hh, rows, parts, F, H, s);
         if (e == cudaSuccess) e = mark(4, s);
         if (e != cudaSuccess) return cuda_fail(e, "moe_forward: down (tensor cores)");
+    } else if (use_tq(L, T)) {
+        // int8 tensor cores (the q8_1 contract bit for bit): every matrix is Q2_0, the shared expert rides along
+        Work wq = wk;
+        wq.shared_slots = sh ? T : 0;
+        e = launch_tq_gate_up(mg, mu, sg, su, wq, E, xa, ha, 1, H, F, s);
+        if (e == cudaSuccess) e = mark(3, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: gate/up (int8 tensor cores)");
+        e = launch_tq_down(md, sd, wq, E, ha, parts, F, H, s);
+        if (e == cudaSuccess) e = mark(4, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: down (int8 tensor cores)");
     } else {
     // The shared expert rides in the routed launches when its types match; otherwise it gets its own.
     const bool gu_same = sh && L->sg_type == L->gu_type && L->su_type == L->gu_type;
@@ -659,7 +687,8 @@ smoe_status smoe_ep_forward(const smoe_layer* L, const smoe_ep* ep, const float*
 
     if (phases & 1) {
         if (T > 0) {
-            e = launch_bf16_gemv(x, true, L->router, sh ? L->gate_inp_shexp : nullptr, logits, sh_logit, T, H, E, s);
+            e = launch_bf16_gemv(x, true, L->router, sh ? L->gate_inp_shexp : nullptr, logits, sh_logit, T, H, E, s,
+                                 base + lo.rsplit);
             if (e == cudaSuccess) e = mark(0, s);
             if (e == cudaSuccess) e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, nullptr, 1);
             if (e == cudaSuccess) e = mark(1, s);
@@ -713,6 +742,15 @@ smoe_status smoe_ep_forward(const smoe_layer* L, const smoe_ep* ep, const float*
             e = launch_tc_down(md, sd, wk, El, hh, rows, nullptr, F, H, s);
             if (e == cudaSuccess) e = mark(4, s);
             if (e != cudaSuccess) return cuda_fail(e, "ep_forward: down (tensor cores)");
+        } else if (use_tq(L, R)) {
+            const KAct ha = ka_at(base + lo.ha, rows, F / 32);
+            e = launch_tq_gate_up(mg, mu, sg, su, wk, El, xa, ha, 1, H, F, s);
+            if (e == cudaSuccess) e = mark(3, s);
+            if (e != cudaSuccess) return cuda_fail(e, "ep_forward: gate/up (int8 tensor cores)");
+            wk.ep_done = done;
+            e = launch_tq_down(md, sd, wk, El, ha, nullptr, F, H, s);
+            if (e == cudaSuccess) e = mark(4, s);
+            if (e != cudaSuccess) return cuda_fail(e, "ep_forward: down (int8 tensor cores)");
         } else {
             float* gu = reinterpret_cast<float*>(base + lo.gu);
             const KAct ha = ka_at(base + lo.ha, rows, F / 32);

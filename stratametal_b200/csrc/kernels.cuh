@@ -28,8 +28,11 @@ inline KAct ka_at(void* base, int64_t rows, int nblk) {
 }
 
 // ---- router.cu ----
+// split_scratch (router_split_bytes of it, 256-byte aligned): few-token f32 calls take the fp64 tensor-path GEMM
+// split over K instead of the GEMV, to fill the SMs.
 cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, const uint16_t* extra, float* y,
-                             float* y_extra, int T, int H, int n_out, cudaStream_t s);
+                             float* y_extra, int T, int H, int n_out, cudaStream_t s, void* split_scratch = nullptr);
+size_t router_split_bytes(int T, int n_rows, int H);
 // xa (optional): the activation in the expert kernels' layout, permuted for Q2_0 gate/up when xa_q2 != 0.
 cudaError_t launch_router_topk(const float* logits, int T, int E, int k, int32_t* ids, float* w, const float* x,
                                uint8_t* xq, int H, cudaStream_t s, const KAct* xa = nullptr, int xa_q2 = 1);
@@ -153,6 +156,16 @@ cudaError_t launch_tc_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, 
 // down rows of every slot into parts[slot][n_embd].
 cudaError_t launch_tc_down(Matrix down, Matrix sdown, Work w, int n_expert, const __half* hh, int R, float* parts,
                            int n_ff, int n_embd, cudaStream_t s);
+
+// ---- tq.cu ---- (Q2_0 weights, n_embd and n_ff in {512, 1024, 2048}; work list built with chunk kChunk = 8)
+// The q8_1 integer contract on the int8 tensor cores, bitwise the SIMT kernels' results.
+bool tq_qualifies(int H, int F);
+// gate/up + SwiGLU + q8_1 of h into ha (the down matrix's KAct layout).
+cudaError_t launch_tq_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, Work w, int n_expert, KAct xa,
+                              KAct ha, int down_q2, int n_embd, int n_ff, cudaStream_t s);
+// down rows of every slot into y[slot][n_embd] (or the expert-parallel destinations of the Work).
+cudaError_t launch_tq_down(Matrix down, Matrix sdown, Work w, int n_expert, KAct ha, float* y, int n_ff, int n_embd,
+                           cudaStream_t s);
 
 // ---- elementwise.cu ----
 // x[r] = rms_norm(x[r] + residual[r]) * w (residual and w may be null): the host rule of rms_ref.

@@ -137,9 +137,13 @@ __device__ __forceinline__ void dmma_8x8x4(double (&d)[2], double a, double b) {
                  : "d"(a), "d"(b));
 }
 
+// Split-K (few tokens): blockIdx.z takes K range [z H / S, (z + 1) H / S) and writes its fp64 partial sums to
+// part[z][t][o]; router_reduce_kernel adds the S partials in z order.  The fp64 sums are exact on this data, so
+// the split changes nothing in the result.
 __global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restrict__ x, const uint16_t* __restrict__ w,
                                                           const uint16_t* __restrict__ extra, float* __restrict__ y,
-                                                          float* __restrict__ y_extra, int T, int H, int n_out) {
+                                                          float* __restrict__ y_extra, int T, int H, int n_out,
+                                                          double* __restrict__ part) {
     extern __shared__ __align__(16) double rg_smem[];
     double (*ws)[kRgRows + kRgPad] = reinterpret_cast<double (*)[kRgRows + kRgPad]>(rg_smem);
     double (*xs)[kRgToks + kRgPad] = reinterpret_cast<double (*)[kRgToks + kRgPad]>(rg_smem + kRgK * (kRgRows + kRgPad));
@@ -153,6 +157,8 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restric
     const uint16_t* wrow = (wo < n_out ? w + (size_t) wo * H : extra) + wk;
     const int xr = tid & 127, xk = (tid >> 7) * 16;
     const float* xrow = x + (size_t) min(t0 + xr, T - 1) * H + xk;
+    const int S = gridDim.z;
+    const int k_len = H / S, k_beg = (int) blockIdx.z * k_len;
     uint4 wreg;
     float4 xreg[4];
     auto load = [&](int kc) {
@@ -183,12 +189,14 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restric
     for (int i = 0; i < 4; i++)
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j][0] = acc[i][j][1] = 0.0;
-    load(0);
-    for (int kc = 0; kc < H; kc += kRgK) {
+    const bool active = t0 + wto < T;  // warps whose tokens are all padding skip the products
+    load(k_beg);
+    for (int kc = k_beg; kc < k_beg + k_len; kc += kRgK) {
         __syncthreads();  // the previous chunk is consumed
         stage();
         __syncthreads();
-        if (kc + kRgK < H) load(kc + kRgK);
+        if (kc + kRgK < k_beg + k_len) load(kc + kRgK);
+        if (!active) continue;
 #pragma unroll
         for (int k = 0; k < kRgK; k += 4) {
             double a[4], bv[4];
@@ -203,6 +211,24 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restric
         }
     }
     // D[row gid][token 2 tig + c]
+    if (S == 1) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int o = o0 + wro + 8 * i + gid;
+            if (o >= n_rows) continue;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    const int t = t0 + wto + 8 * j + 2 * tig + c;
+                    if (t >= T) continue;
+                    if (o < n_out) y[(size_t) t * n_out + o] = (float) acc[i][j][c];
+                    else y_extra[t] = (float) acc[i][j][c];
+                }
+        }
+        return;
+    }
+    double* my = part + (size_t) blockIdx.z * T * n_rows;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int o = o0 + wro + 8 * i + gid;
@@ -212,11 +238,43 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const float* __restric
 #pragma unroll
             for (int c = 0; c < 2; c++) {
                 const int t = t0 + wto + 8 * j + 2 * tig + c;
-                if (t >= T) continue;
-                if (o < n_out) y[(size_t) t * n_out + o] = (float) acc[i][j][c];
-                else y_extra[t] = (float) acc[i][j][c];
+                if (t < T) my[(size_t) t * n_rows + o] = acc[i][j][c];
             }
     }
+}
+
+// y[t][o] = (float) sum_z part[z][t][o], z in order (independent loads, then the adds).
+__global__ void __launch_bounds__(256) router_reduce_kernel(const double* __restrict__ part, int S, int T, int n_rows,
+                                                            int n_out, float* __restrict__ y,
+                                                            float* __restrict__ y_extra) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= T * n_rows) return;
+    double v[32];
+#pragma unroll
+    for (int z = 0; z < 32; z++)
+        if (z < S) v[z] = __ldg(part + (size_t) z * T * n_rows + i);
+    double acc = 0.0;
+#pragma unroll
+    for (int z = 0; z < 32; z++)
+        if (z < S) acc += v[z];
+    const int t = i / n_rows, o = i % n_rows;
+    if (o < n_out) y[(size_t) t * n_out + o] = (float) acc;
+    else y_extra[t] = (float) acc;
+}
+
+// K splits of the few-token router GEMM: enough CTAs for the SMs, K a multiple of the 32-wide chunk.
+int router_splits(int T, int n_rows, int H) {
+    if (T < 2 || T > kRouterGemmMinTokens || H % kRgK) return 1;
+    const int tiles = ((n_rows + kRgRows - 1) / kRgRows) * ((T + kRgToks - 1) / kRgToks);
+    int S = 1;
+    while (S < 32 && 2 * S * tiles <= 160 && (H / kRgK) % (2 * S) == 0) S *= 2;
+    return S;
+}
+
+size_t router_split_bytes(int T, int n_rows, int H) {
+    const int S = router_splits(T, n_rows, H);
+    if (S == 1) return 0;
+    return ((size_t) S * T * n_rows * 8 + 255) & ~(size_t) 255;
 }
 
 constexpr size_t kRgSmem = (size_t) kRgK * (kRgRows + kRgPad + kRgToks + kRgPad) * sizeof(double);
@@ -358,15 +416,18 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const floa
 // ------------------------------------------------------------------------------------------------
 
 cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, const uint16_t* extra, float* y,
-                             float* y_extra, int T, int H, int n_out, cudaStream_t s) {
+                             float* y_extra, int T, int H, int n_out, cudaStream_t s, void* split_scratch) {
     const int n_rows = n_out + (extra ? 1 : 0);
-    if (f32_in && T > kRouterGemmMinTokens && H % kRgK == 0) {
-        const dim3 grid((n_rows + kRgRows - 1) / kRgRows, (T + kRgToks - 1) / kRgToks);
+    const int S = split_scratch ? router_splits(T, n_rows, H) : 1;
+    if (f32_in && H % kRgK == 0 && (T > kRouterGemmMinTokens || S > 1)) {
+        const dim3 grid((n_rows + kRgRows - 1) / kRgRows, (T + kRgToks - 1) / kRgToks, S);
         cudaError_t err = cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                (int) kRgSmem);
         if (err != cudaSuccess) return err;
+        double* part = S > 1 ? static_cast<double*>(split_scratch) : nullptr;
         router_gemm_kernel<<<grid, 256, kRgSmem, s>>>(static_cast<const float*>(x), w, extra, y, y_extra, T, H,
-                                                      n_out);
+                                                      n_out, part);
+        if (S > 1) router_reduce_kernel<<<(T * n_rows + 255) / 256, 256, 0, s>>>(part, S, T, n_rows, n_out, y, y_extra);
         return cudaGetLastError();
     }
     const size_t smem = (size_t) kRouterTokTile * H * 2;

@@ -5,6 +5,7 @@
 #include "expert.cu"
 #include "combine.cu"
 #include "tc.cu"
+#include "tq.cu"
 #include "elementwise.cu"
 #include "decode.cu"
 #include "ep.cu"

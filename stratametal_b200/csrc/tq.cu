@@ -1,0 +1,622 @@
+// tq.cu - grouped expert GEMVs of the q8_1 integer contract on the 5th-generation tensor cores
+// (tcgen05.mma kind::i8, s32 accumulators in tensor memory): the decode-shaped path (a few tokens per expert),
+// with results bit for bit those of the reference's row dot (iq.metal:459-514, host row_dot iq_parity.cpp:275-292).
+//
+// The contract.  A weight row against a q8_1 activation is a sum of 32-value partials
+//   p_k = (d_w(k) * d_x(k)) * (float)(sum_i code_i * q_i - sum_i q_i)            (two f32 multiplies)
+// added in the reference's order: partial k goes to lane k & 31 (in-lane sums start from 0 and follow k), then
+// the 32 lane sums meet in an xor butterfly 16, 8, 4, 2, 1.  Here one MMA of K = 32 gives sum code * q of one
+// partial for 128 rows x 8 tokens exactly (int32), each K step into its own tensor-memory columns (no
+// accumulation across K), and the epilogue evaluates the partials and the reference's tree of f32 additions:
+// lane sums s_l, level-1 nodes a_j = s_j + s_(j+16) (j < 16), then b_j = a_j + a_(j+8), c_j = b_j + b_(j+4),
+// d_j = c_j + c_(j+2), result d_0 + d_1 (float addition commutes, so only the grouping matters).
+//
+// Shapes (swap-AB): M = 128 weight rows (tensor-memory lanes), N = 8 tokens (slots) of one work entry, K = 32
+// per MMA.  P = K / 32 partials per row (16, 32 or 64).  A stage is 4 whole Q2_0 blocks of a row (8 K steps)
+// chosen so that the epilogue can finish tree nodes from it: P = 64: blocks m, m+8, m+16, m+24 (nodes a_2m,
+// a_2m+1); P = 32: blocks 2m, 2m+1, 2m+8, 2m+9 (a_4m..a_4m+3); P = 16: blocks 4m..4m+3 (a_8m..a_8m+7).  The
+// epilogue keeps a_0..a_7 until a_8..a_15 arrive (8 floats per token).
+//
+// Operands.  Weights: Q2_0 rows TMA-loaded raw (2D boxes of 144 B x 128 rows), decoded by eight warps into int8
+// codes 0..3 straight into tensor memory (tcgen05.st; A of the MMA is read from tensor memory).  The word
+// (qs >> 2j) & 0x03030303 holds in byte b the code of value 4b + j of a 16-value run; the activation rows are the
+// expert kernels' layout (KAct), whose q words use the same order, so the MMA's K order matches without a
+// shuffle.  Activations: per entry, the tokens' q words of every K step gathered by cp.async into the canonical
+// K-major layout (8 tokens x 16 B core matrices), and each (token, K step)'s scale and sum of q beside them.
+//
+//   gate/up (MODE 0): gate and up rows of one 128-row tile per item, the epilogue applies SwiGLU and the q8_1
+//                     rule to each warp's 32 rows (one 32-value block of h) and writes h in the KAct layout;
+//   down (MODE 1):    128 output rows per item, the epilogue stores f32 per (slot, row).
+//
+// Warps: 0 raw weight producer (TMA; tensor memory allocation), 1 MMA issuer, 2-3 activation producers, 4-11
+// decoders, 12-19 epilogue.  Every wait is bounded; on a timeout the kernel records kDevTimeout, drains what it
+// issued (bounded), frees tensor memory and returns.
+#include "common.cuh"
+#include "ep.cuh"
+#include "kernels.cuh"
+#include "q8.cuh"
+
+namespace smoe {
+
+constexpr int kTqThreads = 640;
+constexpr int kTqEpiWarp0 = 12;
+constexpr int kTqM = 128;
+constexpr int kTqN = 8;                 // tokens per MMA (work entries of kChunk = 8 slots)
+constexpr uint32_t kTqQuarter = kTqM * 144;  // one 2D box: 8 blocks of 128 rows
+
+// idesc of kind::i8: s32 accumulator (c_format 2), A and B signed 8-bit, both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
+    asm volatile("{ .reg .pred p; setp.ne.b32 p, 0, 0; tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p; }" ::"r"(
+                     d_tmem),
+                 "r"(a_tmem), "l"(b_desc), "r"(idesc)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tq_tma_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_addr(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tq_cp16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void tq_cp8(uint32_t dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void tq_cp_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool tq_wait(uint64_t* bar, uint32_t parity) {
+    const bool ok = mbar_wait_sleep(bar, parity, kWaitLimitNs);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Block slot s (0..3) of stage m: the blocks whose partials finish tree nodes together (see the header).
+template <int P>
+__host__ __device__ constexpr int tq_block(int m, int s) {
+    return P == 64 ? m + 8 * s : P == 32 ? 2 * m + (s & 1) + 8 * (s >> 1) : 4 * m + s;
+}
+
+// The order in which an item's stages run: a stage's level-1 nodes meet their level-2 partners early, so the
+// epilogue keeps at most 6 (P = 64) or 8 values per token.
+template <int P>
+__host__ __device__ constexpr int tq_order(int i) {
+    return P == 64 ? (i >> 1) + 4 * (i & 1) : P == 32 ? (i >> 1) + 2 * (i & 1) : i;
+}
+
+// One item = one 128-row tile of one matrix for one work entry.  Gate/up runs an entry's gate tile and its up
+// tile as two consecutive items on the same CTA (a group): the epilogue keeps g in registers and applies SwiGLU
+// when u is done, and the activation buffer is loaded once per group.
+template <int MODE, int P>
+struct TqCfg {
+    static constexpr int G = MODE == 0 ? 2 : 1;       // items per group (matrices of one tile)
+    static constexpr int QS = P / 16;                 // raw quarters (8 blocks = 16 partials) per row
+    static constexpr int S = P / 8;                   // stages per item
+    static constexpr uint32_t kRawItem = QS * kTqQuarter;
+    static constexpr int kRaw = kRawItem > 40 * 1024 ? 2 : 4;  // items of raw weights in flight
+    static constexpr int kA = 4, kD = 4, kDW = 4;
+    static constexpr int kBB = MODE == 0 || kRawItem > 40 * 1024 ? 2 : 4;  // activation buffers (groups)
+    static constexpr uint32_t kStCols = 64;           // one A or D stage: 8 K steps x 8 columns
+    static constexpr uint32_t kTmemCols = 512;
+    static_assert((kA + kD) * kStCols <= kTmemCols, "tensor memory budget");
+    static constexpr uint32_t kBBytes = P * 256;      // q words: [K step][2 core matrices][8 tokens][16 B]
+    static constexpr uint32_t kSBytes = P * kTqN * 8; // [K step][token] {d_x f32, sum q}
+    static constexpr uint32_t kBBuf = kBBytes + kSBytes;
+    static constexpr uint32_t kDWStage = 4 * kTqM * 2;  // fp16 block scales [slot][row]
+    static constexpr size_t smem = (size_t) kRaw * kRawItem + kBB * kBBuf + kDW * kDWStage + 64 * 8 + 1024;
+    static_assert(smem <= 232448, "shared memory per block");
+};
+
+struct TqArgs {
+    Work w;
+    const uint8_t* act;  // activation rows in the KAct layout (tokens for gate/up, slots for down)
+    int m_tiles;         // 128-row tiles per expert matrix
+    int rows_per_expert; // n_ff (gate/up) or n_embd (down)
+    int n_out;           // gate/up: n_ff (h row length); down: n_embd
+    uint8_t* ha;         // gate/up: h in the KAct layout [slot][n_ff / 32][48]
+    int ha_q2;           // the down matrix is Q2_0 (permuted q words)
+    float* y;            // down: [slot][n_embd]
+};
+
+template <int MODE, int P>
+__global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_constant__ CUtensorMap mw0,
+                                                                  const __grid_constant__ CUtensorMap mw1,
+                                                                  const __grid_constant__ CUtensorMap sw0,
+                                                                  const __grid_constant__ CUtensorMap sw1,
+                                                                  TqArgs args) {
+    using Cfg = TqCfg<MODE, P>;
+    constexpr int G = Cfg::G, QS = Cfg::QS, S = Cfg::S, kRaw = Cfg::kRaw, kA = Cfg::kA, kD = Cfg::kD,
+                  kDW = Cfg::kDW, kBB = Cfg::kBB;
+    constexpr uint32_t kStCols = Cfg::kStCols;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint8_t* sRaw = smem;                                          // [kRaw][QS][128 rows][144 B]
+    uint8_t* sB = sRaw + (size_t) kRaw * Cfg::kRawItem;            // [kBB][kBBuf]
+    uint16_t* sDW = reinterpret_cast<uint16_t*>(sB + kBB * Cfg::kBBuf);  // [kDW][4][128]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sDW) + kDW * Cfg::kDWStage);
+    uint64_t* raw_full = bars;            // TMA tx
+    uint64_t* raw_empty = raw_full + 4;   // decoders (8 warps)
+    uint64_t* b_full = raw_empty + 4;     // 64 producer threads (cp.async)
+    uint64_t* b_empty = b_full + 4;       // MMA commit + 8 epilogue warps
+    uint64_t* a_full = b_empty + 4;       // the 4 decoder warps of the stage
+    uint64_t* a_empty = a_full + kA;      // MMA commit
+    uint64_t* d_full = a_empty + kA;      // MMA commit
+    uint64_t* d_empty = d_full + kD;      // epilogue warps
+    uint64_t* dw_full = d_empty + kD;     // the 4 decoder warps of the stage
+    uint64_t* dw_empty = dw_full + kDW;   // epilogue warps
+    uint64_t* mma_done = dw_empty + kDW;
+    __shared__ uint32_t s_tmem;
+
+    const Work w = args.w;
+    const int n_groups = work_entries(w) * args.m_tiles;
+    // item j of this CTA: group blockIdx.x + (j / G) gridDim.x, matrix j % G
+    auto group_of = [&](int j) { return (int) blockIdx.x + (j / G) * (int) gridDim.x; };
+
+    if (tid == 0) {
+        for (int i = 0; i < 4; i++) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], 8);
+            mbar_init(&b_full[i], 64);
+            mbar_init(&b_empty[i], 1 + 8);
+        }
+        for (int i = 0; i < kA; i++) {
+            mbar_init(&a_full[i], 4);
+            mbar_init(&a_empty[i], 1);
+        }
+        for (int i = 0; i < kD; i++) {
+            mbar_init(&d_full[i], 1);
+            mbar_init(&d_empty[i], 8);
+        }
+        for (int i = 0; i < kDW; i++) {
+            mbar_init(&dw_full[i], 4);
+            mbar_init(&dw_empty[i], 8);
+        }
+        mbar_init(mma_done, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&s_tmem, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    const uint32_t tA = tmem, tD = tmem + kA * kStCols;
+
+    if (warp == 0) {
+        // ---------------- raw weights: the item's row tile, one box per quarter ----------------
+        bool ok = true;
+        int j = 0;
+        for (;; j++) {
+            const int gid = group_of(j);
+            if (gid >= n_groups) break;
+            const Entry en = work_entry(w, gid / args.m_tiles);
+            const int mat = j % G;
+            const int row = (en.shared ? 0 : en.e * args.rows_per_expert) + (gid % args.m_tiles) * kTqM;
+            const int rs = j % kRaw;
+            if (j >= kRaw && !tq_wait(&raw_empty[rs], (uint32_t) ((j / kRaw - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            if (lane == 0) {
+                uint8_t* dst = sRaw + (size_t) rs * Cfg::kRawItem;
+                const CUtensorMap* map = en.shared ? (mat ? &sw1 : &sw0) : (mat ? &mw1 : &mw0);
+                mbar_expect_tx(&raw_full[rs], Cfg::kRawItem);
+                for (int q = 0; q < QS; q++) tq_tma_2d(dst + (size_t) q * kTqQuarter, map, q * 144, row, &raw_full[rs]);
+            }
+            __syncwarp();
+        }
+        if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
+        if (lane == 0)
+            for (int i = max(0, j - kRaw); i < j; i++)
+                mbar_wait_sleep(&raw_full[i % kRaw], (uint32_t) ((i / kRaw) & 1), kWaitLimitNs);
+        __syncwarp();
+    } else if (warp == 2 || warp == 3) {
+        // ---------------- activations: the entry's slots, every K step, once per group ----------------
+        const int pt = tid - 64;  // 0..63
+        bool ok = true;
+        for (int g = 0; ok; g++) {
+            const int gid = group_of(g * G);
+            if (gid >= n_groups) break;
+            const Entry en = work_entry(w, gid / args.m_tiles);
+            const int bb = g % kBB;
+            if (g >= kBB && !tq_wait(&b_empty[bb], (uint32_t) ((g / kBB - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            uint8_t* buf = sB + (size_t) bb * Cfg::kBBuf;
+            const uint32_t bq = smem_addr(buf), bs = smem_addr(buf + Cfg::kBBytes);
+            // thread pt copies token t = pt / 8, K steps pt % 8, pt % 8 + 8, ...: its q bytes (two 16-byte halves)
+            // and {d, sum q}.  gate/up reads the slot's token row of x, down the slot's own row of h.
+            const int t = pt >> 3;
+            if (t < en.n) {
+                const int tok = MODE == 0 ? entry_token(w, en, en.beg + t) : en.beg + t;
+                const uint8_t* row = args.act + (size_t) tok * ((size_t) P * kKaBlock);
+#pragma unroll
+                for (int k = pt & 7; k < P; k += 8) {
+                    const uint8_t* src = row + (size_t) k * kKaBlock;
+                    tq_cp16(bq + k * 256 + t * 16, src);
+                    tq_cp16(bq + k * 256 + 128 + t * 16, src + 16);
+                    tq_cp8(bs + (k * kTqN + t) * 8, src + 32);
+                }
+            }
+            tq_cp_arrive(&b_full[bb]);
+        }
+        if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_i8(kTqM, kTqN);
+            int sa_c = 0, sd_c = 0;
+            bool ok = true, issued = false;
+            for (int j = 0; ok; j++) {
+                const int gid = group_of(j);
+                if (gid >= n_groups) break;
+                const int g = j / G, bb = g % kBB;
+                if (j % G == 0 && !mbar_wait_sleep(&b_full[bb], (uint32_t) ((g / kBB) & 1), kWaitLimitNs)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* buf = sB + (size_t) bb * Cfg::kBBuf;
+                for (int i = 0; i < S; i++, sa_c++, sd_c++) {
+                    const int m = tq_order<P>(i);
+                    const int sa = sa_c % kA, sd = sd_c % kD;
+                    if (!mbar_wait_sleep(&a_full[sa], (uint32_t) ((sa_c / kA) & 1), kWaitLimitNs) ||
+                        (sd_c >= kD && !mbar_wait_sleep(&d_empty[sd], (uint32_t) ((sd_c / kD - 1) & 1), kWaitLimitNs))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // cp.async writes -> MMA reads
+#pragma unroll
+                    for (int s = 0; s < 4; s++)
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const int k = 2 * tq_block<P>(m, s) + h;
+                            const uint64_t bd = umma_desc(buf + k * 256, 128, 256);
+                            umma_i8_ts(tD + sd * kStCols + (uint32_t) (h * 4 + s) * 8,
+                                       tA + sa * kStCols + (uint32_t) (s * 2 + h) * 8, bd, idesc);
+                        }
+                    umma_commit(&a_empty[sa]);
+                    umma_commit(&d_full[sd]);
+                    issued = true;
+                }
+                if (!ok) break;
+                if (j % G == G - 1) umma_commit(&b_empty[bb]);
+            }
+            if (!ok) atomicOr(&g_smoe_status, kDevTimeout);
+            if (issued) {
+                umma_commit(mma_done);
+                mbar_wait_sleep(mma_done, 0, kWaitLimitNs);
+            }
+        }
+        __syncwarp();
+    } else if (warp >= 4 && warp < kTqEpiWarp0) {
+        // ---------------- decoders: raw Q2_0 -> int8 codes in tensor memory, block scales to shared memory ------
+        // warp 4 + 4 role + q decodes rows 32q + lane of the stages i with i % 2 == role.
+        const int q = warp & 3, role = (warp - 4) >> 2;
+        const int r = 32 * q + lane;
+        int sa_c = 0, dw_c = 0;
+        bool ok = true;
+        for (int j = 0; ok; j++) {
+            if (group_of(j) >= n_groups) break;
+            const int rs = j % kRaw;
+            if (!tq_wait(&raw_full[rs], (uint32_t) ((j / kRaw) & 1))) {
+                ok = false;
+                break;
+            }
+            const uint8_t* rowq = sRaw + (size_t) rs * Cfg::kRawItem + (size_t) r * 144;
+#pragma unroll
+            for (int i = 0; i < S; i++, sa_c++, dw_c++) {
+                if (!ok) break;
+                if ((i & 1) != role) continue;
+                const int m = tq_order<P>(i);
+                const int sa = sa_c % kA, sw = dw_c % kDW;
+                uint32_t col[64];  // slot s, half h, word c at 16 s + 8 h + c
+                uint16_t dbits[4];
+#pragma unroll
+                for (int s = 0; s < 4; s++) {
+                    const int b = tq_block<P>(m, s);
+                    const int o = ((b & 7) * 18) & 15;  // the block's offset inside its 16-byte chunk (even)
+                    const uint4* cp = reinterpret_cast<const uint4*>(rowq + (size_t) (b >> 3) * kTqQuarter + (b & 7) * 18 - o);
+                    const uint4 c0 = cp[0], c1 = cp[1];
+                    const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                    const int wi = (o + 2) >> 2;                      // the 16 code bytes start at byte o + 2
+                    const uint32_t sh = (uint32_t) ((o + 2) & 3) * 8u;  // 0 or 16
+                    uint32_t qw[4];
+#pragma unroll
+                    for (int x = 0; x < 4; x++)
+                        qw[x] = sh ? __funnelshift_r(wv[wi + x], wv[wi + x + 1 < 8 ? wi + x + 1 : 7], sh) : wv[wi + x];
+                    dbits[s] = (uint16_t) (wv[o >> 2] >> ((o & 3) * 8));
+#pragma unroll
+                    for (int h = 0; h < 2; h++)
+#pragma unroll
+                        for (int hw = 0; hw < 2; hw++)
+#pragma unroll
+                            for (int jj = 0; jj < 4; jj++)
+                                col[16 * s + 8 * h + 4 * hw + jj] = (qw[2 * h + hw] >> (2 * jj)) & 0x03030303u;
+                }
+                if (sa_c >= kA && !tq_wait(&a_empty[sa], (uint32_t) ((sa_c / kA - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                if (dw_c >= kDW && !tq_wait(&dw_empty[sw], (uint32_t) ((dw_c / kDW - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ta = tA + ((uint32_t) (32 * q) << 16) + sa * kStCols;
+                tmem_st16(ta, col);
+                tmem_st16(ta + 16, col + 16);
+                tmem_st16(ta + 32, col + 32);
+                tmem_st16(ta + 48, col + 48);
+                uint16_t* dw = sDW + (size_t) sw * (Cfg::kDWStage / 2);
+#pragma unroll
+                for (int s2 = 0; s2 < 4; s2++) dw[s2 * kTqM + r] = dbits[s2];
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&a_full[sa]);
+                    mbar_arrive(&dw_full[sw]);
+                }
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[rs]);
+        }
+        if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
+    } else if (warp >= kTqEpiWarp0) {
+        // ---------------- epilogue ----------------
+        // warp 12 + 4 role + q owns rows 32q + lane and tokens role, role + 2, role + 4, role + 6 of every item.
+        const int q = warp & 3, role = (warp - kTqEpiWarp0) >> 2;
+        const int r = 32 * q + lane;
+        constexpr int NT = kTqN / 2;
+        int sd_c = 0, dw_c = 0;
+        bool ok = true;
+        float gsave[NT];  // gate/up: g of the group's gate item, until its up item is done
+        for (int j = 0; ok; j++) {
+            const int gid = group_of(j);
+            if (gid >= n_groups) break;
+            const Entry en = work_entry(w, gid / args.m_tiles);
+            const int mt = gid % args.m_tiles;
+            const int mat = j % G, bb = (j / G) % kBB;
+            const uint8_t* buf = sB + (size_t) bb * Cfg::kBBuf;
+            const float2* sc = reinterpret_cast<const float2*>(buf + Cfg::kBBytes);  // [K step][token] {d, sum q}
+            // Per token: A[] holds level-1 nodes a_j waiting for their partner a_(j+8), B[] level-2 nodes b_j (then
+            // level-3 c_j) waiting for theirs.  The stages run in an order that finishes pairs early (tq_order).
+            float A[NT][P == 64 ? 2 : P == 32 ? 4 : 8];
+            float B[NT][4];
+            float res[NT];
+#pragma unroll
+            for (int i = 0; i < S; i++) {
+                const int m = tq_order<P>(i);
+                const int c = sd_c + i, cw = dw_c + i;
+                const int sd = c % kD, sw = cw % kDW;
+                if (!tq_wait(&d_full[sd], (uint32_t) ((c / kD) & 1)) || !tq_wait(&dw_full[sw], (uint32_t) ((cw / kDW) & 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint16_t* dw = sDW + (size_t) sw * (Cfg::kDWStage / 2);
+                float dws[4];
+#pragma unroll
+                for (int s = 0; s < 4; s++) dws[s] = f16_to_f32(dw[s * kTqM + r]);
+                const uint32_t td = tD + ((uint32_t) (32 * q) << 16) + sd * kStCols;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    uint32_t v[32];  // slot s, token t at column 8 s + t (the K steps of half h)
+                    tmem_ld32(td + (uint32_t) h * 32, v);
+                    tmem_wait_ld();
+                    if (h == 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) {
+                            mbar_arrive(&d_empty[sd]);
+                            mbar_arrive(&dw_empty[sw]);
+                        }
+                    }
+#pragma unroll
+                    for (int tt = 0; tt < NT; tt++) {
+                        const int t = 2 * tt + role;
+                        if (t >= en.n) continue;  // uniform across the warp
+                        float p[4];
+#pragma unroll
+                        for (int s = 0; s < 4; s++) {
+                            const int k = 2 * tq_block<P>(m, s) + h;
+                            const float2 dsq = sc[k * kTqN + t];
+                            const int seed = 0x4B400000 - __float_as_int(dsq.y);
+                            // t is runtime (role): pick between two constant register indices
+                            const uint32_t vt = role ? v[8 * s + 2 * tt + 1] : v[8 * s + 2 * tt];
+                            const float f = __fsub_rn(__int_as_float(seed + (int) vt), 12582912.0f);
+                            p[s] = __fmul_rn(__fmul_rn(dws[s], dsq.x), f);
+                        }
+                        // level-1 nodes of half h of this stage, and their place in the tree
+                        if (P == 64) {
+                            // a_(2m+h) = ((0 + p_(2m+h)) + p_(2m+h+32)) + ((0 + p_(2m+h+16)) + p_(2m+h+48))
+                            const float a = __fadd_rn(__fadd_rn(__fadd_rn(0.f, p[0]), p[2]),
+                                                      __fadd_rn(__fadd_rn(0.f, p[1]), p[3]));
+                            // order m = 0 4 1 5 2 6 3 7: a_j (j < 8) waits in A, a_(j+8) makes b_j
+                            if (m < 4) {
+                                A[tt][h] = a;
+                            } else {
+                                const float bj = __fadd_rn(A[tt][h], a);  // b_(2(m-4)+h)
+                                const int jb = 2 * (m - 4) + h;
+                                if (jb < 4) B[tt][jb] = bj;
+                                else B[tt][jb - 4] = __fadd_rn(B[tt][jb - 4], bj);  // c_(jb-4)
+                            }
+                        } else if (P == 32) {
+                            // a_(4m+h) from p_(4m+h), p_(4m+h+16); a_(4m+2+h) from p_(4m+2+h), p_(4m+2+h+16)
+                            const float a0 = __fadd_rn(__fadd_rn(0.f, p[0]), __fadd_rn(0.f, p[2]));
+                            const float a1 = __fadd_rn(__fadd_rn(0.f, p[1]), __fadd_rn(0.f, p[3]));
+                            // order m = 0 2 1 3
+                            if (m < 2) {
+                                A[tt][2 * h] = a0;
+                                A[tt][2 * h + 1] = a1;
+                            } else {
+                                const float b0 = __fadd_rn(A[tt][2 * h], a0), b1 = __fadd_rn(A[tt][2 * h + 1], a1);
+                                if (m == 2) {  // b_h, b_(2+h)
+                                    B[tt][h] = b0;
+                                    B[tt][2 + h] = b1;
+                                } else {  // c_h, c_(2+h)
+                                    B[tt][h] = __fadd_rn(B[tt][h], b0);
+                                    B[tt][2 + h] = __fadd_rn(B[tt][2 + h], b1);
+                                }
+                            }
+                        } else {
+                            // lanes 8m + 2s + h: a = (0 + p) + 0 (lanes 16..31 add nothing)
+#pragma unroll
+                            for (int s = 0; s < 4; s++) {
+                                const float a = __fadd_rn(__fadd_rn(0.f, p[s]), 0.f);
+                                if (m == 0) {
+                                    A[tt][2 * s + h] = a;
+                                } else {
+                                    const float bj = __fadd_rn(A[tt][2 * s + h], a);  // b_(2s+h)
+                                    const int jb = 2 * s + h;
+                                    if (jb < 4) B[tt][jb] = bj;
+                                    else B[tt][jb - 4] = __fadd_rn(B[tt][jb - 4], bj);
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            sd_c += S;
+            dw_c += S;
+            if (!ok) break;
+            // B now holds c_0..c_3: d_j = c_j + c_(j+2), result d_0 + d_1
+#pragma unroll
+            for (int tt = 0; tt < NT; tt++)
+                res[tt] = __fadd_rn(__fadd_rn(B[tt][0], B[tt][2]), __fadd_rn(B[tt][1], B[tt][3]));
+            if (mat == G - 1) {  // the activation buffer (scales) is no longer needed
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&b_empty[bb]);
+            }
+            if (MODE == 1) {
+                const int row = mt * kTqM + r;
+#pragma unroll
+                for (int tt = 0; tt < NT; tt++) {
+                    const int t = 2 * tt + role;
+                    if (t < en.n) down_row(w, args.y, en.beg + t, args.n_out)[row] = res[tt];
+                }
+            } else if (mat == 0) {
+#pragma unroll
+                for (int tt = 0; tt < NT; tt++) gsave[tt] = res[tt];
+            } else {
+                // SwiGLU, then the q8_1 rule over the warp's 32 rows (one 32-value block of h)
+                const int nb = args.n_out / 32;
+                const int blk = (mt * kTqM + 32 * q) / 32;
+#pragma unroll
+                for (int tt = 0; tt < NT; tt++) {
+                    const int t = 2 * tt + role;
+                    if (t >= en.n) break;  // uniform across the warp
+                    const float hv = silu_mul(gsave[tt], res[tt]);
+                    quant_ka_warp(hv, args.ha + ((size_t) (en.beg + t) * nb + blk) * kKaBlock, lane, args.ha_q2 != 0);
+                }
+            }
+        }
+        if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
+        if (MODE == 1) ep_signal_done(w.ep_done, gridDim.x * 8);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+}
+
+namespace {
+
+template <int MODE, int P>
+cudaError_t launch_tq(const CUtensorMap* maps, const TqArgs& a, cudaStream_t s) {
+    const size_t smem = TqCfg<MODE, P>::smem;
+    cudaError_t err =
+        cudaFuncSetAttribute(tq_expert_kernel<MODE, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (err != cudaSuccess) return err;
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    tq_expert_kernel<MODE, P><<<nsm, kTqThreads, smem, s>>>(maps[0], maps[1], maps[2], maps[3], a);
+    return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch_tq_p(int P, const CUtensorMap* maps, const TqArgs& a, cudaStream_t s) {
+    if (P == 16) return launch_tq<MODE, 16>(maps, a, s);
+    if (P == 32) return launch_tq<MODE, 32>(maps, a, s);
+    if (P == 64) return launch_tq<MODE, 64>(maps, a, s);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace
+
+bool tq_qualifies(int H, int F) {
+    const auto okp = [](int n) { return n == 512 || n == 1024 || n == 2048; };
+    return okp(H) && okp(F);
+}
+
+cudaError_t launch_tq_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, Work w, int n_expert, KAct xa,
+                              KAct ha, int down_q2, int n_embd, int n_ff, cudaStream_t s) {
+    const int rb = (n_embd / 64) * 18;
+    const int64_t routed_rows = (int64_t) n_ff * n_expert;
+    CUtensorMap maps[4];
+    const bool ok = weight_map(&maps[0], gate.base, routed_rows, rb) && weight_map(&maps[1], up.base, routed_rows, rb) &&
+                    weight_map(&maps[2], sgate.base ? sgate.base : gate.base, n_ff, rb) &&
+                    weight_map(&maps[3], sup.base ? sup.base : up.base, n_ff, rb);
+    if (!ok) return cudaErrorInvalidValue;
+    TqArgs a{};
+    a.w = w;
+    a.act = xa.base;
+    a.m_tiles = n_ff / kTqM;
+    a.rows_per_expert = n_ff;
+    a.n_out = n_ff;
+    a.ha = ha.base;
+    a.ha_q2 = down_q2;
+    return launch_tq_p<0>(n_embd / 32, maps, a, s);
+}
+
+cudaError_t launch_tq_down(Matrix down, Matrix sdown, Work w, int n_expert, KAct ha, float* y, int n_ff, int n_embd,
+                           cudaStream_t s) {
+    const int rb = (n_ff / 64) * 18;
+    const int64_t routed_rows = (int64_t) n_embd * n_expert;
+    CUtensorMap maps[4];
+    const uint8_t* sd = sdown.base ? sdown.base : down.base;
+    const bool ok = weight_map(&maps[0], down.base, routed_rows, rb) && weight_map(&maps[2], sd, n_embd, rb);
+    if (!ok) return cudaErrorInvalidValue;
+    maps[1] = maps[0];
+    maps[3] = maps[2];
+    TqArgs a{};
+    a.w = w;
+    a.act = ha.base;
+    a.m_tiles = n_embd / kTqM;
+    a.rows_per_expert = n_embd;
+    a.n_out = n_embd;
+    a.y = y;
+    return launch_tq_p<1>(n_ff / 32, maps, a, s);
+}
+
+}  // namespace smoe

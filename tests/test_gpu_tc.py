@@ -110,9 +110,9 @@ def test_path_selection(cuda):
     spec, _ = synth.config_spec(1)
     m = api.MoeLayer(synth.make_layer(spec, 0, cuda), 8, cuda)
     f = _lib.lib().smoe_expert_path_for
-    assert f(C.byref(m.c), 8) == 1 and f(C.byref(m.c), 4096) == 2 and f(C.byref(m.c), 1) == 3
+    assert f(C.byref(m.c), 8) == 4 and f(C.byref(m.c), 4096) == 2 and f(C.byref(m.c), 1) == 3
     iq = synth.LayerSpec(n_embd=512, n_ff=512, n_expert=16, k=4, gu_type=synth.IQ2_S, seed=3)
     mi = api.MoeLayer(synth.make_layer(iq, 0, cuda), 8, cuda)
-    assert f(C.byref(mi.c), 4096) == 1   # IQ2_S stays on the SIMT kernels
+    assert f(C.byref(mi.c), 4096) == 1 and f(C.byref(mi.c), 8) == 1  # IQ2_S stays on the SIMT kernels
     with pytest.raises(api.SmoeError):
-        api.set_expert_path(4)
+        api.set_expert_path(5)
