@@ -123,7 +123,8 @@ struct TqCfg {
     static constexpr uint32_t kSBytes = P * kTqN * 8; // [K step][token] {d_x f32, sum q}
     static constexpr uint32_t kBBuf = kBBytes + kSBytes;
     static constexpr uint32_t kDWStage = 4 * kTqM * 2;  // fp16 block scales [slot][row]
-    static constexpr size_t smem = (size_t) kRaw * kRawItem + kBB * kBBuf + kDW * kDWStage + 64 * 8 + 1024;
+    static constexpr uint32_t kXch = 3 * 4 * kTqN * 32 * 4;  // d_1 hand-over (2 buffers) and g, per lane quarter
+    static constexpr size_t smem = (size_t) kRaw * kRawItem + kBB * kBBuf + kDW * kDWStage + kXch + 64 * 8 + 1024;
     static_assert(smem <= 232448, "shared memory per block");
 };
 
@@ -154,7 +155,8 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
     uint8_t* sRaw = smem;                                          // [kRaw][QS][128 rows][144 B]
     uint8_t* sB = sRaw + (size_t) kRaw * Cfg::kRawItem;            // [kBB][kBBuf]
     uint16_t* sDW = reinterpret_cast<uint16_t*>(sB + kBB * Cfg::kBBuf);  // [kDW][4][128]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sDW) + kDW * Cfg::kDWStage);
+    float* sX = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sDW) + kDW * Cfg::kDWStage);  // [2][4][8][32]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sX) + Cfg::kXch);
     uint64_t* raw_full = bars;            // TMA tx
     uint64_t* raw_empty = raw_full + 4;   // decoders (8 warps)
     uint64_t* b_full = raw_empty + 4;     // 64 producer threads (cp.async)
@@ -165,7 +167,9 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
     uint64_t* d_empty = d_full + kD;      // epilogue warps
     uint64_t* dw_full = d_empty + kD;     // the 4 decoder warps of the stage
     uint64_t* dw_empty = dw_full + kDW;   // epilogue warps
-    uint64_t* mma_done = dw_empty + kDW;
+    uint64_t* x_full = dw_empty + kDW;    // [2][4] h = 1 warp -> h = 0 warp
+    uint64_t* x_empty = x_full + 8;       // [2][4] h = 0 warp -> h = 1 warp
+    uint64_t* mma_done = x_empty + 8;
     __shared__ uint32_t s_tmem;
 
     const Work w = args.w;
@@ -191,6 +195,10 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
         for (int i = 0; i < kDW; i++) {
             mbar_init(&dw_full[i], 4);
             mbar_init(&dw_empty[i], 8);
+        }
+        for (int i = 0; i < 8; i++) {
+            mbar_init(&x_full[i], 1);
+            mbar_init(&x_empty[i], 1);
         }
         mbar_init(mma_done, 1);
         fence_mbar_init();
@@ -391,13 +399,14 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
         if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
     } else if (warp >= kTqEpiWarp0) {
         // ---------------- epilogue ----------------
-        // warp 12 + 4 role + q owns rows 32q + lane and tokens role, role + 2, role + 4, role + 6 of every item.
-        const int q = warp & 3, role = (warp - kTqEpiWarp0) >> 2;
+        // Warp 12 + 4 h + q owns rows 32q + lane and the partials of half h (K steps 2 b + h) of every token.  The
+        // reference's tree keeps the two parities apart until its last addition (a_j, b_j, c_j and d_j only meet
+        // nodes of the same parity), so each warp finishes d_h and the h = 1 warp hands d_1 over once per item.
+        const int q = warp & 3, hh = (warp - kTqEpiWarp0) >> 2;
         const int r = 32 * q + lane;
-        constexpr int NT = kTqN / 2;
         int sd_c = 0, dw_c = 0;
         bool ok = true;
-        float gsave[NT];  // gate/up: g of the group's gate item, until its up item is done
+        float* gs = sX + (size_t) 2 * 4 * kTqN * 32 + (size_t) q * kTqN * 32;  // gate/up: g until the up item
         for (int j = 0; ok; j++) {
             const int gid = group_of(j);
             if (gid >= n_groups) break;
@@ -406,11 +415,10 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
             const int mat = j % G, bb = (j / G) % kBB;
             const uint8_t* buf = sB + (size_t) bb * Cfg::kBBuf;
             const float2* sc = reinterpret_cast<const float2*>(buf + Cfg::kBBytes);  // [K step][token] {d, sum q}
-            // Per token: A[] holds level-1 nodes a_j waiting for their partner a_(j+8), B[] level-2 nodes b_j (then
-            // level-3 c_j) waiting for theirs.  The stages run in an order that finishes pairs early (tq_order).
-            float A[NT][P == 64 ? 2 : P == 32 ? 4 : 8];
-            float B[NT][4];
-            float res[NT];
+            // Per token: A[] holds level-1 nodes a_j of parity h waiting for a_(j+8); B[] b_h, b_(2+h), then c_h,
+            // c_(2+h).  The stages run in an order that finishes pairs early (tq_order).
+            float A[kTqN][P == 64 ? 1 : P == 32 ? 2 : 4];
+            float B[kTqN][2];
 #pragma unroll
             for (int i = 0; i < S; i++) {
                 const int m = tq_order<P>(i);
@@ -421,85 +429,62 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                     break;
                 }
                 tc_fence_after();
+                uint32_t v[32];  // slot s, token t at column 8 s + t (the K steps 2 b + h)
+                tmem_ld32(tD + ((uint32_t) (32 * q) << 16) + sd * kStCols + (uint32_t) hh * 32, v);
                 const uint16_t* dw = sDW + (size_t) sw * (Cfg::kDWStage / 2);
                 float dws[4];
 #pragma unroll
-                for (int s = 0; s < 4; s++) dws[s] = f16_to_f32(dw[s * kTqM + r]);
-                const uint32_t td = tD + ((uint32_t) (32 * q) << 16) + sd * kStCols;
+                for (int s2 = 0; s2 < 4; s2++) dws[s2] = f16_to_f32(dw[s2 * kTqM + r]);
+                tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&d_empty[sd]);
+                    mbar_arrive(&dw_empty[sw]);
+                }
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    uint32_t v[32];  // slot s, token t at column 8 s + t (the K steps of half h)
-                    tmem_ld32(td + (uint32_t) h * 32, v);
-                    tmem_wait_ld();
-                    if (h == 1) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) {
-                            mbar_arrive(&d_empty[sd]);
-                            mbar_arrive(&dw_empty[sw]);
-                        }
+                for (int t = 0; t < kTqN; t++) {
+                    if (t >= en.n) break;  // uniform across the warp
+                    float p[4];
+#pragma unroll
+                    for (int s = 0; s < 4; s++) {
+                        const int k = 2 * tq_block<P>(m, s) + hh;
+                        const float2 dsq = sc[k * kTqN + t];
+                        const int seed = 0x4B400000 - __float_as_int(dsq.y);
+                        const float f = __fsub_rn(__int_as_float(seed + (int) v[8 * s + t]), 12582912.0f);
+                        p[s] = __fmul_rn(__fmul_rn(dws[s], dsq.x), f);
                     }
-#pragma unroll
-                    for (int tt = 0; tt < NT; tt++) {
-                        const int t = 2 * tt + role;
-                        if (t >= en.n) continue;  // uniform across the warp
-                        float p[4];
+                    if (P == 64) {
+                        // a_(2m+h) = ((0 + p_(2m+h)) + p_(2m+h+32)) + ((0 + p_(2m+h+16)) + p_(2m+h+48))
+                        const float a = __fadd_rn(__fadd_rn(__fadd_rn(0.f, p[0]), p[2]),
+                                                  __fadd_rn(__fadd_rn(0.f, p[1]), p[3]));
+                        // order m = 0 4 1 5 2 6 3 7
+                        if (m < 4) A[t][0] = a;
+                        else if (m < 6) B[t][m - 4] = __fadd_rn(A[t][0], a);                        // b_(2(m-4)+h)
+                        else B[t][m - 6] = __fadd_rn(B[t][m - 6], __fadd_rn(A[t][0], a));           // c
+                    } else if (P == 32) {
+                        // a_(4m+h) from p_(4m+h), p_(4m+h+16); a_(4m+2+h) from p_(4m+2+h), p_(4m+2+h+16)
+                        const float a0 = __fadd_rn(__fadd_rn(0.f, p[0]), __fadd_rn(0.f, p[2]));
+                        const float a1 = __fadd_rn(__fadd_rn(0.f, p[1]), __fadd_rn(0.f, p[3]));
+                        // order m = 0 2 1 3
+                        if (m < 2) {
+                            A[t][0] = a0;
+                            A[t][1] = a1;
+                        } else if (m == 2) {
+                            B[t][0] = __fadd_rn(A[t][0], a0);  // b_h
+                            B[t][1] = __fadd_rn(A[t][1], a1);  // b_(2+h)
+                        } else {
+                            B[t][0] = __fadd_rn(B[t][0], __fadd_rn(A[t][0], a0));  // c_h
+                            B[t][1] = __fadd_rn(B[t][1], __fadd_rn(A[t][1], a1));  // c_(2+h)
+                        }
+                    } else {
+                        // lanes 8m + 2s + h hold one partial each (lanes 16..31 nothing): a = (0 + p) + 0
 #pragma unroll
                         for (int s = 0; s < 4; s++) {
-                            const int k = 2 * tq_block<P>(m, s) + h;
-                            const float2 dsq = sc[k * kTqN + t];
-                            const int seed = 0x4B400000 - __float_as_int(dsq.y);
-                            // t is runtime (role): pick between two constant register indices
-                            const uint32_t vt = role ? v[8 * s + 2 * tt + 1] : v[8 * s + 2 * tt];
-                            const float f = __fsub_rn(__int_as_float(seed + (int) vt), 12582912.0f);
-                            p[s] = __fmul_rn(__fmul_rn(dws[s], dsq.x), f);
-                        }
-                        // level-1 nodes of half h of this stage, and their place in the tree
-                        if (P == 64) {
-                            // a_(2m+h) = ((0 + p_(2m+h)) + p_(2m+h+32)) + ((0 + p_(2m+h+16)) + p_(2m+h+48))
-                            const float a = __fadd_rn(__fadd_rn(__fadd_rn(0.f, p[0]), p[2]),
-                                                      __fadd_rn(__fadd_rn(0.f, p[1]), p[3]));
-                            // order m = 0 4 1 5 2 6 3 7: a_j (j < 8) waits in A, a_(j+8) makes b_j
-                            if (m < 4) {
-                                A[tt][h] = a;
-                            } else {
-                                const float bj = __fadd_rn(A[tt][h], a);  // b_(2(m-4)+h)
-                                const int jb = 2 * (m - 4) + h;
-                                if (jb < 4) B[tt][jb] = bj;
-                                else B[tt][jb - 4] = __fadd_rn(B[tt][jb - 4], bj);  // c_(jb-4)
-                            }
-                        } else if (P == 32) {
-                            // a_(4m+h) from p_(4m+h), p_(4m+h+16); a_(4m+2+h) from p_(4m+2+h), p_(4m+2+h+16)
-                            const float a0 = __fadd_rn(__fadd_rn(0.f, p[0]), __fadd_rn(0.f, p[2]));
-                            const float a1 = __fadd_rn(__fadd_rn(0.f, p[1]), __fadd_rn(0.f, p[3]));
-                            // order m = 0 2 1 3
-                            if (m < 2) {
-                                A[tt][2 * h] = a0;
-                                A[tt][2 * h + 1] = a1;
-                            } else {
-                                const float b0 = __fadd_rn(A[tt][2 * h], a0), b1 = __fadd_rn(A[tt][2 * h + 1], a1);
-                                if (m == 2) {  // b_h, b_(2+h)
-                                    B[tt][h] = b0;
-                                    B[tt][2 + h] = b1;
-                                } else {  // c_h, c_(2+h)
-                                    B[tt][h] = __fadd_rn(B[tt][h], b0);
-                                    B[tt][2 + h] = __fadd_rn(B[tt][2 + h], b1);
-                                }
-                            }
-                        } else {
-                            // lanes 8m + 2s + h: a = (0 + p) + 0 (lanes 16..31 add nothing)
-#pragma unroll
-                            for (int s = 0; s < 4; s++) {
-                                const float a = __fadd_rn(__fadd_rn(0.f, p[s]), 0.f);
-                                if (m == 0) {
-                                    A[tt][2 * s + h] = a;
-                                } else {
-                                    const float bj = __fadd_rn(A[tt][2 * s + h], a);  // b_(2s+h)
-                                    const int jb = 2 * s + h;
-                                    if (jb < 4) B[tt][jb] = bj;
-                                    else B[tt][jb - 4] = __fadd_rn(B[tt][jb - 4], bj);
-                                }
-                            }
+                            const float a = __fadd_rn(__fadd_rn(0.f, p[s]), 0.f);
+                            if (m == 0) A[t][s] = a;
+                            else if (s < 2) B[t][s] = __fadd_rn(A[t][s], a);                        // b_(2s+h)
+                            else B[t][s - 2] = __fadd_rn(B[t][s - 2], __fadd_rn(A[t][s], a));       // c
                         }
                     }
                 }
@@ -507,36 +492,50 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
             sd_c += S;
             dw_c += S;
             if (!ok) break;
-            // B now holds c_0..c_3: d_j = c_j + c_(j+2), result d_0 + d_1
-#pragma unroll
-            for (int tt = 0; tt < NT; tt++)
-                res[tt] = __fadd_rn(__fadd_rn(B[tt][0], B[tt][2]), __fadd_rn(B[tt][1], B[tt][3]));
             if (mat == G - 1) {  // the activation buffer (scales) is no longer needed
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&b_empty[bb]);
             }
-            if (MODE == 1) {
-                const int row = mt * kTqM + r;
-#pragma unroll
-                for (int tt = 0; tt < NT; tt++) {
-                    const int t = 2 * tt + role;
-                    if (t < en.n) down_row(w, args.y, en.beg + t, args.n_out)[row] = res[tt];
+            // d_h = c_h + c_(2+h); the h = 1 warp hands d_1 to the h = 0 warp, which adds d_0 + d_1
+            const int xb = j & 1;
+            float* xs = sX + ((size_t) xb * 4 + q) * kTqN * 32;
+            uint64_t* xf = &x_full[xb * 4 + q];
+            uint64_t* xe = &x_empty[xb * 4 + q];
+            const uint32_t xpar = (uint32_t) ((j / 2) & 1);
+            if (hh == 1) {
+                if (j >= 2 && !tq_wait(xe, xpar ^ 1u)) {
+                    ok = false;
+                    break;
                 }
-            } else if (mat == 0) {
 #pragma unroll
-                for (int tt = 0; tt < NT; tt++) gsave[tt] = res[tt];
-            } else {
-                // SwiGLU, then the q8_1 rule over the warp's 32 rows (one 32-value block of h)
-                const int nb = args.n_out / 32;
-                const int blk = (mt * kTqM + 32 * q) / 32;
+                for (int t = 0; t < kTqN; t++)
+                    if (t < en.n) xs[t * 32 + lane] = __fadd_rn(B[t][0], B[t][1]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(xf);
+                continue;
+            }
+            if (!tq_wait(xf, xpar)) {
+                ok = false;
+                break;
+            }
+            const int nb = args.n_out / 32;
+            const int blk = (mt * kTqM + 32 * q) / 32;
 #pragma unroll
-                for (int tt = 0; tt < NT; tt++) {
-                    const int t = 2 * tt + role;
-                    if (t >= en.n) break;  // uniform across the warp
-                    const float hv = silu_mul(gsave[tt], res[tt]);
+            for (int t = 0; t < kTqN; t++) {
+                if (t >= en.n) break;  // uniform across the warp
+                const float res = __fadd_rn(__fadd_rn(B[t][0], B[t][1]), xs[t * 32 + lane]);
+                if (MODE == 1) {
+                    down_row(w, args.y, en.beg + t, args.n_out)[mt * kTqM + r] = res;
+                } else if (mat == 0) {
+                    gs[t * 32 + lane] = res;
+                } else {
+                    // SwiGLU, then the q8_1 rule over the warp's 32 rows (one 32-value block of h)
+                    const float hv = silu_mul(gs[t * 32 + lane], res);
                     quant_ka_warp(hv, args.ha + ((size_t) (en.beg + t) * nb + blk) * kKaBlock, lane, args.ha_q2 != 0);
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(xe);
         }
         if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
         if (MODE == 1) ep_signal_done(w.ep_done, gridDim.x * 8);
