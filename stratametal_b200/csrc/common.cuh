@@ -269,6 +269,18 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// tcgen05.ld completes asynchronously: its destination registers hold the data only after tcgen05.wait::ld.  The
+// compiler sees the load's outputs as ready at once, so the wait names the loaded registers (in and out): no use
+// of them can be scheduled before it.
+#define SMOE_R8(a, o) "+r"(a[o + 0]), "+r"(a[o + 1]), "+r"(a[o + 2]), "+r"(a[o + 3]), "+r"(a[o + 4]), "+r"(a[o + 5]), \
+                      "+r"(a[o + 6]), "+r"(a[o + 7])
+__device__ __forceinline__ void tmem_wait_ld8x4(uint32_t (&a)[8], uint32_t (&b)[8], uint32_t (&c)[8], uint32_t (&d)[8]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : SMOE_R8(a, 0), SMOE_R8(b, 0), SMOE_R8(c, 0), SMOE_R8(d, 0)::"memory");
+}
+__device__ __forceinline__ void tmem_wait_ld32(uint32_t (&a)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : SMOE_R8(a, 0), SMOE_R8(a, 8), SMOE_R8(a, 16), SMOE_R8(a, 24)::"memory");
+}
+
 // 16 consecutive 32-bit columns of this thread's tensor-memory lane (the warp writes lanes 32 (warp % 4) + 0..31).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
     asm volatile(
@@ -280,5 +292,14 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
 }
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// tcgen05.st reads its source registers asynchronously too: the wait names them, so they stay live and unchanged
+// until the store has completed.
+__device__ __forceinline__ void tmem_wait_st16(uint32_t* a) {
+    asm volatile("tcgen05.wait::st.sync.aligned;" : SMOE_R8(a, 0), SMOE_R8(a, 8)::"memory");
+}
+__device__ __forceinline__ void tmem_wait_st32(uint32_t* a) {
+    asm volatile("tcgen05.wait::st.sync.aligned;" : SMOE_R8(a, 0), SMOE_R8(a, 8), SMOE_R8(a, 16), SMOE_R8(a, 24)::"memory");
+}
 
 }  // namespace smoe

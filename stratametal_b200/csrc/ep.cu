@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(uint8_t* __restrict__ 
 }
 
 // One 32-value q8_1 block (36 bytes) into the SIMT kernels' layout: the words of quant_ka_warp, the scale read
-// back from its fp16 bits, the sum of the q.
+// back from its fp16 bits, 0x4B400000 - the sum of the q.
 __device__ __forceinline__ void ka_from_q8_warp(const uint8_t* __restrict__ qb, uint8_t* __restrict__ blk48, int lane,
                                                 bool q2_layout) {
     const int q = (int) (int8_t) qb[4 + lane];
@@ -190,7 +190,7 @@ __device__ __forceinline__ void ka_from_q8_warp(const uint8_t* __restrict__ qb, 
     }
     if (lane < 8) reinterpret_cast<uint32_t*>(blk48)[lane] = word;
     if (lane == 8) reinterpret_cast<float*>(blk48)[8] = f16_to_f32((uint16_t) (qb[0] | (qb[1] << 8)));
-    if (lane == 9) reinterpret_cast<int*>(blk48)[9] = qs;
+    if (lane == 9) reinterpret_cast<int*>(blk48)[9] = 0x4B400000 - qs;
 }
 
 __global__ void __launch_bounds__(256) ep_receive_kernel(uint8_t* __restrict__ area, int expert_first, int n_local,

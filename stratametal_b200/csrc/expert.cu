@@ -489,7 +489,7 @@ __device__ __forceinline__ float partial_ka(const Dec& w, const uint8_t* blk) {
     const uint4 a0 = reinterpret_cast<const uint4*>(blk)[0];
     const uint4 a1 = reinterpret_cast<const uint4*>(blk)[1];
     const float2 ds = reinterpret_cast<const float2*>(blk)[4];
-    return partial<TYPE>(w, a0, a1, ds.x, __float_as_int(ds.y));
+    return partial<TYPE>(w, a0, a1, ds.x, 0x4B400000 - __float_as_int(ds.y));
 }
 
 // Layer-path dot: the dp4a chain starts from the bits of 1.5 * 2^23 minus the block's sum of q, so after the
@@ -512,7 +512,7 @@ __device__ __forceinline__ ActRegs load_act(const uint8_t* blk) {
     r.a1 = reinterpret_cast<const uint4*>(blk)[1];
     const float2 ds = reinterpret_cast<const float2*>(blk)[4];
     r.dx = ds.x;
-    r.seed = 0x4B400000 - __float_as_int(ds.y);
+    r.seed = __float_as_int(ds.y);
     return r;
 }
 

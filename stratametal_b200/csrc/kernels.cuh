@@ -14,7 +14,7 @@ constexpr int kMaxK = 64;
 
 // Activations in the expert kernels' layout ("ka"): per 32-value block 48 bytes = 8 words (Q2_0 weights:
 // byte b of word j of each half = value 4b + j of that 16-value half; IQ2_S weights: natural order), the q8_1
-// scale as f32 (the fp16 d read back), the sum of the 32 q, and 8 bytes of padding so every block is 16-byte
+// scale as f32 (the fp16 d read back), 0x4B400000 - the sum of the 32 q, and 8 bytes of padding so every block is 16-byte
 // aligned and a row of blocks is one bulk copy.
 constexpr int kKaBlock = 48;
 struct KAct {

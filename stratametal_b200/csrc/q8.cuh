@@ -37,7 +37,8 @@ __device__ __forceinline__ void quant_q8_1_warp(float xi, uint8_t* __restrict__ 
 
 // The same q8_1 rule, written in the expert kernels' layout (KAct): 8 words (permuted for Q2_0 weights:
 // byte b of word j of half h = value 16h + 4b + j; natural order otherwise), the stored scale read back as the
-// dot reads it (f32 of the fp16 d) and the sum of the 32 q.
+// dot reads it (f32 of the fp16 d) and 0x4B400000 - (the sum of the 32 q): the bits of 1.5 * 2^23 - sum q, the
+// seed of the exact integer-to-float step of the Q2_0 dot (see expert.cu).
 __device__ __forceinline__ void quant_ka_warp(float xi, uint8_t* __restrict__ blk48, int lane, bool q2_layout) {
     float amax = fabsf(xi);
 #pragma unroll
@@ -64,7 +65,7 @@ __device__ __forceinline__ void quant_ka_warp(float xi, uint8_t* __restrict__ bl
     }
     if (lane < 8) reinterpret_cast<uint32_t*>(blk48)[lane] = word;
     if (lane == 8) reinterpret_cast<float*>(blk48)[8] = f16_to_f32(f16_bits(d));
-    if (lane == 9) reinterpret_cast<int*>(blk48)[9] = qs;
+    if (lane == 9) reinterpret_cast<int*>(blk48)[9] = 0x4B400000 - qs;
 }
 
 // silu(g) * u (iq.metal:630-663).  exp is taken in fp64 and rounded to f32: that is the correctly rounded

@@ -421,7 +421,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                                         (uint32_t) m * (kTcK / 2) + (uint32_t) (8 * j0);
                     tmem_st16(ta, col);
                     if (NW == 4) tmem_st16(ta + 16, col + 16);
-                    tmem_wait_st();
+                    if constexpr (NW == 4) tmem_wait_st32(col);
+                    else tmem_wait_st16(col);
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&a_full[sa]);
@@ -466,7 +467,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_expert_kernel(const __grid_c
                     tmem_ld8(tbase + kMatCols + (uint32_t) c0, u8);
                     tmem_ld8(tbase + kMatCols + (uint32_t) (npad + c0), ul8);
                 }
-                tmem_wait_ld();
+                tmem_wait_ld8x4(g8, gl8, u8, ul8);
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
                     const float g = __fadd_rn(__uint_as_float(g8[i]), __uint_as_float(gl8[i]));

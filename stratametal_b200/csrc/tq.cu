@@ -91,14 +91,37 @@ __device__ __forceinline__ bool tq_wait(uint64_t* bar, uint32_t parity) {
     return __all_sync(0xffffffffu, ok);
 }
 
-// Block slot s (0..3) of stage m: the blocks whose partials finish tree nodes together (see the header).
-template <int P>
-__host__ __device__ constexpr int tq_block(int m, int s) {
-    return P == 64 ? m + 8 * s : P == 32 ? 2 * m + (s & 1) + 8 * (s >> 1) : 4 * m + s;
+// Packed f32x2 multiply and add with round-to-nearest: each lane rounds as the scalar operation does.  ptxas may
+// still fuse a packed multiply into a packed add that consumes it, so they are used only where no addition
+// takes a product.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+    float2 o;
+    asm("{ .reg .b64 x, y, z; mov.b64 x, {%2, %3}; mov.b64 y, {%4, %5}; mul.rn.f32x2 z, x, y; mov.b64 {%0, %1}, z; }"
+        : "=f"(o.x), "=f"(o.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return o;
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    float2 o;
+    asm("{ .reg .b64 x, y, z; mov.b64 x, {%2, %3}; mov.b64 y, {%4, %5}; add.rn.f32x2 z, x, y; mov.b64 {%0, %1}, z; }"
+        : "=f"(o.x), "=f"(o.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return o;
 }
 
-// The order in which an item's stages run: a stage's level-1 nodes meet their level-2 partners early, so the
-// epilogue keeps at most 6 (P = 64) or 8 values per token.
+// Block slot s (0..3) of stage m: the blocks whose partials finish tree nodes together.  For the K steps of
+// parity h (partials 2 b + h):
+//   P = 64: blocks m, m+8, m+16, m+24 -> a_(2m+h) (four partials, two per lane);
+//   P = 32: blocks m, m+8 -> a_(2m+h) and m+4, m+12 -> a_(2m+8+h): b_(2m+h) at once;
+//   P = 16: blocks 2m+s (s < 2) -> a_(4m+2s+h) and 2m+s+2 -> a_(4m+2s+8+h): b_(4m+2s+h) at once.
+template <int P>
+__host__ __device__ constexpr int tq_block(int m, int s) {
+    return P == 64 ? m + 8 * s : P == 32 ? m + (s == 1 ? 8 : s == 2 ? 4 : s == 3 ? 12 : 0) : 2 * m + s + (s >= 2 ? 2 : 0);
+}
+
+// The order in which an item's stages run, so that nodes meet their partners early: P = 64: a_j then a_(j+8)
+// (m = 0 4 1 5 2 6 3 7); P = 32: b_j then b_(j+4) (m = 0 2 1 3); P = 16: b_h, b_(2+h), then b_(4+h), b_(6+h).
+// The epilogue keeps at most 3 values per token.
 template <int P>
 __host__ __device__ constexpr int tq_order(int i) {
     return P == 64 ? (i >> 1) + 4 * (i & 1) : P == 32 ? (i >> 1) + 2 * (i & 1) : i;
@@ -384,7 +407,8 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                 uint16_t* dw = sDW + (size_t) sw * (Cfg::kDWStage / 2);
 #pragma unroll
                 for (int s2 = 0; s2 < 4; s2++) dw[s2 * kTqM + r] = dbits[s2];
-                tmem_wait_st();
+                tmem_wait_st32(col);
+                tmem_wait_st32(col + 32);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
@@ -417,7 +441,7 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
             const float2* sc = reinterpret_cast<const float2*>(buf + Cfg::kBBytes);  // [K step][token] {d, sum q}
             // Per token: A[] holds level-1 nodes a_j of parity h waiting for a_(j+8); B[] b_h, b_(2+h), then c_h,
             // c_(2+h).  The stages run in an order that finishes pairs early (tq_order).
-            float A[kTqN][P == 64 ? 1 : P == 32 ? 2 : 4];
+            float A[kTqN][1];
             float B[kTqN][2];
 #pragma unroll
             for (int i = 0; i < S; i++) {
@@ -435,7 +459,7 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                 float dws[4];
 #pragma unroll
                 for (int s2 = 0; s2 < 4; s2++) dws[s2] = f16_to_f32(dw[s2 * kTqM + r]);
-                tmem_wait_ld();
+                tmem_wait_ld32(v);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
@@ -445,46 +469,53 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
 #pragma unroll
                 for (int t = 0; t < kTqN; t++) {
                     if (t >= en.n) break;  // uniform across the warp
-                    float p[4];
+                    // p_s = (d_w * d_x) * (float) (sum code q - sum q), slots in pairs on the packed f32x2 path
+                    // (each lane of a packed operation rounds as the scalar one does)
+                    float2 sq[4];
 #pragma unroll
-                    for (int s = 0; s < 4; s++) {
-                        const int k = 2 * tq_block<P>(m, s) + hh;
-                        const float2 dsq = sc[k * kTqN + t];
-                        const int seed = 0x4B400000 - __float_as_int(dsq.y);
-                        const float f = __fsub_rn(__int_as_float(seed + (int) v[8 * s + t]), 12582912.0f);
-                        p[s] = __fmul_rn(__fmul_rn(dws[s], dsq.x), f);
+                    for (int s = 0; s < 4; s++) sq[s] = sc[(2 * tq_block<P>(m, s) + hh) * kTqN + t];  // {d_x, seed}
+                    const float2 kBias = make_float2(-12582912.0f, -12582912.0f);
+                    // Packed f32x2 only where no addition consumes the result (ptxas may fuse a packed multiply
+                    // into a following packed add, which would round once instead of twice): the integer-to-float
+                    // step and d_w * d_x.  The product with f and every addition stay scalar _rn operations,
+                    // which are never contracted.
+                    float2 pp[2];
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        const float2 f = add2_rn(
+                            make_float2(__int_as_float(__float_as_int(sq[2 * u].y) + (int) v[8 * (2 * u) + t]),
+                                        __int_as_float(__float_as_int(sq[2 * u + 1].y) + (int) v[8 * (2 * u + 1) + t])),
+                            kBias);
+                        const float2 dd = mul2_rn(make_float2(dws[2 * u], dws[2 * u + 1]), make_float2(sq[2 * u].x, sq[2 * u + 1].x));
+                        pp[u] = make_float2(__fmul_rn(dd.x, f.x), __fmul_rn(dd.y, f.y));
                     }
                     if (P == 64) {
                         // a_(2m+h) = ((0 + p_(2m+h)) + p_(2m+h+32)) + ((0 + p_(2m+h+16)) + p_(2m+h+48))
-                        const float a = __fadd_rn(__fadd_rn(__fadd_rn(0.f, p[0]), p[2]),
-                                                  __fadd_rn(__fadd_rn(0.f, p[1]), p[3]));
+                        const float a = __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), pp[1].x),
+                                                  __fadd_rn(__fadd_rn(0.f, pp[0].y), pp[1].y));
                         // order m = 0 4 1 5 2 6 3 7
                         if (m < 4) A[t][0] = a;
                         else if (m < 6) B[t][m - 4] = __fadd_rn(A[t][0], a);                        // b_(2(m-4)+h)
                         else B[t][m - 6] = __fadd_rn(B[t][m - 6], __fadd_rn(A[t][0], a));           // c
                     } else if (P == 32) {
-                        // a_(4m+h) from p_(4m+h), p_(4m+h+16); a_(4m+2+h) from p_(4m+2+h), p_(4m+2+h+16)
-                        const float a0 = __fadd_rn(__fadd_rn(0.f, p[0]), __fadd_rn(0.f, p[2]));
-                        const float a1 = __fadd_rn(__fadd_rn(0.f, p[1]), __fadd_rn(0.f, p[3]));
-                        // order m = 0 2 1 3
-                        if (m < 2) {
-                            A[t][0] = a0;
-                            A[t][1] = a1;
-                        } else if (m == 2) {
-                            B[t][0] = __fadd_rn(A[t][0], a0);  // b_h
-                            B[t][1] = __fadd_rn(A[t][1], a1);  // b_(2+h)
-                        } else {
-                            B[t][0] = __fadd_rn(B[t][0], __fadd_rn(A[t][0], a0));  // c_h
-                            B[t][1] = __fadd_rn(B[t][1], __fadd_rn(A[t][1], a1));  // c_(2+h)
-                        }
+                        // a_(2m+h) = (0 + p_(2m+h)) + (0 + p_(2m+h+16)) from blocks m, m+8; a_(2m+8+h) from m+4, m+12
+                        const float bj = __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), __fadd_rn(0.f, pp[0].y)),
+                                                   __fadd_rn(__fadd_rn(0.f, pp[1].x), __fadd_rn(0.f, pp[1].y)));  // b_(2m+h)
+                        // order m = 0 2 1 3: b_h, b_(4+h) -> c_h; b_(2+h), b_(6+h) -> c_(2+h)
+                        if (m < 2) B[t][m] = bj;
+                        else B[t][m - 2] = __fadd_rn(B[t][m - 2], bj);
                     } else {
-                        // lanes 8m + 2s + h hold one partial each (lanes 16..31 nothing): a = (0 + p) + 0
-#pragma unroll
-                        for (int s = 0; s < 4; s++) {
-                            const float a = __fadd_rn(__fadd_rn(0.f, p[s]), 0.f);
-                            if (m == 0) A[t][s] = a;
-                            else if (s < 2) B[t][s] = __fadd_rn(A[t][s], a);                        // b_(2s+h)
-                            else B[t][s - 2] = __fadd_rn(B[t][s - 2], __fadd_rn(A[t][s], a));       // c
+                        // lanes 4m + 2s + h (s < 2) and 4m + 2s + 8 + h hold one partial each (lanes 16..31 nothing):
+                        // a = (0 + p) + 0, b_(4m+2s+h) = a + a'
+                        const float2 b01 = make_float2(  // b_(4m+h) from slots 0, 2; b_(4m+2+h) from slots 1, 3
+                            __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), 0.f), __fadd_rn(__fadd_rn(0.f, pp[1].x), 0.f)),
+                            __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].y), 0.f), __fadd_rn(__fadd_rn(0.f, pp[1].y), 0.f)));
+                        if (m == 0) {
+                            B[t][0] = b01.x;
+                            B[t][1] = b01.y;
+                        } else {  // c_h = b_h + b_(4+h), c_(2+h) = b_(2+h) + b_(6+h)
+                            B[t][0] = __fadd_rn(B[t][0], b01.x);
+                            B[t][1] = __fadd_rn(B[t][1], b01.y);
                         }
                     }
                 }
