@@ -63,6 +63,18 @@ def check_equal(xs, outs, trs, want, wtr):
 
 
 @pytest.mark.parametrize("world", [2, 4])
+def test_ep_int8_tensor_cores_match_single(cuda, world):
+    # the int8 tensor-core kernels (path 4) store the down rows to the token ranks and signal from their epilogue
+    spec = synth.LayerSpec(n_embd=2048, n_ff=512, n_expert=64, k=10, seed=55)
+    sizes = [16, 5, 0, 11][:world]
+    xs = [synth.make_x(65 + r, n, spec.n_embd, cuda) for r, n in enumerate(sizes)]
+    want, wtr = single_reference(cuda, spec, xs, 4)
+    layers, views, outs, trs = run_group(cuda, spec, xs, 16, 4)
+    check_equal(xs, outs, trs, want, wtr)
+    views[0].close()
+
+
+@pytest.mark.parametrize("world", [2, 4])
 def test_ep_simt_matches_single(cuda, world):
     spec = synth.LayerSpec(n_embd=1024, n_ff=256, n_expert=64, k=8, seed=51)
     sizes = [13, 0, 7, 16][:world]  # ragged, one rank without tokens
@@ -154,7 +166,7 @@ def _two_gpu_worker(rank, world, port, q):
         Tm = 24
         sizes = [24, 17, 9, 24][:world]
         xs = [synth.make_x(100 + r, n, spec.n_embd, dev) for r, n in enumerate(sizes)]
-        api.set_expert_path(1)
+        api.set_expert_path(4)  # the int8 tensor-core kernels, whose down epilogue stores to the other GPU
         full = api.MoeLayer(synth.make_layer(spec, 0, dev), sum(sizes), dev)
         want = full.forward(torch.cat(xs))
         areas = ep.EpAreas.distributed(spec, Tm)
