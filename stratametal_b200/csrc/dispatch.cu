@@ -75,16 +75,17 @@ __device__ __forceinline__ int block_excl_scan(int v, int* warp_sums, int* total
 // min(count, 63), heaviest bucket first, ascending id inside a bucket (per-warp bucket counts, scanned
 // bucket-major then warp-minor, plus the rank among same-bucket lanes), then each expert cut into chunks of at
 // most sched.chunk slots.
-__device__ void build_sched(GroupTables g, Sched sched, int E, int* warp_sums) {
-    __shared__ int whist[32][64];
+// counts / offsets: the tables as this CTA holds them (shared memory when it just computed them); whist
+// (32 x 64 ints) and sorted (kMaxExperts ints): shared scratch.
+__device__ void build_sched(const int* counts, const int* offsets, int n_active, Sched sched, int E, int* warp_sums,
+                           int (*whist)[64], int* sorted) {
     __shared__ int bucket_off[64];
-    __shared__ int sorted[kMaxExperts];
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     for (int i = tid; i < 32 * 64; i += blockDim.x) whist[i / 64][i % 64] = 0;
     __syncthreads();
     const int e = tid;
-    const int cnt = e < E ? g.counts[e] : 0;
+    const int cnt = e < E ? counts[e] : 0;
     const int b = cnt > 0 ? 63 - min(cnt, 63) : -1;
     if (b >= 0) atomicAdd(&whist[warp][b], 1);
     __syncthreads();
@@ -98,27 +99,30 @@ __device__ void build_sched(GroupTables g, Sched sched, int E, int* warp_sums) {
         bucket_off[tid] = acc;
     }
     __syncthreads();
-    if (tid == 0) {
-        int off = 0;
-        for (int i = 0; i < 64; i++) {
-            const int t = bucket_off[i];
-            bucket_off[i] = off;
-            off += t;
+    if (tid < 32) {  // exclusive scan of the 64 bucket totals by one warp (two per lane)
+        const int a = bucket_off[2 * tid], b = bucket_off[2 * tid + 1];
+        int x = a + b;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (tid >= o) x += y;
         }
+        const int before = x - a - b;
+        bucket_off[2 * tid] = before;
+        bucket_off[2 * tid + 1] = before + a;
     }
     __syncthreads();
     const uint32_t same = __match_any_sync(0xffffffffu, b);
     if (b >= 0) sorted[bucket_off[b] + whist[warp][b] + __popc(same & lanemask_lt())] = e;
     __syncthreads();
-    const int n_active = g.n_active[0];
     const int ej = tid < n_active ? sorted[tid] : -1;
-    const int cj = ej >= 0 ? g.counts[ej] : 0;
+    const int cj = ej >= 0 ? counts[ej] : 0;
     const int chunk = sched.chunk;
     const int nch = (cj + chunk - 1) / chunk;
     int total = 0;
     const int off = block_excl_scan(nch, warp_sums, &total);
     if (ej >= 0) {
-        const int base = g.offsets[ej];
+        const int base = offsets[ej];
         for (int c = 0; c < nch; c++) {
             sched.e[off + c] = ej;
             sched.beg[off + c] = base + c * chunk;
@@ -128,7 +132,80 @@ __device__ void build_sched(GroupTables g, Sched sched, int E, int* warp_sums) {
     if (tid == 0) sched.count[0] = total;
 }
 
+// One CTA, up to kGroupWideMinTokens tokens (4 chunks of 64): every chunk's per-expert token masks are built once
+// and kept in shared memory; the counts, the exclusive offsets, the slots and the work list all come from them.
+constexpr int kGroupMaxChunks = kGroupWideMinTokens / 64;
 __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__ ids, int T, int k, int E,
+                                                     GroupTables g, int32_t* __restrict__ slot,
+                                                     int32_t* __restrict__ src, Sched sched, int with_sched,
+                                                     int skip_negative, int32_t* __restrict__ pair) {
+    __shared__ unsigned long long mask[kGroupMaxChunks][kMaxExperts];
+    __shared__ int cnt_s[kMaxExperts];
+    __shared__ int off_s[kMaxExperts];
+    __shared__ int warp_sums[32];
+    __shared__ int n_active_s;
+    const int tid = threadIdx.x;
+    const int nchunks = (T + 63) / 64;
+
+    for (int i = tid; i < nchunks * E; i += blockDim.x) mask[i / E][i % E] = 0ull;
+    __syncthreads();
+    for (int p = tid; p < T * k; p += blockDim.x) {
+        const int t = p / k;
+        const int e = ids[p];
+        if (e >= 0 && e < E) atomicOr(&mask[t >> 6][e], 1ull << (t & 63));
+    }
+    __syncthreads();
+    // counts -> exclusive offsets and the active list (experts with rows, ascending id)
+    int carry = 0, carry_act = 0;
+    for (int e0 = 0; e0 < E; e0 += blockDim.x) {
+        const int e = e0 + tid;
+        int cnt = 0;
+        if (e < E)
+            for (int c = 0; c < nchunks; c++) cnt += __popcll(mask[c][e]);
+        int tot, tot_act;
+        const int off = block_excl_scan(cnt, warp_sums, &tot);
+        const int act = block_excl_scan(cnt > 0 ? 1 : 0, warp_sums, &tot_act);
+        if (e < E) {
+            cnt_s[e] = cnt;
+            off_s[e] = carry + off;
+            g.counts[e] = cnt;
+            g.offsets[e] = carry + off;
+            if (cnt > 0) g.active[carry_act + act] = e;
+        }
+        carry += tot;
+        carry_act += tot_act;
+    }
+    if (tid == 0) {
+        g.offsets[E] = carry;
+        g.n_active[0] = carry_act;
+        n_active_s = carry_act;
+        g.work[0] = g.work[1] = g.work[2] = g.work[3] = 0;
+    }
+    __syncthreads();
+    // slots: expert base + the pairs of that expert in earlier chunks + the rank among this chunk's tokens
+    for (int i = tid; i < T * k; i += blockDim.x) {
+        const int t = i / k, c = t >> 6, tl = t & 63;
+        const int e = ids[i];
+        if (e < 0 || e >= E) {
+            slot[i] = -1;
+            if (!(skip_negative && e < 0)) atomicOr(&g_smoe_status, kDevBadId);
+            continue;
+        }
+        int pos = off_s[e] + __popcll(mask[c][e] & ((1ull << tl) - 1ull));
+        for (int cc = 0; cc < c; cc++) pos += __popcll(mask[cc][e]);
+        slot[i] = pos;
+        if (src) src[pos] = t;
+        if (pair) pair[pos] = i;
+    }
+    __syncthreads();
+    // the work list reuses the mask memory as its scratch
+    if (with_sched)
+        build_sched(cnt_s, off_s, n_active_s, sched, E, warp_sums, reinterpret_cast<int (*)[64]>(&mask[0][0]),
+                    reinterpret_cast<int*>(&mask[0][0]) + 32 * 64);
+}
+
+// Any number of tokens in one CTA (the stage entry points without chunk scratch): two passes over 64-token chunks.
+__global__ void __launch_bounds__(1024) group_kernel_any(const int32_t* __restrict__ ids, int T, int k, int E,
                                                      GroupTables g, int32_t* __restrict__ slot,
                                                      int32_t* __restrict__ src, Sched sched, int with_sched,
                                                      int skip_negative, int32_t* __restrict__ pair) {
@@ -197,7 +274,11 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__
             __syncthreads();
         }
     }
-    if (with_sched) build_sched(g, sched, E, warp_sums);
+    if (with_sched) {
+        __shared__ int whist[32][64];
+        __shared__ int sorted[kMaxExperts];
+        build_sched(g.counts, g.offsets, g.n_active[0], sched, E, warp_sums, whist, sorted);
+    }
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -246,7 +327,14 @@ __global__ void __launch_bounds__(1024) group_scan_kernel(int E, int nchunks, in
         g.work[0] = g.work[1] = g.work[2] = g.work[3] = 0;
     }
     __syncthreads();
-    if (with_sched) build_sched(g, sched, E, warp_sums);
+    if (with_sched) {
+        __shared__ int whist[32][64];
+        __shared__ int sorted[kMaxExperts];
+        __shared__ int n_act;
+        if (e == 0) n_act = tot_act;
+        __syncthreads();
+        build_sched(g.counts, g.offsets, n_act, sched, E, warp_sums, whist, sorted);
+    }
 }
 
 __global__ void __launch_bounds__(256) group_assign_kernel(const int32_t* __restrict__ ids, int T, int k, int E,
@@ -289,8 +377,12 @@ cudaError_t launch_group(const int32_t* ids, int T, int k, int E, GroupTables g,
         group_assign_kernel<<<nchunks, 256, 0, s>>>(ids, T, k, E, chunk_counts, slot, src, skip_negative, pair);
         return cudaGetLastError();
     }
-    group_kernel<<<1, 1024, 0, s>>>(ids, T, k, E, g, slot, src, sched ? *sched : Sched{}, sched ? 1 : 0,
-                                    skip_negative, pair);
+    if (T <= kGroupWideMinTokens)
+        group_kernel<<<1, 1024, 0, s>>>(ids, T, k, E, g, slot, src, sched ? *sched : Sched{}, sched ? 1 : 0,
+                                        skip_negative, pair);
+    else
+        group_kernel_any<<<1, 1024, 0, s>>>(ids, T, k, E, g, slot, src, sched ? *sched : Sched{}, sched ? 1 : 0,
+                                            skip_negative, pair);
     return cudaGetLastError();
 }
 
