@@ -114,17 +114,19 @@ __device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
 //   P = 64: blocks m, m+8, m+16, m+24 -> a_(2m+h) (four partials, two per lane);
 //   P = 32: blocks m, m+8 -> a_(2m+h) and m+4, m+12 -> a_(2m+8+h): b_(2m+h) at once;
 //   P = 16: blocks 2m+s (s < 2) -> a_(4m+2s+h) and 2m+s+2 -> a_(4m+2s+8+h): b_(4m+2s+h) at once.
+//   P = 64 (eight slots): blocks m, m+8, m+16, m+24 -> a_(2m+h) and m+4, m+12, m+20, m+28 -> a_(2m+8+h):
+//           b_(2m+h) at once (four partials per node, two per lane).
 template <int P>
 __host__ __device__ constexpr int tq_block(int m, int s) {
-    return P == 64 ? m + 8 * s : P == 32 ? m + (s == 1 ? 8 : s == 2 ? 4 : s == 3 ? 12 : 0) : 2 * m + s + (s >= 2 ? 2 : 0);
+    return P == 64 ? m + (s >= 4 ? 4 + 8 * (s - 4) : 8 * s)
+                   : P == 32 ? m + (s == 1 ? 8 : s == 2 ? 4 : s == 3 ? 12 : 0) : 2 * m + s + (s >= 2 ? 2 : 0);
 }
 
-// The order in which an item's stages run, so that nodes meet their partners early: P = 64: a_j then a_(j+8)
-// (m = 0 4 1 5 2 6 3 7); P = 32: b_j then b_(j+4) (m = 0 2 1 3); P = 16: b_h, b_(2+h), then b_(4+h), b_(6+h).
-// The epilogue keeps at most 3 values per token.
+// The order in which an item's stages run, so that nodes meet their partners early: P = 64 and P = 32: b_j then
+// b_(j+4) (m = 0 2 1 3); P = 16: b_h, b_(2+h), then b_(4+h), b_(6+h).  The epilogue keeps 2 values per token.
 template <int P>
 __host__ __device__ constexpr int tq_order(int i) {
-    return P == 64 ? (i >> 1) + 4 * (i & 1) : P == 32 ? (i >> 1) + 2 * (i & 1) : i;
+    return P == 16 ? i : (i >> 1) + 2 * (i & 1);
 }
 
 // One item = one 128-row tile of one matrix for one work entry.  Gate/up runs an entry's gate tile and its up
@@ -134,18 +136,19 @@ template <int MODE, int P>
 struct TqCfg {
     static constexpr int G = MODE == 0 ? 2 : 1;       // items per group (matrices of one tile)
     static constexpr int QS = P / 16;                 // raw quarters (8 blocks = 16 partials) per row
-    static constexpr int S = P / 8;                   // stages per item
+    static constexpr int NB = P == 64 ? 8 : 4;        // blocks (slots) per stage
+    static constexpr int S = P / (2 * NB);            // stages per item
     static constexpr uint32_t kRawItem = QS * kTqQuarter;
     static constexpr int kRaw = kRawItem > 40 * 1024 ? 2 : 4;  // items of raw weights in flight
-    static constexpr int kA = 4, kD = 4, kDW = 4;
+    static constexpr int kA = NB == 8 ? 2 : 4, kD = kA, kDW = 4;
     static constexpr int kBB = MODE == 0 || kRawItem > 40 * 1024 ? 2 : 4;  // activation buffers (groups)
-    static constexpr uint32_t kStCols = 64;           // one A or D stage: 8 K steps x 8 columns
+    static constexpr uint32_t kStCols = NB * 16;      // one A or D stage: 2 NB K steps x 8 columns
     static constexpr uint32_t kTmemCols = 512;
     static_assert((kA + kD) * kStCols <= kTmemCols, "tensor memory budget");
     static constexpr uint32_t kBBytes = P * 256;      // q words: [K step][2 core matrices][8 tokens][16 B]
     static constexpr uint32_t kSBytes = P * kTqN * 8; // [K step][token] {d_x f32, sum q}
     static constexpr uint32_t kBBuf = kBBytes + kSBytes;
-    static constexpr uint32_t kDWStage = 4 * kTqM * 2;  // fp16 block scales [slot][row]
+    static constexpr uint32_t kDWStage = NB * kTqM * 2;  // fp16 block scales [slot][row]
     static constexpr uint32_t kXch = 3 * 4 * kTqN * 32 * 4;  // d_1 hand-over (2 buffers) and g, per lane quarter
     static constexpr size_t smem = (size_t) kRaw * kRawItem + kBB * kBBuf + kDW * kDWStage + kXch + 64 * 8 + 1024;
     static_assert(smem <= 232448, "shared memory per block");
@@ -170,7 +173,7 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                                                                   TqArgs args) {
     using Cfg = TqCfg<MODE, P>;
     constexpr int G = Cfg::G, QS = Cfg::QS, S = Cfg::S, kRaw = Cfg::kRaw, kA = Cfg::kA, kD = Cfg::kD,
-                  kDW = Cfg::kDW, kBB = Cfg::kBB;
+                  kDW = Cfg::kDW, kBB = Cfg::kBB, NB = Cfg::NB;
     constexpr uint32_t kStCols = Cfg::kStCols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -323,12 +326,12 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                     tc_fence_after();
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // cp.async writes -> MMA reads
 #pragma unroll
-                    for (int s = 0; s < 4; s++)
+                    for (int s = 0; s < NB; s++)
 #pragma unroll
                         for (int h = 0; h < 2; h++) {
                             const int k = 2 * tq_block<P>(m, s) + h;
                             const uint64_t bd = umma_desc(buf + k * 256, 128, 256);
-                            umma_i8_ts(tD + sd * kStCols + (uint32_t) (h * 4 + s) * 8,
+                            umma_i8_ts(tD + sd * kStCols + (uint32_t) (h * NB + s) * 8,
                                        tA + sa * kStCols + (uint32_t) (s * 2 + h) * 8, bd, idesc);
                         }
                     umma_commit(&a_empty[sa]);
@@ -366,30 +369,6 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                 if ((i & 1) != role) continue;
                 const int m = tq_order<P>(i);
                 const int sa = sa_c % kA, sw = dw_c % kDW;
-                uint32_t col[64];  // slot s, half h, word c at 16 s + 8 h + c
-                uint16_t dbits[4];
-#pragma unroll
-                for (int s = 0; s < 4; s++) {
-                    const int b = tq_block<P>(m, s);
-                    const int o = ((b & 7) * 18) & 15;  // the block's offset inside its 16-byte chunk (even)
-                    const uint4* cp = reinterpret_cast<const uint4*>(rowq + (size_t) (b >> 3) * kTqQuarter + (b & 7) * 18 - o);
-                    const uint4 c0 = cp[0], c1 = cp[1];
-                    const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                    const int wi = (o + 2) >> 2;                      // the 16 code bytes start at byte o + 2
-                    const uint32_t sh = (uint32_t) ((o + 2) & 3) * 8u;  // 0 or 16
-                    uint32_t qw[4];
-#pragma unroll
-                    for (int x = 0; x < 4; x++)
-                        qw[x] = sh ? __funnelshift_r(wv[wi + x], wv[wi + x + 1 < 8 ? wi + x + 1 : 7], sh) : wv[wi + x];
-                    dbits[s] = (uint16_t) (wv[o >> 2] >> ((o & 3) * 8));
-#pragma unroll
-                    for (int h = 0; h < 2; h++)
-#pragma unroll
-                        for (int hw = 0; hw < 2; hw++)
-#pragma unroll
-                            for (int jj = 0; jj < 4; jj++)
-                                col[16 * s + 8 * h + 4 * hw + jj] = (qw[2 * h + hw] >> (2 * jj)) & 0x03030303u;
-                }
                 if (sa_c >= kA && !tq_wait(&a_empty[sa], (uint32_t) ((sa_c / kA - 1) & 1))) {
                     ok = false;
                     break;
@@ -399,16 +378,41 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ta = tA + ((uint32_t) (32 * q) << 16) + sa * kStCols;
-                tmem_st16(ta, col);
-                tmem_st16(ta + 16, col + 16);
-                tmem_st16(ta + 32, col + 32);
-                tmem_st16(ta + 48, col + 48);
                 uint16_t* dw = sDW + (size_t) sw * (Cfg::kDWStage / 2);
 #pragma unroll
-                for (int s2 = 0; s2 < 4; s2++) dw[s2 * kTqM + r] = dbits[s2];
-                tmem_wait_st32(col);
-                tmem_wait_st32(col + 32);
+                for (int g4 = 0; g4 < NB / 4; g4++) {  // four slots at a time
+                    uint32_t col[64];  // slot 4 g4 + sl, half h, word c at 16 sl + 8 h + c
+#pragma unroll
+                    for (int sl = 0; sl < 4; sl++) {
+                        const int b = tq_block<P>(m, 4 * g4 + sl);
+                        const int o = ((b & 7) * 18) & 15;  // the block's offset inside its 16-byte chunk (even)
+                        const uint4* cp =
+                            reinterpret_cast<const uint4*>(rowq + (size_t) (b >> 3) * kTqQuarter + (b & 7) * 18 - o);
+                        const uint4 c0 = cp[0], c1 = cp[1];
+                        const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                        const int wi = (o + 2) >> 2;                      // the 16 code bytes start at byte o + 2
+                        const uint32_t sh = (uint32_t) ((o + 2) & 3) * 8u;  // 0 or 16
+                        uint32_t qw[4];
+#pragma unroll
+                        for (int x = 0; x < 4; x++)
+                            qw[x] = sh ? __funnelshift_r(wv[wi + x], wv[wi + x + 1 < 8 ? wi + x + 1 : 7], sh) : wv[wi + x];
+                        dw[(4 * g4 + sl) * kTqM + r] = (uint16_t) (wv[o >> 2] >> ((o & 3) * 8));
+#pragma unroll
+                        for (int h = 0; h < 2; h++)
+#pragma unroll
+                            for (int hw = 0; hw < 2; hw++)
+#pragma unroll
+                                for (int jj = 0; jj < 4; jj++)
+                                    col[16 * sl + 8 * h + 4 * hw + jj] = (qw[2 * h + hw] >> (2 * jj)) & 0x03030303u;
+                    }
+                    const uint32_t ta = tA + ((uint32_t) (32 * q) << 16) + sa * kStCols + (uint32_t) g4 * 64;
+                    tmem_st16(ta, col);
+                    tmem_st16(ta + 16, col + 16);
+                    tmem_st16(ta + 32, col + 32);
+                    tmem_st16(ta + 48, col + 48);
+                    tmem_wait_st32(col);
+                    tmem_wait_st32(col + 32);
+                }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
@@ -439,9 +443,8 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
             const int mat = j % G, bb = (j / G) % kBB;
             const uint8_t* buf = sB + (size_t) bb * Cfg::kBBuf;
             const float2* sc = reinterpret_cast<const float2*>(buf + Cfg::kBBytes);  // [K step][token] {d, sum q}
-            // Per token: A[] holds level-1 nodes a_j of parity h waiting for a_(j+8); B[] b_h, b_(2+h), then c_h,
-            // c_(2+h).  The stages run in an order that finishes pairs early (tq_order).
-            float A[kTqN][1];
+            // Per token: B[] holds b_h, b_(2+h), then c_h, c_(2+h).  Each stage finishes level-2 nodes; the stages
+            // run in an order that finishes level-3 pairs early (tq_order).
             float B[kTqN][2];
 #pragma unroll
             for (int i = 0; i < S; i++) {
@@ -453,69 +456,81 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                     break;
                 }
                 tc_fence_after();
-                uint32_t v[32];  // slot s, token t at column 8 s + t (the K steps 2 b + h)
-                tmem_ld32(tD + ((uint32_t) (32 * q) << 16) + sd * kStCols + (uint32_t) hh * 32, v);
                 const uint16_t* dw = sDW + (size_t) sw * (Cfg::kDWStage / 2);
-                float dws[4];
+                float a0[kTqN];  // P = 64: a_(2m+h) of the first four slots, until a_(2m+8+h) arrives
 #pragma unroll
-                for (int s2 = 0; s2 < 4; s2++) dws[s2] = f16_to_f32(dw[s2 * kTqM + r]);
-                tmem_wait_ld32(v);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&d_empty[sd]);
-                    mbar_arrive(&dw_empty[sw]);
-                }
+                for (int g4 = 0; g4 < NB / 4; g4++) {
+                    uint32_t v[32];  // slot 4 g4 + sl, token t at column 8 sl + t (the K steps 2 b + h)
+                    tmem_ld32(tD + ((uint32_t) (32 * q) << 16) + sd * kStCols + (uint32_t) (hh * NB + 4 * g4) * 8, v);
+                    float dws[4];
 #pragma unroll
-                for (int t = 0; t < kTqN; t++) {
-                    if (t >= en.n) break;  // uniform across the warp
-                    // p_s = (d_w * d_x) * (float) (sum code q - sum q), slots in pairs on the packed f32x2 path
-                    // (each lane of a packed operation rounds as the scalar one does)
-                    float2 sq[4];
-#pragma unroll
-                    for (int s = 0; s < 4; s++) sq[s] = sc[(2 * tq_block<P>(m, s) + hh) * kTqN + t];  // {d_x, seed}
-                    const float2 kBias = make_float2(-12582912.0f, -12582912.0f);
-                    // Packed f32x2 only where no addition consumes the result (ptxas may fuse a packed multiply
-                    // into a following packed add, which would round once instead of twice): the integer-to-float
-                    // step and d_w * d_x.  The product with f and every addition stay scalar _rn operations,
-                    // which are never contracted.
-                    float2 pp[2];
-#pragma unroll
-                    for (int u = 0; u < 2; u++) {
-                        const float2 f = add2_rn(
-                            make_float2(__int_as_float(__float_as_int(sq[2 * u].y) + (int) v[8 * (2 * u) + t]),
-                                        __int_as_float(__float_as_int(sq[2 * u + 1].y) + (int) v[8 * (2 * u + 1) + t])),
-                            kBias);
-                        const float2 dd = mul2_rn(make_float2(dws[2 * u], dws[2 * u + 1]), make_float2(sq[2 * u].x, sq[2 * u + 1].x));
-                        pp[u] = make_float2(__fmul_rn(dd.x, f.x), __fmul_rn(dd.y, f.y));
+                    for (int sl = 0; sl < 4; sl++) dws[sl] = f16_to_f32(dw[(4 * g4 + sl) * kTqM + r]);
+                    tmem_wait_ld32(v);
+                    if (g4 == NB / 4 - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) {
+                            mbar_arrive(&d_empty[sd]);
+                            mbar_arrive(&dw_empty[sw]);
+                        }
                     }
-                    if (P == 64) {
-                        // a_(2m+h) = ((0 + p_(2m+h)) + p_(2m+h+32)) + ((0 + p_(2m+h+16)) + p_(2m+h+48))
-                        const float a = __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), pp[1].x),
-                                                  __fadd_rn(__fadd_rn(0.f, pp[0].y), pp[1].y));
-                        // order m = 0 4 1 5 2 6 3 7
-                        if (m < 4) A[t][0] = a;
-                        else if (m < 6) B[t][m - 4] = __fadd_rn(A[t][0], a);                        // b_(2(m-4)+h)
-                        else B[t][m - 6] = __fadd_rn(B[t][m - 6], __fadd_rn(A[t][0], a));           // c
-                    } else if (P == 32) {
-                        // a_(2m+h) = (0 + p_(2m+h)) + (0 + p_(2m+h+16)) from blocks m, m+8; a_(2m+8+h) from m+4, m+12
-                        const float bj = __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), __fadd_rn(0.f, pp[0].y)),
-                                                   __fadd_rn(__fadd_rn(0.f, pp[1].x), __fadd_rn(0.f, pp[1].y)));  // b_(2m+h)
-                        // order m = 0 2 1 3: b_h, b_(4+h) -> c_h; b_(2+h), b_(6+h) -> c_(2+h)
-                        if (m < 2) B[t][m] = bj;
-                        else B[t][m - 2] = __fadd_rn(B[t][m - 2], bj);
-                    } else {
-                        // lanes 4m + 2s + h (s < 2) and 4m + 2s + 8 + h hold one partial each (lanes 16..31 nothing):
-                        // a = (0 + p) + 0, b_(4m+2s+h) = a + a'
-                        const float2 b01 = make_float2(  // b_(4m+h) from slots 0, 2; b_(4m+2+h) from slots 1, 3
-                            __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), 0.f), __fadd_rn(__fadd_rn(0.f, pp[1].x), 0.f)),
-                            __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].y), 0.f), __fadd_rn(__fadd_rn(0.f, pp[1].y), 0.f)));
-                        if (m == 0) {
-                            B[t][0] = b01.x;
-                            B[t][1] = b01.y;
-                        } else {  // c_h = b_h + b_(4+h), c_(2+h) = b_(2+h) + b_(6+h)
-                            B[t][0] = __fadd_rn(B[t][0], b01.x);
-                            B[t][1] = __fadd_rn(B[t][1], b01.y);
+#pragma unroll
+                    for (int t = 0; t < kTqN; t++) {
+                        if (t >= en.n) break;  // uniform across the warp
+                        // p_s = (d_w * d_x) * (float) (sum code q - sum q), slots in pairs
+                        float2 sq[4];
+#pragma unroll
+                        for (int sl = 0; sl < 4; sl++)
+                            sq[sl] = sc[(2 * tq_block<P>(m, 4 * g4 + sl) + hh) * kTqN + t];  // {d_x, seed}
+                        const float2 kBias = make_float2(-12582912.0f, -12582912.0f);
+                        // Packed f32x2 only where no addition consumes the result (ptxas may fuse a packed multiply
+                        // into a following packed add, which would round once instead of twice): the integer-to-
+                        // float step and d_w * d_x.  The product with f and every addition stay scalar _rn
+                        // operations, which are never contracted.
+                        float2 pp[2];
+#pragma unroll
+                        for (int u = 0; u < 2; u++) {
+                            const float2 f = add2_rn(
+                                make_float2(__int_as_float(__float_as_int(sq[2 * u].y) + (int) v[8 * (2 * u) + t]),
+                                            __int_as_float(__float_as_int(sq[2 * u + 1].y) + (int) v[8 * (2 * u + 1) + t])),
+                                kBias);
+                            const float2 dd = mul2_rn(make_float2(dws[2 * u], dws[2 * u + 1]),
+                                                      make_float2(sq[2 * u].x, sq[2 * u + 1].x));
+                            pp[u] = make_float2(__fmul_rn(dd.x, f.x), __fmul_rn(dd.y, f.y));
+                        }
+                        if (P == 64) {
+                            // four slots: a = ((0 + p_l) + p_(l+32)) + ((0 + p_(l+16)) + p_(l+48)), l = 2m+h (+8)
+                            const float a = __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), pp[1].x),
+                                                      __fadd_rn(__fadd_rn(0.f, pp[0].y), pp[1].y));
+                            if (g4 == 0) {
+                                a0[t] = a;
+                            } else {
+                                const float bj = __fadd_rn(a0[t], a);  // b_(2m+h)
+                                // order m = 0 2 1 3: b_h, b_(4+h) -> c_h; b_(2+h), b_(6+h) -> c_(2+h)
+                                if (m < 2) B[t][m] = bj;
+                                else B[t][m - 2] = __fadd_rn(B[t][m - 2], bj);
+                            }
+                        } else if (P == 32) {
+                            // a_(2m+h) = (0 + p_(2m+h)) + (0 + p_(2m+h+16)) from blocks m, m+8; a_(2m+8+h) from m+4,
+                            // m+12
+                            const float bj = __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), __fadd_rn(0.f, pp[0].y)),
+                                                       __fadd_rn(__fadd_rn(0.f, pp[1].x), __fadd_rn(0.f, pp[1].y)));
+                            // order m = 0 2 1 3: b_h, b_(4+h) -> c_h; b_(2+h), b_(6+h) -> c_(2+h)
+                            if (m < 2) B[t][m] = bj;
+                            else B[t][m - 2] = __fadd_rn(B[t][m - 2], bj);
+                        } else {
+                            // lanes 4m + 2s + h (s < 2) and 4m + 2s + 8 + h hold one partial each (lanes 16..31
+                            // nothing): a = (0 + p) + 0, b_(4m+2s+h) = a + a'
+                            const float2 b01 = make_float2(  // b_(4m+h) from slots 0, 2; b_(4m+2+h) from 1, 3
+                                __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), 0.f), __fadd_rn(__fadd_rn(0.f, pp[1].x), 0.f)),
+                                __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].y), 0.f), __fadd_rn(__fadd_rn(0.f, pp[1].y), 0.f)));
+                            if (m == 0) {
+                                B[t][0] = b01.x;
+                                B[t][1] = b01.y;
+                            } else {  // c_h = b_h + b_(4+h), c_(2+h) = b_(2+h) + b_(6+h)
+                                B[t][0] = __fadd_rn(B[t][0], b01.x);
+                                B[t][1] = __fadd_rn(B[t][1], b01.y);
+                            }
                         }
                     }
                 }
@@ -551,18 +566,29 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
             }
             const int nb = args.n_out / 32;
             const int blk = (mt * kTqM + 32 * q) / 32;
+            float hv[kTqN];  // gate/up: u, then h = silu(g) * u
 #pragma unroll
             for (int t = 0; t < kTqN; t++) {
                 if (t >= en.n) break;  // uniform across the warp
                 const float res = __fadd_rn(__fadd_rn(B[t][0], B[t][1]), xs[t * 32 + lane]);
-                if (MODE == 1) {
-                    down_row(w, args.y, en.beg + t, args.n_out)[mt * kTqM + r] = res;
-                } else if (mat == 0) {
-                    gs[t * 32 + lane] = res;
-                } else {
-                    // SwiGLU, then the q8_1 rule over the warp's 32 rows (one 32-value block of h)
-                    const float hv = silu_mul(gs[t * 32 + lane], res);
-                    quant_ka_warp(hv, args.ha + ((size_t) (en.beg + t) * nb + blk) * kKaBlock, lane, args.ha_q2 != 0);
+                if (MODE == 1) down_row(w, args.y, en.beg + t, args.n_out)[mt * kTqM + r] = res;
+                else if (mat == 0) gs[t * 32 + lane] = res;
+                else hv[t] = res;
+            }
+            if (MODE == 0 && mat == 1) {
+                // SwiGLU of four tokens at a time without branches between them, so their fp64 exps overlap (a
+                // token past the entry's count computes on stale values and is not stored), then the q8_1 rule
+                // over the warp's 32 rows (one 32-value block of h) per token
+#pragma unroll
+                for (int t0 = 0; t0 < kTqN; t0 += 4) {
+                    if (t0 >= en.n) break;
+#pragma unroll
+                    for (int t = t0; t < t0 + 4; t++) hv[t] = silu_mul(gs[t * 32 + lane], hv[t]);
+                }
+#pragma unroll
+                for (int t = 0; t < kTqN; t++) {
+                    if (t >= en.n) break;
+                    quant_ka_warp(hv[t], args.ha + ((size_t) (en.beg + t) * nb + blk) * kKaBlock, lane, args.ha_q2 != 0);
                 }
             }
             __syncwarp();
