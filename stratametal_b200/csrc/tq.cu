@@ -109,24 +109,26 @@ __device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
     return o;
 }
 
-// Block slot s (0..3) of stage m: the blocks whose partials finish tree nodes together.  For the K steps of
-// parity h (partials 2 b + h):
-//   P = 64: blocks m, m+8, m+16, m+24 -> a_(2m+h) (four partials, two per lane);
-//   P = 32: blocks m, m+8 -> a_(2m+h) and m+4, m+12 -> a_(2m+8+h): b_(2m+h) at once;
-//   P = 16: blocks 2m+s (s < 2) -> a_(4m+2s+h) and 2m+s+2 -> a_(4m+2s+8+h): b_(4m+2s+h) at once.
-//   P = 64 (eight slots): blocks m, m+8, m+16, m+24 -> a_(2m+h) and m+4, m+12, m+20, m+28 -> a_(2m+8+h):
-//           b_(2m+h) at once (four partials per node, two per lane).
+// A stage is eight Q2_0 blocks of a row (16 K steps), in two groups of four slots whose partials, for the K steps
+// of parity h (partials 2 b + h), finish tree nodes together:
+//   P = 64 (stages m = 0..3): group 0 = blocks m, m+8, m+16, m+24 -> a_(2m+h), group 1 = m+4, m+12, m+20, m+28
+//           -> a_(2m+8+h): b_(2m+h) = a_(2m+h) + a_(2m+8+h);
+//   P = 32 (stages m = 0, 1): group g = blocks n, n+8, n+4, n+12 with n = m + 2g -> b_(2n+h) (one partial per
+//           lane: a_j = (0 + p_j) + (0 + p_(j+16))), group 1 completing c_(2m+h) = b_(2m+h) + b_(2m+4+h);
+//   P = 16 (one stage): group g = blocks 2g, 2g+1, 2g+4, 2g+5 -> b_(4g+h), b_(4g+2+h) (one partial on lanes
+//           0..15: a_j = (0 + p_j) + 0), group 1 completing c_h and c_(2+h).
 template <int P>
 __host__ __device__ constexpr int tq_block(int m, int s) {
     return P == 64 ? m + (s >= 4 ? 4 + 8 * (s - 4) : 8 * s)
-                   : P == 32 ? m + (s == 1 ? 8 : s == 2 ? 4 : s == 3 ? 12 : 0) : 2 * m + s + (s >= 2 ? 2 : 0);
+         : P == 32 ? (m + 2 * (s >> 2)) + ((s & 3) == 1 ? 8 : (s & 3) == 2 ? 4 : (s & 3) == 3 ? 12 : 0)
+                   : 2 * (s >> 2) + (s & 3) + ((s & 3) >= 2 ? 2 : 0);
 }
 
-// The order in which an item's stages run, so that nodes meet their partners early: P = 64 and P = 32: b_j then
-// b_(j+4) (m = 0 2 1 3); P = 16: b_h, b_(2+h), then b_(4+h), b_(6+h).  The epilogue keeps 2 values per token.
+// The order in which an item's stages run: P = 64: m = 0 2 1 3 (b_h, b_(4+h) -> c_h; b_(2+h), b_(6+h) ->
+// c_(2+h)); otherwise in order.  The epilogue keeps 2 values per token (plus a_(2m+h) within a P = 64 stage).
 template <int P>
 __host__ __device__ constexpr int tq_order(int i) {
-    return P == 16 ? i : (i >> 1) + 2 * (i & 1);
+    return P == 64 ? (i >> 1) + 2 * (i & 1) : i;
 }
 
 // One item = one 128-row tile of one matrix for one work entry.  Gate/up runs an entry's gate tile and its up
@@ -136,11 +138,11 @@ template <int MODE, int P>
 struct TqCfg {
     static constexpr int G = MODE == 0 ? 2 : 1;       // items per group (matrices of one tile)
     static constexpr int QS = P / 16;                 // raw quarters (8 blocks = 16 partials) per row
-    static constexpr int NB = P == 64 ? 8 : 4;        // blocks (slots) per stage
+    static constexpr int NB = 8;                      // blocks (slots) per stage
     static constexpr int S = P / (2 * NB);            // stages per item
     static constexpr uint32_t kRawItem = QS * kTqQuarter;
     static constexpr int kRaw = kRawItem > 40 * 1024 ? 2 : 4;  // items of raw weights in flight
-    static constexpr int kA = NB == 8 ? 2 : 4, kD = kA, kDW = 4;
+    static constexpr int kA = 2, kD = 2, kDW = 4;
     static constexpr int kBB = MODE == 0 || kRawItem > 40 * 1024 ? 2 : 4;  // activation buffers (groups)
     static constexpr uint32_t kStCols = NB * 16;      // one A or D stage: 2 NB K steps x 8 columns
     static constexpr uint32_t kTmemCols = 512;
@@ -350,7 +352,7 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
         __syncwarp();
     } else if (warp >= 4 && warp < kTqEpiWarp0) {
         // ---------------- decoders: raw Q2_0 -> int8 codes in tensor memory, block scales to shared memory ------
-        // warp 4 + 4 role + q decodes rows 32q + lane of the stages i with i % 2 == role.
+        // warp 4 + 4 role + q decodes rows 32q + lane of every other stage (global stage count % 2 == role).
         const int q = warp & 3, role = (warp - 4) >> 2;
         const int r = 32 * q + lane;
         int sa_c = 0, dw_c = 0;
@@ -366,7 +368,7 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
 #pragma unroll
             for (int i = 0; i < S; i++, sa_c++, dw_c++) {
                 if (!ok) break;
-                if ((i & 1) != role) continue;
+                if ((sa_c & 1) != role) continue;  // the two decoder roles take alternate stages
                 const int m = tq_order<P>(i);
                 const int sa = sa_c % kA, sw = dw_c % kDW;
                 if (sa_c >= kA && !tq_wait(&a_empty[sa], (uint32_t) ((sa_c / kA - 1) & 1))) {
@@ -511,20 +513,20 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                                 else B[t][m - 2] = __fadd_rn(B[t][m - 2], bj);
                             }
                         } else if (P == 32) {
-                            // a_(2m+h) = (0 + p_(2m+h)) + (0 + p_(2m+h+16)) from blocks m, m+8; a_(2m+8+h) from m+4,
-                            // m+12
+                            // blocks n, n+8, n+4, n+12 (n = m + 2 g4): b_(2n+h) = a_(2n+h) + a_(2n+8+h),
+                            // a_j = (0 + p_j) + (0 + p_(j+16))
                             const float bj = __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), __fadd_rn(0.f, pp[0].y)),
                                                        __fadd_rn(__fadd_rn(0.f, pp[1].x), __fadd_rn(0.f, pp[1].y)));
-                            // order m = 0 2 1 3: b_h, b_(4+h) -> c_h; b_(2+h), b_(6+h) -> c_(2+h)
-                            if (m < 2) B[t][m] = bj;
-                            else B[t][m - 2] = __fadd_rn(B[t][m - 2], bj);
+                            // group 0: b_(2m+h); group 1: b_(2m+4+h) completes c_(2m+h)
+                            if (g4 == 0) B[t][m] = bj;
+                            else B[t][m] = __fadd_rn(B[t][m], bj);
                         } else {
-                            // lanes 4m + 2s + h (s < 2) and 4m + 2s + 8 + h hold one partial each (lanes 16..31
-                            // nothing): a = (0 + p) + 0, b_(4m+2s+h) = a + a'
+                            // blocks 2 g4 + {0, 1, 4, 5}: lanes 4 g4 + 2s + h and 4 g4 + 2s + 8 + h (s < 2) hold
+                            // one partial each, lanes 16..31 nothing: a = (0 + p) + 0, b = a + a'
                             const float2 b01 = make_float2(  // b_(4m+h) from slots 0, 2; b_(4m+2+h) from 1, 3
                                 __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), 0.f), __fadd_rn(__fadd_rn(0.f, pp[1].x), 0.f)),
                                 __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].y), 0.f), __fadd_rn(__fadd_rn(0.f, pp[1].y), 0.f)));
-                            if (m == 0) {
+                            if (g4 == 0) {
                                 B[t][0] = b01.x;
                                 B[t][1] = b01.y;
                             } else {  // c_h = b_h + b_(4+h), c_(2+h) = b_(2+h) + b_(6+h)
