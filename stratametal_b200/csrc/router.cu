@@ -300,14 +300,17 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, uint16_t* __rest
 }
 
 // ------------------------------------------------------------------------------------------------
-// a3 (+ a4): one warp per token, 8 tokens per CTA.  Lane l holds experts l, l + 32, ... (E <= 1024).
+// a3 (+ a4): one warp per token, 1 to 8 tokens per CTA (few tokens: one per CTA, so that each warp's fp64 exps and
+// selection rounds have an SM's pipes to themselves).  Lane l holds experts l, l + 32, ... (E <= 1024).
 // p_e = exp(l_e - max) in fp64; the ranking is by p_e descending with the lower index on a tie (the order of
 // the normalised probabilities: one positive divisor for all); the k chosen are then normalised exactly as
 // route_ref does: w = (float)(p / sum), chosen = sum of those quotients in rank order, clamped at 2^-14,
-// final (float)((double) w / chosen).  With xq the CTA then writes the q8_1 image of its 8 tokens.
+// final (float)((double) w / chosen).  The CTAs past the routing ones write the q8_1 image of x.
 // ------------------------------------------------------------------------------------------------
 
 constexpr int kTopkWarps = 8;
+
+__host__ __device__ constexpr int topk_tokens_per_cta(int T) { return T <= 148 ? 1 : T <= 592 ? 4 : kTopkWarps; }
 
 // The routing of one token by one warp (route_ref, pack_parity.cpp:5144-5165): ids[0..k) and the renormalised
 // weights wout[0..k) (global or shared memory).  p_e = exp(l_e - max) in fp64 and its sum (per-lane partial sums,
@@ -316,7 +319,14 @@ constexpr int kTopkWarps = 8;
 // logits (at least one f32 ulp apart) give distinct fp64 p in the same order.  So the selection rounds compare
 // floats; p is evaluated again, by the same expression, for the k chosen.  Then w = (float)(p / sum), chosen =
 // the sum of those quotients in rank order, clamped at 2^-14, and the final weight (float)((double) w / chosen).
-__device__ __forceinline__ bool better_f(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+//
+// The selection orders by an unsigned key that sorts as the float does (-0 and +0 equal: the key of v + 0); a NaN
+// logit gets key 0 and is never chosen, nor is an expert past E.  Each round is two warp reductions: the largest
+// key, then the lowest index among the lanes that hold it; the lane that gave the winner offers its next best.
+__device__ __forceinline__ uint32_t route_key(float v) {
+    const uint32_t b = __float_as_uint(v + 0.0f);
+    return v != v ? 0u : (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
 
 template <int PER_LANE>
 __device__ __forceinline__ void route_warp(const float* __restrict__ l, int E, int k, int32_t* ids, float* wout,
@@ -338,37 +348,30 @@ __device__ __forceinline__ void route_warp(const float* __restrict__ l, int E, i
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
     const double sum = part;
-    // selection: each lane offers its best untaken value; k rounds of a warp argmax
-    uint32_t taken = 0;
-    float bv = -INFINITY;
+    // selection: each lane offers its best untaken key (lowest index first among equal keys); k rounds
+    uint32_t kv[PER_LANE];
+#pragma unroll
+    for (int j = 0; j < PER_LANE; j++) kv[j] = lane + 32 * j < E ? route_key(lv[j]) : 0u;
+    uint32_t taken = 0, bk = 0;
     int bi = 0x7fffffff;
 #pragma unroll
     for (int j = 0; j < PER_LANE; j++)
-        if (lane + 32 * j < E && better_f(lv[j], lane + 32 * j, bv, bi)) { bv = lv[j]; bi = lane + 32 * j; }
+        if (kv[j] > bk) { bk = kv[j]; bi = lane + 32 * j; }
     int id0 = 0, id1 = 0;  // ranks lane and 32 + lane (k <= 64)
     for (int i = 0; i < k; i++) {
-        float v = bv;
-        int ix = bi;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
-            if (better_f(ov, oi, v, ix)) { v = ov; ix = oi; }
-        }
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+        const int ix = __reduce_min_sync(0xffffffffu, bk == mk && bk != 0u ? bi : 0x7fffffff);
         if (lane == (i & 31)) {
             if (i < 32) id0 = ix;
             else id1 = ix;
         }
-        if ((ix & 31) == lane) {
+        if (ix != 0x7fffffff && (ix & 31) == lane) {
             taken |= 1u << (ix >> 5);
-            bv = -INFINITY;
+            bk = 0;
             bi = 0x7fffffff;
 #pragma unroll
             for (int j = 0; j < PER_LANE; j++)
-                if (!((taken >> j) & 1u) && lane + 32 * j < E && better_f(lv[j], lane + 32 * j, bv, bi)) {
-                    bv = lv[j];
-                    bi = lane + 32 * j;
-                }
+                if (!((taken >> j) & 1u) && kv[j] > bk) { bk = kv[j]; bi = lane + 32 * j; }
         }
     }
     // weights of the chosen, the chosen sum in rank order
@@ -395,7 +398,8 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const floa
                                                                       uint8_t* __restrict__ xq, int H, KAct xa,
                                                                       int xa_q2) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int route_blocks = (T + kTopkWarps - 1) / kTopkWarps;
+    const int tpc = topk_tokens_per_cta(T);
+    const int route_blocks = (T + tpc - 1) / tpc;
     if ((int) blockIdx.x >= route_blocks) {
         // the remaining CTAs write the q8_1 image of x: one 32-value block per warp, grid-stride
         const int64_t nq = (int64_t) T * (H / 32);
@@ -407,8 +411,8 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const floa
         }
         return;
     }
-    const int t = blockIdx.x * kTopkWarps + warp;
-    if (t < T) route_warp<PER_LANE>(logits + (size_t) t * E, E, k, ids + (size_t) t * k, wout + (size_t) t * k, lane);
+    const int t = blockIdx.x * tpc + warp;
+    if (warp < tpc && t < T) route_warp<PER_LANE>(logits + (size_t) t * E, E, k, ids + (size_t) t * k, wout + (size_t) t * k, lane);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -456,7 +460,7 @@ cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, cons
 
 cudaError_t launch_router_topk(const float* logits, int T, int E, int k, int32_t* ids, float* w, const float* x,
                                uint8_t* xq, int H, cudaStream_t s, const KAct* xa, int xa_q2) {
-    int blocks = (T + kTopkWarps - 1) / kTopkWarps;
+    int blocks = (T + topk_tokens_per_cta(T) - 1) / topk_tokens_per_cta(T);
     if (xq || xa) blocks += (int) std::min<int64_t>(((int64_t) T * (H / 32) + kTopkWarps - 1) / kTopkWarps, 148 * 8);
     const KAct a = xa ? *xa : KAct{};
     if (E <= 256) router_topk_kernel<8><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);

@@ -124,6 +124,17 @@ __host__ __device__ constexpr int tq_block(int m, int s) {
                    : 2 * (s >> 2) + (s & 3) + ((s & 3) >= 2 ? 2 : 0);
 }
 
+// A stage's blocks are its first block plus offsets that do not depend on the stage (the MMA issuer adds them
+// to one descriptor).
+template <int P>
+constexpr bool tq_block_shifts() {
+    for (int m = 0; m < 4; m++)
+        for (int s = 0; s < 8; s++)
+            if (tq_block<P>(m, s) - tq_block<P>(m, 0) != tq_block<P>(0, s) - tq_block<P>(0, 0)) return false;
+    return true;
+}
+static_assert(tq_block_shifts<64>() && tq_block_shifts<32>() && tq_block_shifts<16>(), "stage block offsets");
+
 // The order in which an item's stages run: P = 64: m = 0 2 1 3 (b_h, b_(4+h) -> c_h; b_(2+h), b_(6+h) ->
 // c_(2+h)); otherwise in order.  The epilogue keeps 2 values per token (plus a_(2m+h) within a P = 64 stage).
 template <int P>
@@ -151,8 +162,9 @@ struct TqCfg {
     static constexpr uint32_t kSBytes = P * kTqN * 8; // [K step][token] {d_x f32, sum q}
     static constexpr uint32_t kBBuf = kBBytes + kSBytes;
     static constexpr uint32_t kDWStage = NB * kTqM * 2;  // fp16 block scales [slot][row]
-    static constexpr uint32_t kXch = 3 * 4 * kTqN * 32 * 4;  // d_1 hand-over (2 buffers) and g, per lane quarter
-    static constexpr size_t smem = (size_t) kRaw * kRawItem + kBB * kBBuf + kDW * kDWStage + kXch + 64 * 8 + 1024;
+    static constexpr uint32_t kXch = 3 * 4 * kTqN * 32 * 4;  // d hand-over (2 buffers) and g, per lane quarter
+    static constexpr int kBars = 80;                         // mbarriers
+    static constexpr size_t smem = (size_t) kRaw * kRawItem + kBB * kBBuf + kDW * kDWStage + kXch + kBars * 8 + 1024;
     static_assert(smem <= 232448, "shared memory per block");
 };
 
@@ -195,9 +207,10 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
     uint64_t* d_empty = d_full + kD;      // epilogue warps
     uint64_t* dw_full = d_empty + kD;     // the 4 decoder warps of the stage
     uint64_t* dw_empty = dw_full + kDW;   // epilogue warps
-    uint64_t* x_full = dw_empty + kDW;    // [2][4] h = 1 warp -> h = 0 warp
-    uint64_t* x_empty = x_full + 8;       // [2][4] h = 0 warp -> h = 1 warp
-    uint64_t* mma_done = x_empty + 8;
+    uint64_t* x_full = dw_empty + kDW;    // [h][2][4] the h warp wrote its half of the hand-over buffer
+    uint64_t* x_empty = x_full + 16;      // [h][2][4] the other warp read it
+    uint64_t* mma_done = x_empty + 16;
+    static_assert(4 * 4 + 2 * (kA + kD + kDW) + 2 * 16 + 1 <= Cfg::kBars, "mbarrier region");
     __shared__ uint32_t s_tmem;
 
     const Work w = args.w;
@@ -224,7 +237,7 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
             mbar_init(&dw_full[i], 4);
             mbar_init(&dw_empty[i], 8);
         }
-        for (int i = 0; i < 8; i++) {
+        for (int i = 0; i < 16; i++) {
             mbar_init(&x_full[i], 1);
             mbar_init(&x_empty[i], 1);
         }
@@ -312,11 +325,18 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                 const int gid = group_of(j);
                 if (gid >= n_groups) break;
                 const int g = j / G, bb = g % kBB;
-                if (j % G == 0 && !mbar_wait_sleep(&b_full[bb], (uint32_t) ((g / kBB) & 1), kWaitLimitNs)) {
-                    ok = false;
-                    break;
+                if (j % G == 0) {
+                    if (!mbar_wait_sleep(&b_full[bb], (uint32_t) ((g / kBB) & 1), kWaitLimitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    // the producers' cp.async writes of this group's activations -> the MMA's (async proxy) reads;
+                    // the A operands come through tensor memory, so once per group is enough
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 }
-                const uint8_t* buf = sB + (size_t) bb * Cfg::kBBuf;
+                // K step k of the group's activations: the descriptor of K step 0 plus k * 256 B (start address
+                // field, in 16-byte units, of an address below 256 KB: no carry out of the field)
+                const uint64_t bd0 = umma_desc(sB + (size_t) bb * Cfg::kBBuf, 128, 256);
                 for (int i = 0; i < S; i++, sa_c++, sd_c++) {
                     const int m = tq_order<P>(i);
                     const int sa = sa_c % kA, sd = sd_c % kD;
@@ -326,15 +346,15 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                         break;
                     }
                     tc_fence_after();
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // cp.async writes -> MMA reads
+                    const uint64_t bdm = bd0 + (uint64_t) (2 * 16 * tq_block<P>(m, 0));
+                    const uint32_t dst = tD + sd * kStCols, ast = tA + sa * kStCols;
 #pragma unroll
                     for (int s = 0; s < NB; s++)
 #pragma unroll
                         for (int h = 0; h < 2; h++) {
-                            const int k = 2 * tq_block<P>(m, s) + h;
-                            const uint64_t bd = umma_desc(buf + k * 256, 128, 256);
-                            umma_i8_ts(tD + sd * kStCols + (uint32_t) (h * NB + s) * 8,
-                                       tA + sa * kStCols + (uint32_t) (s * 2 + h) * 8, bd, idesc);
+                            const int k_off = 2 * (tq_block<P>(0, s) - tq_block<P>(0, 0)) + h;
+                            umma_i8_ts(dst + (uint32_t) (h * NB + s) * 8, ast + (uint32_t) (s * 2 + h) * 8,
+                                       bdm + (uint64_t) (16 * k_off), idesc);
                         }
                     umma_commit(&a_empty[sa]);
                     umma_commit(&d_full[sd]);
@@ -448,7 +468,9 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
             // Per token: B[] holds b_h, b_(2+h), then c_h, c_(2+h).  Each stage finishes level-2 nodes; the stages
             // run in an order that finishes level-3 pairs early (tq_order).
             float B[kTqN][2];
-#pragma unroll
+            // one copy of the stage code serves every stage (a smaller instruction footprint): the node a stage
+            // writes is chosen by selects on m & 1, so the register arrays keep constant indices
+#pragma unroll 1
             for (int i = 0; i < S; i++) {
                 const int m = tq_order<P>(i);
                 const int c = sd_c + i, cw = dw_c + i;
@@ -509,17 +531,19 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                             } else {
                                 const float bj = __fadd_rn(a0[t], a);  // b_(2m+h)
                                 // order m = 0 2 1 3: b_h, b_(4+h) -> c_h; b_(2+h), b_(6+h) -> c_(2+h)
-                                if (m < 2) B[t][m] = bj;
-                                else B[t][m - 2] = __fadd_rn(B[t][m - 2], bj);
+                                const float nv = m < 2 ? bj : __fadd_rn((m & 1) ? B[t][1] : B[t][0], bj);
+                                if (m & 1) B[t][1] = nv;
+                                else B[t][0] = nv;
                             }
                         } else if (P == 32) {
                             // blocks n, n+8, n+4, n+12 (n = m + 2 g4): b_(2n+h) = a_(2n+h) + a_(2n+8+h),
                             // a_j = (0 + p_j) + (0 + p_(j+16))
                             const float bj = __fadd_rn(__fadd_rn(__fadd_rn(0.f, pp[0].x), __fadd_rn(0.f, pp[0].y)),
                                                        __fadd_rn(__fadd_rn(0.f, pp[1].x), __fadd_rn(0.f, pp[1].y)));
-                            // group 0: b_(2m+h); group 1: b_(2m+4+h) completes c_(2m+h)
-                            if (g4 == 0) B[t][m] = bj;
-                            else B[t][m] = __fadd_rn(B[t][m], bj);
+                            // group 0: b_(2m+h); group 1: b_(2m+4+h) completes c_(2m+h)  (m = 0, 1)
+                            const float nv = g4 == 0 ? bj : __fadd_rn(m ? B[t][1] : B[t][0], bj);
+                            if (m) B[t][1] = nv;
+                            else B[t][0] = nv;
                         } else {
                             // blocks 2 g4 + {0, 1, 4, 5}: lanes 4 g4 + 2s + h and 4 g4 + 2s + 8 + h (s < 2) hold
                             // one partial each, lanes 16..31 nothing: a = (0 + p) + 0, b = a + a'
@@ -544,57 +568,78 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&b_empty[bb]);
             }
-            // d_h = c_h + c_(2+h); the h = 1 warp hands d_1 to the h = 0 warp, which adds d_0 + d_1
-            const int xb = j & 1;
-            float* xs = sX + ((size_t) xb * 4 + q) * kTqN * 32;
-            uint64_t* xf = &x_full[xb * 4 + q];
-            uint64_t* xe = &x_empty[xb * 4 + q];
+            // d_h = c_h + c_(2+h); the result is d_0 + d_1.  Gate and down items: the h = 1 warp hands d_1 to the
+            // h = 0 warp, which finishes every token.  Up items (the SwiGLU and q8_1 step): token t is finished by
+            // the warp of half t & 1, each warp handing the other its d_h of the other's tokens (d_1 + d_0 = d_0 +
+            // d_1 exactly: a two-operand IEEE addition is commutative).  The g of a token reaches its up finisher
+            // through gs, written by the h = 0 warp before it signals the up item's hand-over.
+            const bool split = MODE == 0 && mat == 1;
+            const int xb = j & 1;  // gate/up: xb = mat, so the gate and up items keep to their own barriers
+            float* xs = sX + ((size_t) xb * 4 + q) * kTqN * 32;  // [token][lane]: d of the token's other half
             const uint32_t xpar = (uint32_t) ((j / 2) & 1);
-            if (hh == 1) {
-                if (j >= 2 && !tq_wait(xe, xpar ^ 1u)) {
+            float dsum[kTqN];
+#pragma unroll
+            for (int t = 0; t < kTqN; t++) {
+                if (t >= en.n) break;  // uniform across the warp
+                dsum[t] = __fadd_rn(B[t][0], B[t][1]);
+            }
+            // x_full[h]: warp h wrote its part of xs; x_empty[h]: the other warp read it (the part is free again)
+            if (split || hh == 1) {
+                if (j >= 2 && !tq_wait(&x_empty[(hh * 2 + xb) * 4 + q], xpar ^ 1u)) {
                     ok = false;
                     break;
                 }
 #pragma unroll
-                for (int t = 0; t < kTqN; t++)
-                    if (t < en.n) xs[t * 32 + lane] = __fadd_rn(B[t][0], B[t][1]);
+                for (int t = 0; t < kTqN; t++) {
+                    if (t >= en.n) break;
+                    if (!split || (t & 1) != hh) xs[t * 32 + lane] = dsum[t];
+                }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(xf);
-                continue;
+                if (lane == 0) mbar_arrive(&x_full[(hh * 2 + xb) * 4 + q]);
+                if (!split) continue;
             }
-            if (!tq_wait(xf, xpar)) {
+            if (!tq_wait(&x_full[((1 - hh) * 2 + xb) * 4 + q], xpar)) {
                 ok = false;
                 break;
             }
-            const int nb = args.n_out / 32;
-            const int blk = (mt * kTqM + 32 * q) / 32;
-            float hv[kTqN];  // gate/up: u, then h = silu(g) * u
-#pragma unroll
-            for (int t = 0; t < kTqN; t++) {
-                if (t >= en.n) break;  // uniform across the warp
-                const float res = __fadd_rn(__fadd_rn(B[t][0], B[t][1]), xs[t * 32 + lane]);
-                if (MODE == 1) down_row(w, args.y, en.beg + t, args.n_out)[mt * kTqM + r] = res;
-                else if (mat == 0) gs[t * 32 + lane] = res;
-                else hv[t] = res;
-            }
-            if (MODE == 0 && mat == 1) {
-                // SwiGLU of four tokens at a time without branches between them, so their fp64 exps overlap (a
-                // token past the entry's count computes on stale values and is not stored), then the q8_1 rule
-                // over the warp's 32 rows (one 32-value block of h) per token
-#pragma unroll
-                for (int t0 = 0; t0 < kTqN; t0 += 4) {
-                    if (t0 >= en.n) break;
-#pragma unroll
-                    for (int t = t0; t < t0 + 4; t++) hv[t] = silu_mul(gs[t * 32 + lane], hv[t]);
-                }
+            if (!split) {
 #pragma unroll
                 for (int t = 0; t < kTqN; t++) {
                     if (t >= en.n) break;
-                    quant_ka_warp(hv[t], args.ha + ((size_t) (en.beg + t) * nb + blk) * kKaBlock, lane, args.ha_q2 != 0);
+                    const float res = __fadd_rn(dsum[t], xs[t * 32 + lane]);
+                    if (MODE == 1) down_row(w, args.y, en.beg + t, args.n_out)[mt * kTqM + r] = res;
+                    else gs[t * 32 + lane] = res;
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&x_empty[(2 + xb) * 4 + q]);
+                continue;
+            }
+            float own[kTqN / 2] = {0.f, 0.f, 0.f, 0.f};  // the results of tokens hh + 2u
+#pragma unroll
+            for (int u = 0; u < kTqN / 2; u++) {
+                if (2 * u + hh >= en.n) break;
+                own[u] = __fadd_rn(hh ? dsum[2 * u + 1] : dsum[2 * u], xs[(2 * u + hh) * 32 + lane]);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(xe);
+            if (lane == 0) mbar_arrive(&x_empty[((1 - hh) * 2 + xb) * 4 + q]);
+            const int n_own = (en.n - hh + 1) >> 1;
+            if (n_own > 0) {
+                // SwiGLU of the warp's (at most four) tokens without branches between them, so their fp64 exps
+                // overlap (a token past the entry's count computes on stale values and is not stored), then the
+                // q8_1 rule over the warp's 32 rows (one 32-value block of h) per token
+                float hv[kTqN / 2];
+#pragma unroll
+                for (int u = 0; u < kTqN / 2; u++) hv[u] = silu_mul(gs[(2 * u + hh) * 32 + lane], own[u]);
+#pragma unroll
+                for (int u = 0; u < kTqN / 2; u++) gs[(2 * u + hh) * 32 + lane] = hv[u];
+                const int nb = args.n_out / 32;
+                const int blk = (mt * kTqM + 32 * q) / 32;
+#pragma unroll 1
+                for (int u = 0; u < n_own; u++)
+                    quant_ka_warp(gs[(2 * u + hh) * 32 + lane],
+                                  args.ha + ((size_t) (en.beg + 2 * u + hh) * nb + blk) * kKaBlock, lane,
+                                  args.ha_q2 != 0);
+            }
         }
         if (!ok && lane == 0) atomicOr(&g_smoe_status, kDevTimeout);
         if (MODE == 1) ep_signal_done(w.ep_done, gridDim.x * 8);
