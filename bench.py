@@ -451,6 +451,8 @@ def run_ours(args, ws, rank, local):
         traffic = None
         if dominant == "expert_gate_up" and not tc and not tq and "expert_gate_up_per_expert" in tpu:
             traffic = tpu["expert_gate_up_per_expert"] * (D_mean + 1)
+        elif dominant == "expert_gate_up" and tq and "tq_gate_up_per_expert" in tpu:
+            traffic = tpu["tq_gate_up_per_expert"] * (D_mean + 1)
         expert_gbs = (D_mean + 1) * E_BYTES / (ms_step * 1e-3) / 1e9
         kos = KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE_TQ if tq else KERNEL_OF_STAGE
         if 2 <= T <= 64:
