@@ -215,8 +215,13 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
 
     const Work w = args.w;
     const int n_groups = work_entries(w) * args.m_tiles;
-    // item j of this CTA: group blockIdx.x + (j / G) gridDim.x, matrix j % G
-    auto group_of = [&](int j) { return (int) blockIdx.x + (j / G) * (int) gridDim.x; };
+    // item j of this CTA: matrix j % G of group (j / G) gridDim.x + c, c = blockIdx.x in even rounds and
+    // gridDim.x - 1 - blockIdx.x in odd ones.  The work list runs from the heaviest entries (eight tokens) to the
+    // lightest, so the serpentine order gives each CTA a similar mix; a CTA's groups still increase with j.
+    auto group_of = [&](int j) {
+        const int round = j / G;
+        return round * (int) gridDim.x + ((round & 1) ? (int) gridDim.x - 1 - (int) blockIdx.x : (int) blockIdx.x);
+    };
 
     if (tid == 0) {
         for (int i = 0; i < 4; i++) {
