@@ -215,6 +215,9 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
 
     const Work w = args.w;
     const int n_groups = work_entries(w) * args.m_tiles;
+    // gate/up: the down launch that follows may start now (programmatic dependent launch); its CTAs take SMs as
+    // this grid's CTAs exit and set up while the last ones finish
+    if (MODE == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // item j of this CTA: matrix j % G of group (j / G) gridDim.x + c, c = blockIdx.x in even rounds and
     // gridDim.x - 1 - blockIdx.x in odd ones.  The work list runs from the heaviest entries (eight tokens) to the
     // lightest, so the serpentine order gives each CTA a similar mix; a CTA's groups still increase with j.
@@ -289,6 +292,9 @@ __global__ void __launch_bounds__(kTqThreads, 1) tq_expert_kernel(const __grid_c
         __syncwarp();
     } else if (warp == 2 || warp == 3) {
         // ---------------- activations: the entry's slots, every K step, once per group ----------------
+        // down: h is the previous grid's output.  Only these warps read it, so only they wait for that grid (a
+        // no-op without a programmatic launch); the weight loads, decoding and set-up of the others overlap it.
+        if (MODE == 1) asm volatile("griddepcontrol.wait;" ::: "memory");
         const int pt = tid - 64;  // 0..63
         bool ok = true;
         for (int g = 0; ok; g++) {
@@ -668,8 +674,22 @@ cudaError_t launch_tq(const CUtensorMap* maps, const TqArgs& a, cudaStream_t s) 
     int dev = 0, nsm = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    tq_expert_kernel<MODE, P><<<nsm, kTqThreads, smem, s>>>(maps[0], maps[1], maps[2], maps[3], a);
-    return cudaGetLastError();
+    if (MODE == 0) {
+        tq_expert_kernel<MODE, P><<<nsm, kTqThreads, smem, s>>>(maps[0], maps[1], maps[2], maps[3], a);
+        return cudaGetLastError();
+    }
+    // down: launched as a programmatic dependent of the gate/up grid before it (see griddepcontrol above)
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned) nsm);
+    cfg.blockDim = dim3(kTqThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tq_expert_kernel<MODE, P>, maps[0], maps[1], maps[2], maps[3], a);
 }
 
 template <int MODE>
