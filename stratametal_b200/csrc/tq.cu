@@ -12,10 +12,13 @@
 // d_j = c_j + c_(j+2), result d_0 + d_1 (float addition commutes, so only the grouping matters).
 //
 // Shapes (swap-AB): M = 128 weight rows (tensor-memory lanes), N = 8 tokens (slots) of one work entry, K = 32
-// per MMA.  P = K / 32 partials per row (16, 32 or 64).  A stage is 4 whole Q2_0 blocks of a row (8 K steps)
-// chosen so that the epilogue can finish tree nodes from it: P = 64: blocks m, m+8, m+16, m+24 (nodes a_2m,
-// a_2m+1); P = 32: blocks 2m, 2m+1, 2m+8, 2m+9 (a_4m..a_4m+3); P = 16: blocks 4m..4m+3 (a_8m..a_8m+7).  The
-// epilogue keeps a_0..a_7 until a_8..a_15 arrive (8 floats per token).
+// per MMA.  P = K / 32 partials per row (16, 32 or 64).  A stage is 8 whole Q2_0 blocks of a row (16 K steps),
+// two groups of four chosen so that the epilogue finishes level-2 tree nodes from each stage (tq_block below):
+// P / 16 stages per item, one for down at n_ff = 512.  The epilogue keeps per token two level-2/3 nodes of its
+// K parity across the stages and hands them over once per item (d_h below).
+//
+// Items.  Each CTA takes its groups in serpentine order over the heaviest-first work list; the down kernel is a
+// programmatic dependent launch of gate/up (only its activation producers wait for the gate/up grid).
 //
 // Operands.  Weights: Q2_0 rows TMA-loaded raw (2D boxes of 144 B x 128 rows), decoded by eight warps into int8
 // codes 0..3 straight into tensor memory (tcgen05.st; A of the MMA is read from tensor memory).  The word
