@@ -85,6 +85,8 @@ size_t orc_row_bytes(int type, int64_t n) {
     if (n <= 0) return 0;
     if (type == ORC_Q2_0) return (n % 64) ? 0 : (size_t) (n / 64) * 18u;
     if (type == ORC_IQ2_S) return (n % 256) ? 0 : (size_t) (n / 256) * 82u;
+    if (type == ORC_IQ4_NL) return (n % 32) ? 0 : (size_t) (n / 32) * 18u;
+    if (type == ORC_IQ4_XS) return (n % 256) ? 0 : (size_t) (n / 256) * 136u;
     return 0;
 }
 
@@ -183,17 +185,53 @@ static float iq2_s_partial(const uint8_t* blk, const uint8_t* xblk, int g) {
     return d * (float) sumi;
 }
 
-/* row_dot (iq_parity.cpp:275-292): partial k covers values [32k, 32k + 32); it is added to lane k & 31 in
- * order, then the 32 lane sums meet in an xor butterfly (16, 8, 4, 2, 1). */
+/* The IQ4 code values (iq_parity.cpp:106): the format's fixed non-linear table, index = one 4-bit code. */
+static const int8_t k_iq4_values[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+/* IQ4_NL (fp16 d, qs[16]: byte i holds value i in its low nibble and value i + 16 in its high nibble) has two
+ * 16-value partials per 32-value block (iq_parity.cpp:196-206): partial p reads qs bytes 8p .. 8p + 7, i.e. values
+ * 8p .. 8p + 7 and 16 + 8p .. 16 + 8p + 7 of the block's q8_1 block; partial = (f32(d_w) * f32(d_x)) * sumi. */
+static float iq4_nl_partial(const uint8_t* blk, const uint8_t* xblk, int p) {
+    const uint8_t* qs = blk + 2;
+    int32_t sumi = 0;
+    for (int i = 8 * p; i < 8 * p + 8; i++) {
+        sumi += k_iq4_values[qs[i] & 15] * (int32_t) q8_at(xblk, i);
+        sumi += k_iq4_values[qs[i] >> 4] * (int32_t) q8_at(xblk, i + 16);
+    }
+    const float d = orc_f32_from_f16(rd16(blk)) * orc_f32_from_f16(rd16(xblk));
+    return d * (float) sumi;
+}
+
+/* IQ4_XS (fp16 d @0, 2-bit high scales u16 @2, 4-bit low scales [4] @4, qs[128] @8; 256 values) 32-value group
+ * ib (iq_parity.cpp:208-222): qs bytes 16 ib .. 16 ib + 15 as in IQ4_NL (low nibble value i, high nibble value
+ * i + 16), the 6-bit scale ls = low nibble ib of scales_l | bits 2 ib, 2 ib + 1 of scales_h << 4, and
+ * sumi * (ls - 32). */
+static float iq4_xs_partial(const uint8_t* blk, const uint8_t* xblk, int ib) {
+    const uint8_t* qs = blk + 8 + 16 * ib;
+    int32_t sumi = 0;
+    for (int i = 0; i < 16; i++) {
+        sumi += k_iq4_values[qs[i] & 15] * (int32_t) q8_at(xblk, i);
+        sumi += k_iq4_values[qs[i] >> 4] * (int32_t) q8_at(xblk, i + 16);
+    }
+    const int sh = rd16(blk + 2);
+    const int ls = ((blk[4 + ib / 2] >> (4 * (ib % 2))) & 15) | (((sh >> (2 * ib)) & 3) << 4);
+    sumi *= ls - 32;
+    const float d = orc_f32_from_f16(rd16(blk)) * orc_f32_from_f16(rd16(xblk));
+    return d * (float) sumi;
+}
+
+/* row_dot (iq_parity.cpp:275-292): the row's partials in order (32 values each, IQ4_NL 16), partial k added to
+ * lane k & 31, then the 32 lane sums meet in an xor butterfly (16, 8, 4, 2, 1). */
 static float row_dot_impl(int type, const uint8_t* row, const uint8_t* col, int n_in, int variant) {
     float lane[32], nxt[32];
     memset(lane, 0, sizeof lane);
-    const int npart = n_in / 32;
+    const int npart = type == ORC_IQ4_NL ? n_in / 16 : n_in / 32;
     for (int k = 0; k < npart; k++) {
-        const uint8_t* xblk = col + (size_t) k * 36;
         float p;
-        if (type == ORC_IQ2_S) p = iq2_s_partial(row + (size_t) (k / 8) * 82, xblk, k % 8);
-        else p = q2_0_partial(row + (size_t) (k / 2) * 18, xblk, k % 2, variant != 1);
+        if (type == ORC_IQ2_S) p = iq2_s_partial(row + (size_t) (k / 8) * 82, col + (size_t) k * 36, k % 8);
+        else if (type == ORC_IQ4_NL) p = iq4_nl_partial(row + (size_t) (k / 2) * 18, col + (size_t) (k / 2) * 36, k % 2);
+        else if (type == ORC_IQ4_XS) p = iq4_xs_partial(row + (size_t) (k / 8) * 136, col + (size_t) k * 36, k % 8);
+        else p = q2_0_partial(row + (size_t) (k / 2) * 18, col + (size_t) k * 36, k % 2, variant != 1);
         lane[k & 31] += p;
     }
     for (int o = 16; o > 0; o >>= 1) {

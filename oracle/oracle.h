@@ -9,6 +9,8 @@
  *   - q8_1 activation block                  metal/src/iq_parity.cpp:350-382 (quant_host_block)
  *   - Q2_0 partial dot (code - 1)            metal/src/iq_parity.cpp:225-252 (dot_q2_0), pack_parity.cpp:2736-2757
  *   - IQ2_S partial dot                      metal/src/iq_parity.cpp:125-151 (dot_iq2_s)
+ *   - IQ4_NL / IQ4_XS partial dots           metal/src/iq_parity.cpp:106-115, 196-222 (dot_iq4_nl, dot_iq4_xs);
+ *                                            geometry :256-263 (geom_of).  Oracle only: no kernel reads them yet
  *   - 32-lane row accumulation + butterfly   metal/src/iq_parity.cpp:275-292 (row_dot), pack_parity.cpp:2759-2772
  *   - SwiGLU then q8_1 of h                  metal/src/iq_parity.cpp:384-411 (silu, ref_expert)
  *   - bf16 router dot, double accumulation   metal/src/pack_parity.cpp:3793-3799 (round_bf16, bf16_dot)
@@ -31,7 +33,7 @@
 extern "C" {
 #endif
 
-enum { ORC_Q2_0 = 42, ORC_IQ2_S = 22 };
+enum { ORC_Q2_0 = 42, ORC_IQ2_S = 22, ORC_IQ4_NL = 20, ORC_IQ4_XS = 23 };
 
 /* ---- formats and bit conversions ---- */
 uint16_t orc_bf16_from_f32(float f);

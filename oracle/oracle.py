@@ -17,6 +17,8 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 Q2_0 = 42
 IQ2_S = 22
+IQ4_NL = 20  # oracle only (no kernel reads it yet)
+IQ4_XS = 23  # oracle only
 
 _f32p = C.POINTER(C.c_float)
 _u8p = C.POINTER(C.c_uint8)

@@ -27,7 +27,7 @@ P = O._ptr
 def rand_rows(rng, t, rows, n_in):
     """Random weight rows with fp16 scales of exponent 7..11, a quarter negative (iq_parity.cpp:316-332)."""
     rb = O.row_bytes(t, n_in)
-    bs = 18 if t == O.Q2_0 else 82
+    bs = {O.Q2_0: 18, O.IQ2_S: 82, O.IQ4_NL: 18, O.IQ4_XS: 136}[t]
     w = rng.integers(0, 256, rows * rb, dtype=np.uint8)
     for o in range(0, w.size, bs):
         h = (0x8000 if rng.integers(0, 4) == 0 else 0) | (int(rng.integers(7, 12)) << 10) | int(rng.integers(0, 1024))
@@ -133,6 +133,15 @@ def main():
     g["bits_v"] = v
     g["bits_bf16"] = np.array([R.ref_bf16_from_f32(float(a)) for a in v], np.uint16)
     g["bits_f16"] = np.array([R.ref_f16_from_f32(float(a)) for a in v], np.uint16)
+    # the IQ4 formats (the reference's next gate/up and down formats; oracle only): their own generator, so the
+    # arrays above do not change
+    r4 = np.random.default_rng(4420)
+    for name, t, n_in, n_out in (("iq4nl_512", O.IQ4_NL, 512, 48), ("iq4xs_2048", O.IQ4_XS, 2048, 48)):
+        w = rand_rows(r4, t, n_out, n_in)
+        xq = ref_q8(r4.standard_normal(n_in).astype(np.float32))
+        g[f"dot_{name}_w"] = w
+        g[f"dot_{name}_x"] = xq
+        g[f"dot_{name}_y"] = ref_rows(t, w, xq, n_in, n_out)
     out = Path(__file__).with_name("golden.npz")
     np.savez_compressed(out, **g)
     print(f"wrote {out} ({out.stat().st_size} bytes, {len(g)} arrays)")

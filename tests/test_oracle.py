@@ -30,7 +30,8 @@ def test_q8_1_bitwise_including_clamped_scale(golden):
 
 
 @pytest.mark.parametrize("name,t,n_in", [("q2_2048", O.Q2_0, 2048), ("q2_512", O.Q2_0, 512),
-                                         ("iq2s_2048", O.IQ2_S, 2048), ("q2_64", O.Q2_0, 64)])
+                                         ("iq2s_2048", O.IQ2_S, 2048), ("q2_64", O.Q2_0, 64),
+                                         ("iq4nl_512", O.IQ4_NL, 512), ("iq4xs_2048", O.IQ4_XS, 2048)])
 def test_row_dot_bitwise(golden, name, t, n_in):
     w, xq, want = golden[f"dot_{name}_w"], golden[f"dot_{name}_x"], golden[f"dot_{name}_y"]
     got = O.mmvq(t, w, xq, n_in, want.size, 1)[0]
@@ -105,10 +106,10 @@ def test_live_reference_cross_check():
     if R is None:
         pytest.skip("oracle/_ref not built here (the reference tree is absent)")
     rng = np.random.default_rng(7)
-    for t, n_in in ((O.Q2_0, 2048), (O.IQ2_S, 2048), (O.Q2_0, 512)):
+    for t, n_in in ((O.Q2_0, 2048), (O.IQ2_S, 2048), (O.Q2_0, 512), (O.IQ4_NL, 512), (O.IQ4_XS, 2048)):
         rb = O.row_bytes(t, n_in)
         w = rng.integers(0, 256, 8 * rb, dtype=np.uint8)
-        bs = 18 if t == O.Q2_0 else 82
+        bs = {O.Q2_0: 18, O.IQ2_S: 82, O.IQ4_NL: 18, O.IQ4_XS: 136}[t]
         for o in range(0, w.size, bs):
             h = int(np.float16(abs(rng.standard_normal()) * 0.05).view(np.uint16))
             w[o], w[o + 1] = h & 255, h >> 8
@@ -212,3 +213,21 @@ def test_rms_norm_rule():
     g2 = O.add_rms_norm(x, r, None, 1e-6)
     assert np.allclose((g2.astype(np.float64) ** 2).mean(axis=1), 1.0, atol=1e-5)
     assert np.array_equal(g2, O.add_rms_norm((x + r).astype(np.float32), None, None, 1e-6))
+
+
+def test_iq4_fields_are_observable(golden):
+    """The IQ4 partials read each code byte's two nibbles as values i and i + 16, and IQ4_XS's 6-bit scales take
+    two high bits from the scales_h word: swapping the nibbles, or clearing scales_h, must move the rows far."""
+    for name, t, n_in, bs in (("iq4nl_512", O.IQ4_NL, 512, 18), ("iq4xs_2048", O.IQ4_XS, 2048, 136)):
+        w, xq, want = golden[f"dot_{name}_w"], golden[f"dot_{name}_x"], golden[f"dot_{name}_y"]
+        qs0 = 2 if t == O.IQ4_NL else 8
+        sw = w.copy()
+        for o in range(0, sw.size, bs):
+            b = sw[o + qs0:o + bs]
+            sw[o + qs0:o + bs] = (b >> 4) | ((b & 15) << 4)
+        assert O.rel_l1(want, O.mmvq(t, sw, xq, n_in, want.size, 1)[0]) > 0.05
+        if t == O.IQ4_XS:
+            hz = w.copy()
+            for o in range(0, hz.size, bs):
+                hz[o + 2] = hz[o + 3] = 0
+            assert O.rel_l1(want, O.mmvq(t, hz, xq, n_in, want.size, 1)[0]) > 0.05
