@@ -82,7 +82,8 @@ smoe_status smoe_iq_quantize_q8_1(const float* x, int64_t n, uint8_t* y, void* s
 /* iq_mmvq (iq.hpp:50-51, iq.mm:148-169; CUDA contract include/strata/kernels/iq_kernels.hpp:30):
  * y[c * n_out + r] = W[r] . x[c] for n_col q8_1 columns, W n_out rows of ggml_type over n_in values.
  * The sum of a row follows the reference's 32-lane order (iq.metal:459-514) and is bitwise its host
- * reference (iq_parity.cpp:275-292). */
+ * reference (iq_parity.cpp:275-292).  Types: Q2_0 (42), IQ2_S (22), and at this entry point only IQ4_NL (20,
+ * 18 B / 32 values) and IQ4_XS (23, 136 B / 256; iq_parity.cpp:196-222); n_col at most 65535 for the IQ4 types. */
 smoe_status smoe_iq_mmvq(int ggml_type, const uint8_t* w, const uint8_t* x_q8, int64_t n_in, int64_t n_out,
                          int64_t n_col, float* y, void* stream);
 

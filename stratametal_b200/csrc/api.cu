@@ -334,7 +334,18 @@ smoe_status smoe_iq_mmvq(int ggml_type, const uint8_t* w, const uint8_t* x_q8, i
     // iq.mm:150-158
     if (n_in == 0 || n_out == 0 || n_col == 0) return ok();
     if (n_in < 0 || n_out < 0 || n_col < 0) return fail(SMOE_INVALID_ARG, "iq_mmvq: negative size");
-    if (!block_values(ggml_type)) return fail(SMOE_UNSUPPORTED, "iq_mmvq: type is not Q2_0 or IQ2_S");
+    if (ggml_type == kIQ4_NL || ggml_type == kIQ4_XS) {  // iq4.cu: this entry point only, not the layer path
+        if (n_in % (ggml_type == kIQ4_NL ? 32 : 256))
+            return fail(SMOE_INVALID_ARG, "iq_mmvq: n_in is not a whole number of blocks");
+        if (n_in > 4096) return fail(SMOE_UNSUPPORTED, "iq_mmvq: n_in is at most 4096");
+        if (n_out > 0x7fffffff || n_col > 65535) return fail(SMOE_INVALID_ARG, "iq_mmvq: size does not fit");
+        if (!stream) return fail(SMOE_INVALID_ARG, "iq_mmvq: a non-null stream is required");
+        if (!w || !x_q8 || !y) return fail(SMOE_INVALID_ARG, "iq_mmvq: null buffer");
+        const cudaError_t e = launch_iq4_mmvq(ggml_type, w, x_q8, (int) n_in, (int) n_out, (int) n_col, y,
+                                              (cudaStream_t) stream);
+        return e == cudaSuccess ? ok() : cuda_fail(e, "iq_mmvq");
+    }
+    if (!block_values(ggml_type)) return fail(SMOE_UNSUPPORTED, "iq_mmvq: type is not Q2_0, IQ2_S, IQ4_NL or IQ4_XS");
     if (!row_bytes(ggml_type, n_in)) return fail(SMOE_INVALID_ARG, "iq_mmvq: n_in is not a whole number of blocks");
     if (n_in > 4096) return fail(SMOE_UNSUPPORTED, "iq_mmvq: n_in is at most 4096");
     if (n_out > 0x7fffffff || n_col > 0x7fffffff) return fail(SMOE_INVALID_ARG, "iq_mmvq: size does not fit in int");

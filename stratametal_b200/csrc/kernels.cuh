@@ -107,6 +107,9 @@ struct Matrix {
 };
 
 // y[slot][r] = down_e[r] . act[slot] for every slot, y row stride y_stride floats; act rows n_in / 32 blocks.
+// ---- iq4.cu ---- (IQ4_NL / IQ4_XS rows against q8_1 columns, the reference's row_dot order)
+cudaError_t launch_iq4_mmvq(int type, const uint8_t* w, const uint8_t* x, int n_in, int n_out, int n_col,
+                            float* y, cudaStream_t s);
 cudaError_t launch_expert_down(Matrix down, Matrix sdown, GroupView g, const uint8_t* act, int act_by_token,
                                float* y, int64_t y_stride, int n_in, int n_out, cudaStream_t s);
 

@@ -6,6 +6,7 @@
 #include "combine.cu"
 #include "tc.cu"
 #include "tq.cu"
+#include "iq4.cu"
 #include "elementwise.cu"
 #include "decode.cu"
 #include "ep.cu"

@@ -57,6 +57,8 @@ def test_mmvq_and_combine_refusals(L):
     assert L.smoe_iq_mmvq(42, None, None, 100, 4, 1, None, None) == 1         # not whole blocks
     assert L.smoe_iq_mmvq(42, None, None, -64, 4, 1, None, None) == 1         # negative
     assert L.smoe_iq_mmvq(42, None, None, 0, 4, 1, None, None) == 0           # zero: no launch
+    assert L.smoe_iq_mmvq(20, None, None, 48, 4, 1, None, None) == 1         # IQ4_NL: not whole blocks
+    assert L.smoe_iq_mmvq(23, None, None, 256, 4, 1, None, None) == 1        # IQ4_XS: no stream
     assert L.smoe_moe_combine(None, None, None, None, 16, 65, 1, None) == 1   # k = 65
     assert L.smoe_moe_combine(None, None, None, None, -1, 4, 1, None) == 1    # negative
     assert L.smoe_moe_combine(None, None, None, None, 0, 10, 1, None) == 0    # zero length

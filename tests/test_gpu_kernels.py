@@ -39,7 +39,8 @@ def test_bf16_bulk_bitwise(golden, cuda):
 
 
 @pytest.mark.parametrize("name,t,n_in", [("q2_2048", O.Q2_0, 2048), ("q2_512", O.Q2_0, 512),
-                                         ("iq2s_2048", O.IQ2_S, 2048), ("q2_64", O.Q2_0, 64)])
+                                         ("iq2s_2048", O.IQ2_S, 2048), ("q2_64", O.Q2_0, 64),
+                                         ("iq4nl_512", O.IQ4_NL, 512), ("iq4xs_2048", O.IQ4_XS, 2048)])
 def test_mmvq_golden_bitwise(golden, cuda, name, t, n_in):
     w, xq, want = golden[f"dot_{name}_w"], golden[f"dot_{name}_x"], golden[f"dot_{name}_y"]
     y = torch.full((want.size + 16,), 7.0, device=cuda)
@@ -51,12 +52,14 @@ def test_mmvq_golden_bitwise(golden, cuda, name, t, n_in):
 
 @pytest.mark.parametrize("t,n_in,n_out,n_col", [(O.Q2_0, 2048, 512, 5), (O.Q2_0, 512, 2048, 3),
                                                 (O.IQ2_S, 2048, 96, 4), (O.Q2_0, 256, 40, 3), (O.IQ2_S, 512, 40, 3),
-                                                (O.Q2_0, 2560, 100, 2), (O.Q2_0, 640, 70, 2)])
+                                                (O.Q2_0, 2560, 100, 2), (O.Q2_0, 640, 70, 2),
+                                                (O.IQ4_NL, 2048, 70, 3), (O.IQ4_NL, 32, 9, 2), (O.IQ4_XS, 4096, 33, 2),
+                                                (O.IQ4_XS, 256, 8, 3)])
 def test_mmvq_random_bitwise(cuda, t, n_in, n_out, n_col):
     rng = np.random.default_rng(n_in * 7 + n_out)
     rb = O.row_bytes(t, n_in)
     w = rng.integers(0, 256, n_out * rb, dtype=np.uint8)
-    bs = 18 if t == O.Q2_0 else 82
+    bs = {O.Q2_0: 18, O.IQ2_S: 82, O.IQ4_NL: 18, O.IQ4_XS: 136}[t]
     for o in range(0, w.size, bs):
         h = int(np.float16(abs(rng.standard_normal()) * 0.05).view(np.uint16))
         w[o], w[o + 1] = h & 255, h >> 8
