@@ -15,6 +15,12 @@
 static const uint64_t k_iq2s_grid[1024] = {
 #include "../stratametal_b200/csrc/iq2s_grid.inc"
 };
+static const uint32_t k_iq3xxs_grid[256] = {
+#include "../stratametal_b200/csrc/iq3xxs_grid.inc"
+};
+static const uint32_t k_iq3s_grid[512] = {
+#include "../stratametal_b200/csrc/iq3s_grid.inc"
+};
 
 /* ------------------------------------------------------------------------------------------------ */
 /* bit conversions                                                                                  */
@@ -87,6 +93,8 @@ size_t orc_row_bytes(int type, int64_t n) {
     if (type == ORC_IQ2_S) return (n % 256) ? 0 : (size_t) (n / 256) * 82u;
     if (type == ORC_IQ4_NL) return (n % 32) ? 0 : (size_t) (n / 32) * 18u;
     if (type == ORC_IQ4_XS) return (n % 256) ? 0 : (size_t) (n / 256) * 136u;
+    if (type == ORC_IQ3_XXS) return (n % 256) ? 0 : (size_t) (n / 256) * 98u;
+    if (type == ORC_IQ3_S) return (n % 256) ? 0 : (size_t) (n / 256) * 110u;
     return 0;
 }
 
@@ -220,6 +228,61 @@ static float iq4_xs_partial(const uint8_t* blk, const uint8_t* xblk, int ib) {
     return d * (float) sumi;
 }
 
+/* Sum over one 4-value codebook entry: magnitudes (bytes of `e`) times q, value j negated when bit j of `neg`
+ * is set. */
+static int32_t grid4(uint32_t e, unsigned neg, const uint8_t* xblk, int v0) {
+    int32_t s = 0;
+    for (int j = 0; j < 4; j++) {
+        int v = (int) ((e >> (8 * j)) & 0xFFu);
+        if ((neg >> j) & 1u) v = -v;
+        s += v * (int32_t) q8_at(xblk, v0 + j);
+    }
+    return s;
+}
+
+/* IQ3_XXS (fp16 d, qs[64] grid indices, 8 words of signs and scale @66; 256 values) 32-value group g
+ * (iq_parity.cpp:153-173): word w = bytes 66 + 4g; chunk c (8 values) uses grid entries qs[8g + 2c] (values
+ * 8c..8c+3) and qs[8g + 2c + 1] (8c+4..8c+7) with the 7 sign bits (w >> 7c) & 127 completed by their parity as
+ * bit 7; sumi = (ls * sumi + sumi / 2) / 2 (C truncating division), ls = w >> 28. */
+static float iq3_xxs_partial(const uint8_t* blk, const uint8_t* xblk, int g) {
+    const uint8_t* qs = blk + 2;
+    const uint32_t w = (uint32_t) qs[64 + 4 * g] | ((uint32_t) qs[65 + 4 * g] << 8) | ((uint32_t) qs[66 + 4 * g] << 16) |
+                       ((uint32_t) qs[67 + 4 * g] << 24);
+    int32_t sumi = 0;
+    for (int c = 0; c < 4; c++) {
+        unsigned s7 = (w >> (7 * c)) & 127u, par = 0;
+        for (int b = 0; b < 7; b++) par ^= (s7 >> b) & 1u;
+        const unsigned sg = s7 | (par << 7);
+        sumi += grid4(k_iq3xxs_grid[qs[8 * g + 2 * c]], sg & 15u, xblk, 8 * c);
+        sumi += grid4(k_iq3xxs_grid[qs[8 * g + 2 * c + 1]], sg >> 4, xblk, 8 * c + 4);
+    }
+    const int32_t ls = (int32_t) (w >> 28);
+    sumi = (ls * sumi + sumi / 2) / 2;
+    const float d = orc_f32_from_f16(rd16(blk)) * orc_f32_from_f16(rd16(xblk));
+    return d * (float) sumi;
+}
+
+/* IQ3_S (fp16 d, qs[64], qh[8] @66, signs[32] @74, scales[4] @106; 256 values) 32-value group g
+ * (iq_parity.cpp:175-194): chunk c takes 9-bit indices qs[8g + 2c] | bit 2c of qh[g] << 8 and qs[8g + 2c + 1] |
+ * bit 2c + 1 << 8, sign byte signs[4g + c] (bits 0-3 the first entry's values, 4-7 the second's); sumi * (1 + 2
+ * nib), nib = nibble g & 1 of scales[g / 2]. */
+static float iq3_s_partial(const uint8_t* blk, const uint8_t* xblk, int g) {
+    const uint8_t* qs = blk + 2;
+    const unsigned qh = blk[66 + g];
+    int32_t sumi = 0;
+    for (int c = 0; c < 4; c++) {
+        const unsigned i0 = qs[8 * g + 2 * c] | (((qh >> (2 * c)) & 1u) << 8);
+        const unsigned i1 = qs[8 * g + 2 * c + 1] | (((qh >> (2 * c + 1)) & 1u) << 8);
+        const unsigned sb = blk[74 + 4 * g + c];
+        sumi += grid4(k_iq3s_grid[i0], sb & 15u, xblk, 8 * c);
+        sumi += grid4(k_iq3s_grid[i1], sb >> 4, xblk, 8 * c + 4);
+    }
+    const int nib = (blk[106 + g / 2] >> (4 * (g & 1))) & 15;
+    sumi *= 1 + 2 * nib;
+    const float d = orc_f32_from_f16(rd16(blk)) * orc_f32_from_f16(rd16(xblk));
+    return d * (float) sumi;
+}
+
 /* row_dot (iq_parity.cpp:275-292): the row's partials in order (32 values each, IQ4_NL 16), partial k added to
  * lane k & 31, then the 32 lane sums meet in an xor butterfly (16, 8, 4, 2, 1). */
 static float row_dot_impl(int type, const uint8_t* row, const uint8_t* col, int n_in, int variant) {
@@ -231,6 +294,8 @@ static float row_dot_impl(int type, const uint8_t* row, const uint8_t* col, int 
         if (type == ORC_IQ2_S) p = iq2_s_partial(row + (size_t) (k / 8) * 82, col + (size_t) k * 36, k % 8);
         else if (type == ORC_IQ4_NL) p = iq4_nl_partial(row + (size_t) (k / 2) * 18, col + (size_t) (k / 2) * 36, k % 2);
         else if (type == ORC_IQ4_XS) p = iq4_xs_partial(row + (size_t) (k / 8) * 136, col + (size_t) k * 36, k % 8);
+        else if (type == ORC_IQ3_XXS) p = iq3_xxs_partial(row + (size_t) (k / 8) * 98, col + (size_t) k * 36, k % 8);
+        else if (type == ORC_IQ3_S) p = iq3_s_partial(row + (size_t) (k / 8) * 110, col + (size_t) k * 36, k % 8);
         else p = q2_0_partial(row + (size_t) (k / 2) * 18, col + (size_t) k * 36, k % 2, variant != 1);
         lane[k & 31] += p;
     }

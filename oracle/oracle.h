@@ -10,7 +10,9 @@
  *   - Q2_0 partial dot (code - 1)            metal/src/iq_parity.cpp:225-252 (dot_q2_0), pack_parity.cpp:2736-2757
  *   - IQ2_S partial dot                      metal/src/iq_parity.cpp:125-151 (dot_iq2_s)
  *   - IQ4_NL / IQ4_XS partial dots           metal/src/iq_parity.cpp:106-115, 196-222 (dot_iq4_nl, dot_iq4_xs);
- *                                            geometry :256-263 (geom_of).  Oracle only: no kernel reads them yet
+ *   - IQ3_XXS / IQ3_S partial dots           metal/src/iq_parity.cpp:79-101, 153-194 (dot_iq3_xxs, dot_iq3_s);
+ *                                            geometry :256-263 (geom_of).  The layer path takes none of these
+ *                                            four; the stage entry point smoe_iq_mmvq takes IQ4_NL and IQ4_XS
  *   - 32-lane row accumulation + butterfly   metal/src/iq_parity.cpp:275-292 (row_dot), pack_parity.cpp:2759-2772
  *   - SwiGLU then q8_1 of h                  metal/src/iq_parity.cpp:384-411 (silu, ref_expert)
  *   - bf16 router dot, double accumulation   metal/src/pack_parity.cpp:3793-3799 (round_bf16, bf16_dot)
@@ -33,7 +35,7 @@
 extern "C" {
 #endif
 
-enum { ORC_Q2_0 = 42, ORC_IQ2_S = 22, ORC_IQ4_NL = 20, ORC_IQ4_XS = 23 };
+enum { ORC_Q2_0 = 42, ORC_IQ2_S = 22, ORC_IQ4_NL = 20, ORC_IQ4_XS = 23, ORC_IQ3_XXS = 18, ORC_IQ3_S = 21 };
 
 /* ---- formats and bit conversions ---- */
 uint16_t orc_bf16_from_f32(float f);

@@ -27,7 +27,7 @@ P = O._ptr
 def rand_rows(rng, t, rows, n_in):
     """Random weight rows with fp16 scales of exponent 7..11, a quarter negative (iq_parity.cpp:316-332)."""
     rb = O.row_bytes(t, n_in)
-    bs = {O.Q2_0: 18, O.IQ2_S: 82, O.IQ4_NL: 18, O.IQ4_XS: 136}[t]
+    bs = {O.Q2_0: 18, O.IQ2_S: 82, O.IQ4_NL: 18, O.IQ4_XS: 136, O.IQ3_XXS: 98, O.IQ3_S: 110}[t]
     w = rng.integers(0, 256, rows * rb, dtype=np.uint8)
     for o in range(0, w.size, bs):
         h = (0x8000 if rng.integers(0, 4) == 0 else 0) | (int(rng.integers(7, 12)) << 10) | int(rng.integers(0, 1024))
@@ -139,6 +139,13 @@ def main():
     for name, t, n_in, n_out in (("iq4nl_512", O.IQ4_NL, 512, 48), ("iq4xs_2048", O.IQ4_XS, 2048, 48)):
         w = rand_rows(r4, t, n_out, n_in)
         xq = ref_q8(r4.standard_normal(n_in).astype(np.float32))
+        g[f"dot_{name}_w"] = w
+        g[f"dot_{name}_x"] = xq
+        g[f"dot_{name}_y"] = ref_rows(t, w, xq, n_in, n_out)
+    r3 = np.random.default_rng(4421)
+    for name, t, n_in, n_out in (("iq3xxs_2048", O.IQ3_XXS, 2048, 48), ("iq3s_2048", O.IQ3_S, 2048, 48)):
+        w = rand_rows(r3, t, n_out, n_in)
+        xq = ref_q8(r3.standard_normal(n_in).astype(np.float32))
         g[f"dot_{name}_w"] = w
         g[f"dot_{name}_x"] = xq
         g[f"dot_{name}_y"] = ref_rows(t, w, xq, n_in, n_out)

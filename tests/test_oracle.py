@@ -31,7 +31,8 @@ def test_q8_1_bitwise_including_clamped_scale(golden):
 
 @pytest.mark.parametrize("name,t,n_in", [("q2_2048", O.Q2_0, 2048), ("q2_512", O.Q2_0, 512),
                                          ("iq2s_2048", O.IQ2_S, 2048), ("q2_64", O.Q2_0, 64),
-                                         ("iq4nl_512", O.IQ4_NL, 512), ("iq4xs_2048", O.IQ4_XS, 2048)])
+                                         ("iq4nl_512", O.IQ4_NL, 512), ("iq4xs_2048", O.IQ4_XS, 2048),
+                                         ("iq3xxs_2048", O.IQ3_XXS, 2048), ("iq3s_2048", O.IQ3_S, 2048)])
 def test_row_dot_bitwise(golden, name, t, n_in):
     w, xq, want = golden[f"dot_{name}_w"], golden[f"dot_{name}_x"], golden[f"dot_{name}_y"]
     got = O.mmvq(t, w, xq, n_in, want.size, 1)[0]
@@ -106,10 +107,11 @@ def test_live_reference_cross_check():
     if R is None:
         pytest.skip("oracle/_ref not built here (the reference tree is absent)")
     rng = np.random.default_rng(7)
-    for t, n_in in ((O.Q2_0, 2048), (O.IQ2_S, 2048), (O.Q2_0, 512), (O.IQ4_NL, 512), (O.IQ4_XS, 2048)):
+    for t, n_in in ((O.Q2_0, 2048), (O.IQ2_S, 2048), (O.Q2_0, 512), (O.IQ4_NL, 512), (O.IQ4_XS, 2048),
+                    (O.IQ3_XXS, 512), (O.IQ3_S, 512)):
         rb = O.row_bytes(t, n_in)
         w = rng.integers(0, 256, 8 * rb, dtype=np.uint8)
-        bs = {O.Q2_0: 18, O.IQ2_S: 82, O.IQ4_NL: 18, O.IQ4_XS: 136}[t]
+        bs = {O.Q2_0: 18, O.IQ2_S: 82, O.IQ4_NL: 18, O.IQ4_XS: 136, O.IQ3_XXS: 98, O.IQ3_S: 110}[t]
         for o in range(0, w.size, bs):
             h = int(np.float16(abs(rng.standard_normal()) * 0.05).view(np.uint16))
             w[o], w[o + 1] = h & 255, h >> 8
