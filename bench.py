@@ -1,28 +1,33 @@
 #!/usr/bin/env python
 """MoE-layer throughput of the B200 implementation (and, with --impl reference, of the reference's CPU path).
 
-Workload: one MoE layer (hidden 2048, 512 experts of intermediate 512, top-10,
-Q2_0 experts, sigmoid-gated shared expert), 64 decode tokens per step, Zipf(1.1) expert popularity.
-A step is one smoe_moe_forward over one batch: router, dispatch, expert products, combine.
+Headline workload: one MoE layer (hidden 2048, 512 experts of intermediate 512, top-10,
+Q2_0 experts, sigmoid-gated shared expert), 64 decode tokens per step, Zipf(1.1) expert popularity.  A step is
+one smoe_moe_forward over one batch: router, dispatch, expert products, combine.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C] [--subs LIST]
+
+The same JSON line carries a sub-record per other BASELINE configuration ("configs"): configs[0] (one decode
+token), configs[2] (4096-token prefill), configs[3] (the 48-layer stack at batch 1 and at batch 16) and configs[4]
+(IQ2_S gate/up, batch 8), each timed the same way with the same K and W.
 
 Timing: each step's smoe_moe_forward calls are captured once as a CUDA graph (one graph per (layer, batch)
 forward; for configs[3] one graph for the whole 48-layer stack with its residual add + RMSNorm); W untimed
 replays, then exactly K replays between CUDA events on the replay stream, bracketed by a barrier and a
 synchronize, max over ranks.  Per-stage times come from a separate eager pass with stage events.  Each step's
-expert bytes (~200 MB at 64 tokens) exceed the 126 MB L2 and the steps rotate over --layers distinct seeded
-layers, so weights stream from HBM.  Rank 0 prints one JSON line.  N > 1 runs independent replicas for the
-decode configs (decode does not shard: "replicas only"), value = all ranks' tokens / time; configs[2] and
-configs[3] at batch 16 run expert-parallel instead: the step's tokens split over the N ranks, E / N experts per
-rank, token rows and down rows exchanged over peer memory inside smoe_ep_forward (strong scaling).
+expert bytes exceed the 126 MB L2 or the steps rotate over enough distinct seeded layers that they do, so
+weights stream from HBM.  Rank 0 prints one JSON line.  N > 1 runs independent replicas for the decode configs
+(decode does not shard: "replicas only"), value = all ranks' tokens / time; configs[2] and configs[3] at batch 16
+run expert-parallel instead: the step's tokens split over the N ranks, E / N experts per rank, token rows and down
+rows exchanged over peer memory inside smoe_ep_forward (strong scaling).
 
-  python bench.py --config 3 [--tokens 16]    # the 48-layer stack at batch 1 (or 16)
-  python bench.py --config 2                  # 4096-token prefill (tensor-core expert kernels)
+  python bench.py --config 3 [--tokens 16] --subs none   # the 48-layer stack at batch 1 (or 16) alone
+  python bench.py --config 2 --subs none                 # 4096-token prefill alone
 """
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -44,35 +49,53 @@ KERNEL_OF_STAGE = {"router_gemv": "bf16_gemv_kernel", "router_topk_q8": "router_
                    "expert_down": "layer_down_kernel", "combine": "combine_kernel"}
 KERNEL_OF_STAGE_TC = dict(KERNEL_OF_STAGE, expert_gate_up="tc_expert_kernel<0>", expert_down="tc_expert_kernel<1>")
 KERNEL_OF_STAGE_TQ = dict(KERNEL_OF_STAGE, expert_gate_up="tq_expert_kernel<0>", expert_down="tq_expert_kernel<1>")
+# sub-records: name -> (config, tokens per step, single-layer configs: distinct layers x batches rotated)
+SUBS = {"cfg0_b1": (0, 1, (16, 1)), "cfg2_prefill4096": (2, 4096, (2, 1)), "cfg3_stack48_b1": (3, 1, None),
+        "cfg3_stack48_b16": (3, 16, None), "cfg4_iq2s_b8": (4, 8, (4, 4))}
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
     ap.add_argument("--expert-path", type=int, default=0, choices=[0, 1, 2, 4],
                     help="0 automatic, 1 SIMT expert kernels, 2 fp16 tensor-core kernels, 4 int8 tensor-core kernels")
-    ap.add_argument("--layers", type=int, default=4, help="distinct layers rotated through the steps")
+    ap.add_argument("--layers", type=int, default=4, help="distinct layers rotated through the headline's steps")
     ap.add_argument("--tokens", type=int, default=0, help="override the config's tokens per step (configs[3]: 1 or 16)")
+    ap.add_argument("--subs", default="auto",
+                    help="sub-records to add: 'auto' (every other config when the headline is configs[1]), 'none', "
+                         "or a comma list of " + ",".join(SUBS))
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.subs == "auto":
+        a.sub_list = list(SUBS) if (a.config == 1 and not a.tokens and a.expert_path == 0) else []
+    elif a.subs == "none":
+        a.sub_list = []
+    else:
+        a.sub_list = [s for s in a.subs.split(",") if s]
+        for s in a.sub_list:
+            if s not in SUBS:
+                raise SystemExit(f"unknown sub-record {s}")
+    return a
 
 
 # ---------------------------------------------------------------------------------------------------
-# clocks during the timed region (read-only NVML queries)
+# clocks during the timed regions (read-only NVML queries)
 # ---------------------------------------------------------------------------------------------------
 class ClockSampler:
+    """Samples the SM clock and the throttle reasons every few milliseconds while a timed region is open
+    (`with sampler.timed(): ...`), over every timed region of the run."""
     REASONS = {"gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
                "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, index: int, period: float = 0.01):
+    def __init__(self, index: int, period: float = 0.004):
         self.samples, self.reasons, self.ok = [], set(), False
-        self.period, self.stop_flag = period, threading.Event()
+        self.period, self.stop_flag, self.active = period, threading.Event(), threading.Event()
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -82,27 +105,38 @@ class ClockSampler:
             self.ok = True
         except Exception as e:  # noqa: BLE001
             self.err = str(e)
-
-    def _run(self):
-        nv = self.nv
-        while not self.stop_flag.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
-                for name, bit in self.REASONS.items():
-                    if r & bit and name != "gpu_idle":
-                        self.reasons.add(name)
-            except Exception:  # noqa: BLE001
-                pass
-            time.sleep(self.period)
-
-    def __enter__(self):
         if self.ok:
             self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-        return self
 
-    def __exit__(self, *a):
+    def _sample(self):
+        nv = self.nv
+        try:
+            self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+            r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+            for name, bit in self.REASONS.items():
+                if r & bit and name != "gpu_idle":
+                    self.reasons.add(name)
+        except Exception:  # noqa: BLE001
+            pass
+
+    def _run(self):
+        while not self.stop_flag.is_set():
+            if self.active.is_set():
+                self._sample()
+            time.sleep(self.period)
+
+    @contextlib.contextmanager
+    def timed(self):
+        self.active.set()
+        try:
+            yield
+        finally:
+            self.active.clear()
+            if self.ok:
+                self._sample()  # at least one sample per timed region, however short
+
+    def stop(self):
         if self.ok:
             self.stop_flag.set()
             self.t.join()
@@ -111,15 +145,16 @@ class ClockSampler:
         if not self.ok or not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": getattr(self, "err", "no samples")}
         return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+                "reasons": sorted(self.reasons), "samples": len(self.samples),
+                "window": "every timed region of this run (headline and sub-records)"}
 
 
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
 
 
 def traffic_per_unit():
@@ -225,7 +260,12 @@ def max_over_ranks(v: float, ws: int) -> float:
     return float(t.item())
 
 
-def config_dict(args, spec, T, D_mean, n_layers=None, stack=False):
+def schedule(K: int, n_layers: int, n_batches: int) -> list[tuple[int, int]]:
+    """The (layer, batch) forward that timed step i replays, for the first K steps."""
+    return [(i % n_layers, (i // n_layers) % n_batches) for i in range(K)]
+
+
+def config_dict(gpus, cfg, spec, T, D_mean, n_layers, n_batches, stack=False):
     if stack:
         return {"workload": f"configs[3]: stack of {n_layers} MoE layers (residual add + RMSNorm between them), "
                             f"{T} decode tokens/step",
@@ -233,15 +273,33 @@ def config_dict(args, spec, T, D_mean, n_layers=None, stack=False):
                 "n_expert": spec.n_expert, "top_k": spec.k, "expert_format": "Q2_0", "shared_expert": True,
                 "distinct_experts_per_layer": D_mean, "rms_eps": RMS_EPS,
                 "l2": "inputs larger than L2: one step streams every layer's routed experts (> 400 MB)",
-                "parallelism": f"replicas x{args.gpus}", "seed": spec.seed}
-    return {"workload": f"configs[{args.config}]: one MoE layer, {T} {'decode' if T <= 64 else 'prefill'} tokens/step"
+                "parallelism": f"replicas x{gpus}", "seed": spec.seed}
+    return {"workload": f"configs[{cfg}]: one MoE layer, {T} {'decode' if T <= 64 else 'prefill'} tokens/step"
                         + (", Zipf(1.1) expert popularity" if spec.zipf else "")
                         + (", IQ2_S gate/up" if spec.gu_type == 22 else ""),
             "tokens_per_step": T, "n_embd": spec.n_embd, "n_ff": spec.n_ff, "n_expert": spec.n_expert,
             "top_k": spec.k, "expert_format": "IQ2_S gate/up + Q2_0 down" if spec.gu_type == 22 else "Q2_0",
-            "shared_expert": True, "distinct_experts_per_step": D_mean, "layers_rotated": args.layers,
-            "l2": "inputs larger than L2: each step streams its experts' weights (> 126 MB), layers rotate",
-            "parallelism": f"replicas x{args.gpus}", "seed": spec.seed}
+            "shared_expert": True, "distinct_experts_per_step": D_mean, "layers_rotated": n_layers,
+            "batches_rotated": n_batches,
+            "l2": "inputs larger than L2: the (layer, batch) forwards a step cycles through stream > 126 MB of "
+                  "expert weights",
+            "parallelism": f"replicas x{gpus}", "seed": spec.seed}
+
+
+def reference_distinct_experts(spec, T, n_layers, n_batches, K):
+    """The mean number of distinct routed experts per step of the headline schedule, from the oracle's router
+    stage on the same seeded routers and tokens (the GPU arm reads the same figure from its own traces)."""
+    import numpy as np
+
+    from oracle import oracle as O
+    from stratametal_b200 import synth
+    D = {}
+    for li in range(n_layers):
+        r = synth.router_weights(spec, li, "cpu").numpy().view(np.uint16)
+        for b in range(n_batches):
+            x = synth.make_x(spec.seed, T, spec.n_embd, "cpu", stream=b).numpy()
+            D[(li, b)] = int(np.unique(O.router(r, x, spec.k)[1]).size)
+    return float(np.mean([D[s] for s in schedule(K, n_layers, n_batches)]))
 
 
 def run_reference(args, ws, rank):
@@ -255,6 +313,7 @@ def run_reference(args, ws, rank):
     if args.tokens:
         T = args.tokens
     stack = args.config == 3
+    n_layers, n_batches = (STACK_LAYERS, 1) if stack else (args.layers, 4)
     lay = synth.make_layer(spec, 0, "cpu")
     x = synth.make_x(spec.seed, T, spec.n_embd).numpy()
     run, kind, threads = cpu_layer_runner(lay)
@@ -275,42 +334,47 @@ def run_reference(args, ws, rank):
     if stack:  # the stack's layers share one shape: tokens/s through all of them
         value /= STACK_LAYERS
         sample += f"; stack tokens/s = layer tokens/s / {STACK_LAYERS}"
+    D_mean = None if stack else reference_distinct_experts(spec, T, n_layers, n_batches, args.steps)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int2 dot, f32/f64 sums", "data": "synthetic",
-            "config": config_dict(args, spec, T, None, STACK_LAYERS, stack), "impl": "reference",
+            "config": config_dict(args.gpus, args.config, spec, T, D_mean, n_layers, n_batches, stack),
+            "impl": "reference",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args, ws, rank, local):
+# ---------------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------------
+def measure(args, ws, rank, local, clk, cfg, T_req, rot):
+    """Times one configuration; returns its record (rank 0) after releasing its device memory.  rot = (distinct
+    layers, batches) rotated through the steps of a single-layer config; None for the stack."""
     import ctypes as C
 
     import numpy as np
     import torch
 
-    from stratametal_b200 import api, build, synth
+    from stratametal_b200 import api, synth
     from stratametal_b200._lib import lib
-    build.build()
     dev = torch.device("cuda", local)
-    torch.cuda.set_stream(torch.cuda.Stream(dev))  # the C ABI wants an explicit non-null stream
-    spec, T = synth.config_spec(args.config)
-    if args.tokens:
-        T = args.tokens
+    spec, T = synth.config_spec(cfg)
+    if T_req:
+        T = T_req
     H = spec.n_embd
-    stack = args.config == 3
-    n_layers = STACK_LAYERS if stack else args.layers
-    n_batches = 1 if stack else 4
-    api.set_expert_path(args.expert_path)
+    stack = cfg == 3
+    n_layers, n_batches = (STACK_LAYERS, 1) if stack else rot
     # expert parallelism for the batched and prefill workloads on N > 1 GPUs: the step's tokens split evenly over
     # the ranks (strong scaling), E / N routed experts per rank, the exchange inside smoe_ep_forward
-    ep_mode = ws > 1 and (args.config == 2 or (stack and T > 1))
+    ep_mode = ws > 1 and (cfg == 2 or (stack and T > 1))
+    T_all = T
+    areas = None
     if ep_mode:
         from stratametal_b200 import ep
         if T % ws:
             raise SystemExit(f"{T} tokens do not split over {ws} ranks")
-        T_all, T = T, T // ws
+        T = T // ws
         areas = ep.EpAreas.distributed(spec, T)
         layers = [ep.EpLayer(ep.shard_layer(spec, li, rank, ws, dev), areas, dev) for li in range(n_layers)]
         path = lib().smoe_expert_path_for(C.byref(layers[0].c), T_all)
@@ -383,7 +447,7 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     barrier(ws)
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    with clk.timed():
         start.record(gstream)
         for i in range(K):
             graphs[i % G].replay()
@@ -395,9 +459,9 @@ def run_ours(args, ws, rank, local):
     value = ws * T / (ms_step * 1e-3)
     assert api.device_status() == 0
 
-    # per-stage device time: an eager pass with stage events (single layers only)
+    # per-stage device time: an eager pass with stage events (single layers, one rank per layer)
     stage_ms = None
-    if not stack:
+    if not stack and not ep_mode:
         Ks = min(K, 500)
         ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)] for _ in range(Ks)]
         for row in ev:  # torch creates the CUDA event on its first record
@@ -416,22 +480,37 @@ def run_ours(args, ws, rank, local):
             for j, s in enumerate(STAGES):
                 stage_ms[s] += ev[i][j].elapsed_time(ev[i][j + 1]) / Ks
 
-    hbm_peak, peak_kind = peaks()
+    hbm_peak, tensor_peak, peak_kind = peaks()
     E_BYTES = spec.expert_bytes()
     rbg = synth.row_bytes(spec.gu_type, spec.n_embd) * spec.n_ff
     rbd = synth.row_bytes(spec.d_type, spec.n_ff) * spec.n_embd
     q8x, q8h = (spec.n_embd // 32) * 36, (spec.n_ff // 32) * 36
     rows = T * spec.k + T  # slots per rank (in expectation the same with expert parallelism)
+    flop_gu = 2.0 * rows * 2 * spec.n_embd * spec.n_ff   # useful FLOPs of the gate/up products
+    flop_dn = 2.0 * rows * spec.n_embd * spec.n_ff
     if stack:
         Ds = [D[(li, 0)] for li in range(n_layers)]
         step_bytes = float(sum((d + 1) * E_BYTES for d in Ds))
         D_mean = float(np.mean(Ds))
-        expert_gbs = step_bytes / (ms_step * 1e-3) / 1e9
-        roof = {"bound": "hbm", "kernel": "whole 48-layer stack (CUDA graph)", "achieved": expert_gbs,
-                "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": expert_gbs / hbm_peak,
-                "traffic": None, "algorithmic_bytes_per_launch": step_bytes, "ms_per_launch": ms_step}
+        expert_gbs = step_bytes / (ms_step * 1e-3) / 1e9 * (ws if ep_mode else 1)
+        roof = {"bound": "hbm", "kernel": f"whole {n_layers}-layer stack (CUDA graph"
+                + (f", {ws} ranks" if ep_mode else "") + ")",
+                "achieved": expert_gbs, "peak": hbm_peak * (ws if ep_mode else 1), "peak_kind": peak_kind,
+                "unit": "GB/s", "frac": expert_gbs / (hbm_peak * (ws if ep_mode else 1)), "traffic": None,
+                "algorithmic_bytes_per_launch": step_bytes, "ms_per_launch": ms_step,
+                "per_layer_us": 1e3 * ms_step / n_layers}
+    elif ep_mode:
+        Ds = [D[s] for s in schedule(K, n_layers, n_batches)]
+        D_mean = float(np.mean(Ds))
+        flops = ws * (flop_gu + flop_dn)
+        achieved = flops / (ms_step * 1e-3) / 1e12
+        expert_gbs = ws * (D_mean + 1) * E_BYTES / (ms_step * 1e-3) / 1e9
+        roof = {"bound": "tensor", "kernel": f"whole expert-parallel step over {ws} ranks",
+                "achieved": achieved, "peak": tensor_peak * ws, "peak_kind": peak_kind + " (bf16 dense, burst)",
+                "unit": "TFLOP/s", "frac": achieved / (tensor_peak * ws), "traffic": None,
+                "algorithmic_flops_per_launch": flops, "ms_per_launch": ms_step}
     else:
-        Ds = [D[(i % n_layers, (i // n_layers) % n_batches)] for i in range(K)]
+        Ds = [D[s] for s in schedule(K, n_layers, n_batches)]
         D_mean = float(np.mean(Ds))
         alg = {"expert_gate_up": lambda d: (d + 1) * 2 * rbg + T * q8x + rows * q8h,
                "expert_down": lambda d: (d + 1) * rbd + rows * q8h + rows * spec.n_embd * 4,
@@ -445,22 +524,31 @@ def run_ours(args, ws, rank, local):
         else:
             dominant = max(stage_ms, key=stage_ms.get)
             dom_ms = stage_ms[dominant]
-        dom_bytes = float(np.mean([alg[dominant](d) for d in Ds])) if dominant in alg else None
-        achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_bytes else None
-        tpu = traffic_per_unit()
-        traffic = None
-        if dominant == "expert_gate_up" and not tc and not tq and "expert_gate_up_per_expert" in tpu:
-            traffic = tpu["expert_gate_up_per_expert"] * (D_mean + 1)
-        elif dominant == "expert_gate_up" and tq and "tq_gate_up_per_expert" in tpu:
-            traffic = tpu["tq_gate_up_per_expert"] * (D_mean + 1)
         expert_gbs = (D_mean + 1) * E_BYTES / (ms_step * 1e-3) / 1e9
         kos = KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE_TQ if tq else KERNEL_OF_STAGE
         if 2 <= T <= 64:
             kos = dict(kos, router_gemv="router_gemm_kernel + router_reduce_kernel (split K)")
-        roof = {"bound": "hbm", "kernel": "decode_layer_kernel" if fused else kos[dominant],
-                "achieved": achieved, "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
-                "frac": achieved / hbm_peak if achieved else None, "traffic": traffic,
-                "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms}
+        kname = "decode_layer_kernel" if fused else kos[dominant]
+        if tc and dominant in ("expert_gate_up", "expert_down"):
+            flops = flop_gu if dominant == "expert_gate_up" else flop_dn
+            achieved = flops / (dom_ms * 1e-3) / 1e12
+            roof = {"bound": "tensor", "kernel": kname, "achieved": achieved, "peak": tensor_peak,
+                    "peak_kind": peak_kind + " (bf16 dense, burst)", "unit": "TFLOP/s",
+                    "frac": achieved / tensor_peak, "traffic": None, "algorithmic_flops_per_launch": flops,
+                    "ms_per_launch": dom_ms,
+                    "hbm_gbs_of_weights": float(np.mean([alg[dominant](d) for d in Ds])) / (dom_ms * 1e-3) / 1e9}
+        else:
+            dom_bytes = float(np.mean([alg[dominant](d) for d in Ds])) if dominant in alg else None
+            achieved = dom_bytes / (dom_ms * 1e-3) / 1e9 if dom_bytes else None
+            tpu = traffic_per_unit()
+            traffic = None
+            if dominant == "expert_gate_up" and not tc and not tq and "expert_gate_up_per_expert" in tpu:
+                traffic = tpu["expert_gate_up_per_expert"] * (D_mean + 1)
+            elif dominant == "expert_gate_up" and tq and "tq_gate_up_per_expert" in tpu:
+                traffic = tpu["tq_gate_up_per_expert"] * (D_mean + 1)
+            roof = {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": hbm_peak, "peak_kind": peak_kind,
+                    "unit": "GB/s", "frac": achieved / hbm_peak if achieved else None, "traffic": traffic,
+                    "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms}
 
     # end to end: every step copies its input from pinned host memory, replays the captured API calls and
     # reads the result back
@@ -486,58 +574,98 @@ def run_ours(args, ws, rank, local):
                   "D2H of the output"}
     assert api.device_status() == 0
 
+    # router (GEMV, or split-K GEMM + reduce from 2 to 64 tokens), top-k, grouping (3 launches above 256 tokens),
+    # gate/up, SwiGLU (SIMT only), down, combine; the fp16 tensor-core path adds the hi/lo image
+    router_l = 2 if 2 <= T <= 64 else 1
+    group_l = 3 if T > 256 else 1
+    if tc:
+        per_fwd = router_l + 1 + 1 + group_l + 3
+    elif tq:
+        per_fwd = router_l + 1 + group_l + 3
+    else:
+        per_fwd = router_l + 1 + group_l + 4 + (0 if spec.sg_type == spec.gu_type else 2) + \
+            (0 if spec.sd_type == spec.d_type else 2)
+    if fused:
+        per_fwd = 1
+    if ep_mode:  # router, top-k, dispatch, receive, grouping over the ws * T received rows, experts, wait, combine
+        per_fwd = router_l + 1 + 1 + 1 + (3 if ws * T > 256 else 1) + (2 if tc or tq else 3) + 1 + 1
+    launches_per_step = n_layers * (per_fwd + 1) if stack else per_fwd
+
+    cfgd = config_dict(args.gpus, cfg, spec, T_all, D_mean, n_layers, n_batches, stack)
+    if ep_mode:
+        cfgd["parallelism"] = (f"expert parallel x{ws}: {spec.n_expert // ws} routed experts and {T} of the "
+                               f"{T_all} tokens per GPU; dispatch and return over peer memory (CUDA IPC, "
+                               f"NVLink), no collective on the data path")
+        cfgd["distinct_experts_per_step"] = f"{D_mean} on rank 0 (of its {spec.n_expert // ws})"
+    rec = {"value": value, "unit": UNIT, "ms_per_step": ms_step, "n_gpus": ws,
+           "scaling": "strong" if ep_mode else "weak",
+           "dtype": ("fp16 x fp16 tcgen05 (exact hi/lo q8_1 image), f32 accumulate" if tc
+                     else "int8 x int8 tcgen05 (q8_1 contract, s32 per 32-value partial), f32 epilogue in the "
+                          "reference's order" if tq
+                     else "int8 x int2 dot (q8_1 contract), f32/f64 sums"),
+           "expert_path": ("fp16 tensor cores (tcgen05)" if tc else "int8 tensor cores (tcgen05 kind::i8)" if tq
+                           else "fused single-token kernel (one cooperative launch)" if fused else "SIMT"),
+           "config": cfgd,
+           "timing": "CUDA events around CUDA-graph replays (one captured forward per step"
+                     + (", the whole 48-layer stack" if stack else "") + ")",
+           "expert_weight_gbs": expert_gbs, "expert_weight_frac_of_peak": expert_gbs / (hbm_peak * (ws if ep_mode else 1)),
+           "roofline": roof, "stage_ms_per_step": stage_ms, "e2e": e2e, "gpu_launches_per_step": launches_per_step,
+           "gpu_launches": K * launches_per_step, "_T": T, "_spec": spec, "_x0": xs[0].cpu().numpy(),
+           "_n_layers": n_layers}
+
+    # release this configuration's graphs and buffers before the next one
+    del graphs
+    torch.cuda.synchronize()
+    barrier(ws)
+    if areas is not None:  # every rank's kernels are done before any rank unmaps or frees an exchange area
+        areas.close()
+    del layers, xs, out, sbuf
+    torch.cuda.empty_cache()
+    barrier(ws)
+    return rec
+
+
+def public(rec: dict) -> dict:
+    return {k: v for k, v in rec.items() if not k.startswith("_")}
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+
+    from stratametal_b200 import api, build, synth
+    build.build()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_stream(torch.cuda.Stream(dev))  # the C ABI wants an explicit non-null stream
+    api.set_expert_path(args.expert_path)
+    clk = ClockSampler(local)
+    try:
+        rot = (STACK_LAYERS, 1) if args.config == 3 else (args.layers, 4)
+        head = measure(args, ws, rank, local, clk, args.config, args.tokens, rot)
+        subs = {}
+        for name in args.sub_list:
+            cfg, T, srot = SUBS[name]
+            subs[name] = measure(args, ws, rank, local, clk, cfg, T, srot)
+    finally:
+        clk.stop()
+
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(synth.make_layer(spec, 0, "cpu"), xs[0].cpu().numpy(), args.cpu_seconds,
-                           n_layers if stack else 1)
+        spec = head["_spec"]
+        cpu = cpu_baseline(synth.make_layer(spec, 0, "cpu"), head["_x0"], args.cpu_seconds,
+                           head["_n_layers"] if args.config == 3 else 1)
 
     if rank == 0:
-        # router GEMV, top-k (+ q8_1), dispatch, gate/up, [SwiGLU], down, combine; the tensor-core path adds the
-        # hi/lo activation image and fuses SwiGLU into gate/up; grouping above 256 tokens takes three launches
-        # router (GEMV, or split-K GEMM + reduce from 2 to 64 tokens), top-k, grouping (3 launches above 256
-        # tokens), gate/up, SwiGLU (SIMT only), down, combine; the fp16 tensor-core path adds the hi/lo image
-        router_l = 2 if 2 <= T <= 64 else 1
-        group_l = 3 if T > 256 else 1
-        if tc:
-            per_fwd = router_l + 1 + 1 + group_l + 3
-        elif tq:
-            per_fwd = router_l + 1 + group_l + 3
-        else:
-            per_fwd = router_l + 1 + group_l + 4 + (0 if spec.sg_type == spec.gu_type else 2) + \
-                (0 if spec.sd_type == spec.d_type else 2)
-        if fused:
-            per_fwd = 1
-        if ep_mode:  # router, top-k, dispatch, receive, grouping over the ws * T received rows, experts, wait, combine
-            per_fwd = router_l + 1 + 1 + 1 + (3 if ws * T > 256 else 1) + (2 if tc or tq else 3) + 1 + 1
-        launches_per_step = n_layers * (per_fwd + 1) if stack else per_fwd
-        cfgd = config_dict(args, spec, T_all if ep_mode else T, D_mean, n_layers, stack)
-        if ep_mode:
-            cfgd["parallelism"] = (f"expert parallel x{ws}: {spec.n_expert // ws} routed experts and {T} of the "
-                                   f"{T_all} tokens per GPU; dispatch and return over peer memory (CUDA IPC, "
-                                   f"NVLink), no collective on the data path")
-            cfgd["distinct_experts_per_step"] = f"{D_mean} on rank 0 (of its {spec.n_expert // ws})"
-        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
-                "ms_per_step": ms_step, "higher_is_better": True,
-                "scaling": "strong" if ep_mode else "weak", "vs_baseline": None,
-                "dtype": ("fp16 x fp16 tcgen05 (exact hi/lo q8_1 image), f32 accumulate" if tc
-                          else "int8 x int8 tcgen05 (q8_1 contract, s32 per 32-value partial), f32 epilogue in the "
-                               "reference's order" if tq
-                          else "int8 x int2 dot (q8_1 contract), f32/f64 sums"), "data": "synthetic",
-                "expert_path": ("fp16 tensor cores (tcgen05)" if tc else "int8 tensor cores (tcgen05 kind::i8)" if tq
-                                else "fused single-token kernel (one cooperative launch)" if fused else "SIMT"),
-                "config": cfgd,
-                "timing": "CUDA events around CUDA-graph replays (one captured forward per step"
-                          + (", the whole 48-layer stack" if stack else "") + ")",
-                "expert_weight_gbs": expert_gbs, "expert_weight_frac_of_peak": expert_gbs / hbm_peak,
-                "roofline": roof, "stage_ms_per_step": stage_ms,
-                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": K * launches_per_step,
-                "clocks": clk.summary()}
+        K, W = args.steps, args.warmup
+        line = {"metric": METRIC, "value": head["value"], "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
+                "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": head["scaling"],
+                "vs_baseline": None, "dtype": head["dtype"], "data": "synthetic", "expert_path": head["expert_path"],
+                "config": head["config"], "timing": head["timing"], "expert_weight_gbs": head["expert_weight_gbs"],
+                "expert_weight_frac_of_peak": head["expert_weight_frac_of_peak"], "roofline": head["roofline"],
+                "stage_ms_per_step": head["stage_ms_per_step"], "cpu_baseline": cpu, "e2e": head["e2e"],
+                "gpu_launches": head["gpu_launches"], "clocks": clk.summary()}
+        if subs:
+            line["configs"] = {name: public(r) for name, r in subs.items()}
         print(json.dumps(line), flush=True)
-    if ep_mode:  # every rank's kernels are done before any rank unmaps or frees an exchange area
-        del graphs
-        torch.cuda.synchronize()
-        barrier(ws)
-        areas.close()
 
 
 def main():

@@ -83,7 +83,8 @@ smoe_status smoe_iq_quantize_q8_1(const float* x, int64_t n, uint8_t* y, void* s
  * y[c * n_out + r] = W[r] . x[c] for n_col q8_1 columns, W n_out rows of ggml_type over n_in values.
  * The sum of a row follows the reference's 32-lane order (iq.metal:459-514) and is bitwise its host
  * reference (iq_parity.cpp:275-292).  Types: Q2_0 (42), IQ2_S (22), and at this entry point only IQ4_NL (20,
- * 18 B / 32 values) and IQ4_XS (23, 136 B / 256; iq_parity.cpp:196-222); n_col at most 65535 for the IQ4 types. */
+ * 18 B / 32 values) and IQ4_XS (23, 136 B / 256; iq_parity.cpp:196-222).  Every type: n_in at most 4096, n_out
+ * and n_col at most 2^31 - 1, w 16-byte and x_q8 4-byte aligned. */
 smoe_status smoe_iq_mmvq(int ggml_type, const uint8_t* w, const uint8_t* x_q8, int64_t n_in, int64_t n_out,
                          int64_t n_col, float* y, void* stream);
 
@@ -100,7 +101,9 @@ smoe_status smoe_moe_combine(const float* parts, const float* weights, const flo
 /* fused::group (include/strata/prefill/moe_fused.hpp:46-50): routing ids [n_tok][k] -> expert groups.
  * Writes, inside `scratch` (smoe_moe_group_scratch_bytes), counts[n_expert], offsets[n_expert + 1] and the
  * active-expert list; slot[i] = the grouped row of pair i (i = t * k + j); src[row] = its token.  Rows of
- * one expert are in token order (the reference leaves that order free; this build fixes it). */
+ * one expert are in token order (the reference leaves that order free; this build fixes it).  A token's k ids
+ * must name k different experts, as the router's do: a pair that repeats an expert named earlier in its token
+ * gets slot -1 and no row, and the device status records 2 (an id outside the pool gets the same). */
 size_t smoe_moe_group_scratch_bytes(int n_tok, int k, int n_expert);
 smoe_status smoe_moe_group(const int32_t* ids, int n_tok, int k, int n_expert, void* scratch, int32_t* slot,
                            int32_t* src, void* stream);
@@ -110,8 +113,10 @@ smoe_status smoe_moe_group(const int32_t* ids, int n_tok, int k, int n_expert, v
  * allocation on the token path, plug-ins inside a process that owns the allocator): the grouping tables live
  * in a static 12,544-byte device array instead of caller scratch, so at most 1024 experts (more is refused
  * with SMOE_INVALID_ARG).  Allocates nothing.  The first call on each device looks up the array's device
- * address (cudaGetSymbolAddress) and must come before any stream capture.  All calls on a device share the
- * array; calls that overlap on the GPU race, so order them on one stream. */
+ * address (cudaGetSymbolAddress) and must come before any stream capture.  The address is kept for the life of
+ * the process: after cudaDeviceReset (or anything else that destroys the device's primary context) it is
+ * stale, so do not call this entry point on that device again in the same process.  All calls on a device
+ * share the array; calls that overlap on the GPU race, so order them on one stream. */
 smoe_status smoe_moe_group_noalloc(const int32_t* ids, int n_tok, int k, int n_expert, int32_t* slot, int32_t* src,
                                    void* stream);
 

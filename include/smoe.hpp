@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <memory>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -127,7 +128,14 @@ public:
     uint64_t gpu_bytes() const { return scratch_bytes_; }  // dense buffers this exec owns (the weights are the caller's)
 
 private:
+    // Device buffers of one traced call.  Each allocation is owned as soon as it succeeds, so a failure part way
+    // through the constructor frees the ones already made (the destructor of a half-built object never runs).
     struct DeviceTrace {
+        struct Free {
+            void operator()(void* p) const { cudaFree(p); }
+        };
+        using Buf = std::unique_ptr<void, Free>;
+        Buf bufs[6];
         float* logits = nullptr;
         int32_t* ids = nullptr;
         float* weights = nullptr;
@@ -135,20 +143,18 @@ private:
         float* parts = nullptr;
         float* shared = nullptr;
         DeviceTrace(size_t T, size_t H, size_t K, size_t E, size_t q8) {
-            check_cuda(cudaMalloc(reinterpret_cast<void**>(&logits), T * E * 4), "FfnTrace");
-            check_cuda(cudaMalloc(reinterpret_cast<void**>(&ids), T * K * 4), "FfnTrace");
-            check_cuda(cudaMalloc(reinterpret_cast<void**>(&weights), T * K * 4), "FfnTrace");
-            check_cuda(cudaMalloc(reinterpret_cast<void**>(&xq), T * q8), "FfnTrace");
-            check_cuda(cudaMalloc(reinterpret_cast<void**>(&parts), T * K * H * 4), "FfnTrace");
-            check_cuda(cudaMalloc(reinterpret_cast<void**>(&shared), T * H * 4), "FfnTrace");
-        }
-        ~DeviceTrace() {
-            cudaFree(logits);
-            cudaFree(ids);
-            cudaFree(weights);
-            cudaFree(xq);
-            cudaFree(parts);
-            cudaFree(shared);
+            const size_t bytes[6] = {T * E * 4, T * K * 4, T * K * 4, T * q8, T * K * H * 4, T * H * 4};
+            void* p[6] = {};
+            for (int i = 0; i < 6; i++) {
+                check_cuda(cudaMalloc(&p[i], bytes[i]), "FfnTrace");
+                bufs[i].reset(p[i]);
+            }
+            logits = static_cast<float*>(p[0]);
+            ids = static_cast<int32_t*>(p[1]);
+            weights = static_cast<float*>(p[2]);
+            xq = static_cast<uint8_t*>(p[3]);
+            parts = static_cast<float*>(p[4]);
+            shared = static_cast<float*>(p[5]);
         }
         void copy(void* dst, const void* src, size_t bytes) {
             check_cuda(cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost), "FfnTrace");
@@ -168,7 +174,8 @@ private:
 };
 
 // Several MoE layers walked in order: y_l = MoE_l(x), x = rms_norm(y_l + x) * norm_l (norm_l may be null: unit
-// weight).  Two ping-pong buffers of max_tokens rows are owned by the stack.
+// weight).  Two ping-pong buffers of max_tokens rows are owned by the stack.  Every layer must run on the same
+// stream: layer l + 1 reads the buffer layer l wrote, and only stream order makes that read wait for the write.
 class Stack {
 public:
     Stack(std::vector<FfnExec> layers, std::vector<const float*> norms, float eps)
@@ -180,16 +187,18 @@ public:
         max_tokens_ = layers_[0].max_tokens();
         for (auto& l : layers_) {
             if (l.layer().n_embd != L0.n_embd) throw Error(SMOE_INVALID_ARG, "Stack: layers differ in n_embd");
+            if (l.stream() != layers_[0].stream())
+                throw Error(SMOE_INVALID_ARG, "Stack: every layer must be loaded on the same stream");
             if (l.max_tokens() < max_tokens_) max_tokens_ = l.max_tokens();
         }
-        for (int i = 0; i < 2; i++)
-            check_cuda(cudaMalloc(&buf_[i], (size_t) max_tokens_ * L0.n_embd * 4), "Stack");
+        for (int i = 0; i < 2; i++) {
+            void* p = nullptr;
+            check_cuda(cudaMalloc(&p, (size_t) max_tokens_ * L0.n_embd * 4), "Stack");
+            buf_[i].reset(static_cast<float*>(p));
+        }
     }
     Stack(const Stack&) = delete;
     Stack& operator=(const Stack&) = delete;
-    ~Stack() {
-        for (auto* b : buf_) cudaFree(b);
-    }
 
     // x[T][n_embd] through every layer; returns the device buffer that holds the result (owned by the stack).
     const float* forward(const float* x, int n_tokens) {
@@ -197,7 +206,7 @@ public:
         const int H = layers_[0].layer().n_embd;
         const float* cur = x;
         for (size_t l = 0; l < layers_.size(); l++) {
-            float* nxt = buf_[l & 1];
+            float* nxt = buf_[l & 1].get();
             layers_[l].run(cur, nxt, n_tokens);
             check(smoe_add_rms_norm(nxt, cur, norms_.empty() ? nullptr : norms_[l], n_tokens, H, eps_,
                                     layers_[l].stream()),
@@ -210,11 +219,14 @@ public:
     int max_tokens() const { return max_tokens_; }  // the smallest arena among the layers
 
 private:
+    struct Free {
+        void operator()(float* p) const { cudaFree(p); }
+    };
     std::vector<FfnExec> layers_;
     std::vector<const float*> norms_;
     float eps_;
     int max_tokens_ = 0;
-    float* buf_[2] = {nullptr, nullptr};
+    std::unique_ptr<float, Free> buf_[2];
 };
 
 }  // namespace smoe

@@ -468,6 +468,21 @@ static double dot_f32(int type, const uint8_t* row, const float* x, int n, float
     return acc;
 }
 
+/* The router stage alone for T tokens (layer_exec.cpp:470-472): x rounded to bf16, logits by bf16_dot
+ * (pack_parity.cpp:3793-3799), then route_ref (pack_parity.cpp:5144-5165); the same steps as phase 0 below. */
+void orc_router(const float* x, int T, const uint16_t* router, int n_expert, int n_embd, int k, float* logits,
+                int32_t* ids, float* w) {
+    float* xr = (float*) malloc(sizeof(float) * (size_t) n_embd);
+    for (int t = 0; t < T; t++) {
+        const float* xt = x + (size_t) t * n_embd;
+        float* lt = logits + (size_t) t * n_expert;
+        for (int i = 0; i < n_embd; i++) xr[i] = orc_f32_from_bf16(orc_bf16_from_f32(xt[i]));
+        for (int e = 0; e < n_expert; e++) lt[e] = orc_bf16_dot(xr, router + (size_t) e * n_embd, n_embd);
+        orc_route(lt, n_expert, k, ids + (size_t) t * k, w + (size_t) t * k);
+    }
+    free(xr);
+}
+
 /* phase 0: per token routing + q8_1; phase 1: gate/up rows; phase 2: SwiGLU (+ q8_1 of h);
  * phase 3: down rows. */
 static void run_item(layer_job* J, int item, float* scratch) {

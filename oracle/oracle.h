@@ -56,6 +56,9 @@ void orc_mmvq(int type, const uint8_t* w, const uint8_t* x_q8, int n_in, int n_o
 void orc_swiglu_q8(const float* gate, const float* up, int64_t n, uint8_t* y);
 float orc_bf16_dot(const float* x_rounded, const uint16_t* row, int n);
 void orc_route(const float* logits, int n_expert, int k, int32_t* ids, float* w);
+/* bf16 rounding of x, the router logits and the routing of T tokens (the block's first stage). */
+void orc_router(const float* x, int T, const uint16_t* router, int n_expert, int n_embd, int k, float* logits,
+                int32_t* ids, float* w);
 void orc_combine(const float* parts, const float* w, const float* shared, float* y, int n_embd, int k);
 
 /* Dequantize one row to floats (exact: (code - 1) * d for Q2_0; d * (0.5 + ls) / 4 * signed grid for IQ2_S). */

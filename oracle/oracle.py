@@ -87,6 +87,8 @@ def lib() -> C.CDLL:
         L.orc_bf16_dot.restype = C.c_float
         L.orc_bf16_dot.argtypes = [_f32p, _u16p, C.c_int]
         L.orc_route.argtypes = [_f32p, C.c_int, C.c_int, _i32p, _f32p]
+        L.orc_router.argtypes = [_f32p, C.c_int, _u16p, C.c_int, C.c_int, C.c_int, _f32p, _i32p, _f32p]
+        L.orc_router.restype = None
         L.orc_combine.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_int, C.c_int]
         L.orc_dequant_row.argtypes = [C.c_int, _u8p, C.c_int, _f32p]
         L.orc_add_rms_norm.argtypes = [_f32p, _f32p, _f32p, C.c_int64, C.c_int64, C.c_float, _f32p]
@@ -165,6 +167,20 @@ def route(logits: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
     for t in range(T):
         lib().orc_route(_ptr(logits[t], _f32p), E, k, _ptr(ids[t], _i32p), _ptr(w[t], _f32p))
     return ids, w
+
+
+def router(router_bf16: np.ndarray, x: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """The block's router stage for x [T, n_embd]: (logits [T, E], ids [T, k], weights [T, k])."""
+    x = np.ascontiguousarray(x, np.float32)
+    r = np.ascontiguousarray(router_bf16, np.uint16)
+    T, H = x.shape
+    E = r.size // H
+    logits = np.empty((T, E), np.float32)
+    ids = np.empty((T, k), np.int32)
+    w = np.empty((T, k), np.float32)
+    lib().orc_router(_ptr(x, _f32p), T, _ptr(r, _u16p), E, H, k, _ptr(logits, _f32p), _ptr(ids, _i32p),
+                     _ptr(w, _f32p))
+    return logits, ids, w
 
 
 def combine(parts: np.ndarray, w: np.ndarray, shared: np.ndarray | None) -> np.ndarray:

@@ -178,3 +178,10 @@ class MoeLayer:
         check(lib().smoe_moe_forward(C.byref(self.c), _p(x), T, _p(out), self.scratch_ptr, self.scratch_bytes,
                                      C.byref(tr) if tr is not None else None, _s()))
         return out
+
+
+def expert_path_for(m: "MoeLayer", n_tokens: int) -> int:
+    """The expert path smoe_moe_forward takes for this layer and batch (smoe_expert_path_for): 1 SIMT, 2 fp16 tensor
+    cores, 3 fused single-token kernel, 4 int8 tensor cores."""
+    import ctypes as C
+    return int(lib().smoe_expert_path_for(C.byref(m.c), n_tokens))

@@ -338,9 +338,10 @@ smoe_status smoe_iq_mmvq(int ggml_type, const uint8_t* w, const uint8_t* x_q8, i
         if (n_in % (ggml_type == kIQ4_NL ? 32 : 256))
             return fail(SMOE_INVALID_ARG, "iq_mmvq: n_in is not a whole number of blocks");
         if (n_in > 4096) return fail(SMOE_UNSUPPORTED, "iq_mmvq: n_in is at most 4096");
-        if (n_out > 0x7fffffff || n_col > 65535) return fail(SMOE_INVALID_ARG, "iq_mmvq: size does not fit");
+        if (n_out > 0x7fffffff || n_col > 0x7fffffff) return fail(SMOE_INVALID_ARG, "iq_mmvq: size does not fit in int");
         if (!stream) return fail(SMOE_INVALID_ARG, "iq_mmvq: a non-null stream is required");
-        if (!w || !x_q8 || !y) return fail(SMOE_INVALID_ARG, "iq_mmvq: null buffer");
+        if (!w || !x_q8 || !y || !aligned(w, 16) || !aligned(x_q8, 4))
+            return fail(SMOE_INVALID_ARG, "iq_mmvq: w must be 16-byte and x 4-byte aligned");
         const cudaError_t e = launch_iq4_mmvq(ggml_type, w, x_q8, (int) n_in, (int) n_out, (int) n_col, y,
                                               (cudaStream_t) stream);
         return e == cudaSuccess ? ok() : cuda_fail(e, "iq_mmvq");

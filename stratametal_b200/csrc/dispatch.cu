@@ -39,6 +39,15 @@ Sched sched_at(void* base, int E, int T, int k, int chunk) {
     return Sched{p, p + cap, p + 2 * cap, p + 3 * cap, chunk};
 }
 
+// True when pair i names an expert that an earlier pair of the same token already named.  The router never does
+// (its k ids are distinct); a caller-supplied routing that does is malformed: the repeated pair gets no row
+// (slot -1), the device status records BAD_ID, and the counts include each (token, expert) once.
+__device__ __forceinline__ bool repeats_earlier(const int32_t* __restrict__ ids, size_t i, int k, int e) {
+    for (size_t j = i - i % (size_t) k; j < i; j++)
+        if (ids[j] == e) return true;
+    return false;
+}
+
 __device__ __forceinline__ uint32_t lanemask_lt() {
     uint32_t m;
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
@@ -186,7 +195,7 @@ __global__ void __launch_bounds__(1024) group_kernel(const int32_t* __restrict__
     for (int i = tid; i < T * k; i += blockDim.x) {
         const int t = i / k, c = t >> 6, tl = t & 63;
         const int e = ids[i];
-        if (e < 0 || e >= E) {
+        if (e < 0 || e >= E || repeats_earlier(ids, (size_t) i, k, e)) {
             slot[i] = -1;
             if (!(skip_negative && e < 0)) atomicOr(&g_smoe_status, kDevBadId);
             continue;
@@ -233,7 +242,7 @@ __global__ void __launch_bounds__(1024) group_kernel_any(const int32_t* __restri
                     const int tl = p / k;
                     const size_t i = (size_t) (t0 + tl) * k + (p % k);
                     const int e = ids[i];
-                    if (e < 0 || e >= E) {
+                    if (e < 0 || e >= E || repeats_earlier(ids, i, k, e)) {
                         slot[i] = -1;
                         if (!(skip_negative && e < 0)) atomicOr(&g_smoe_status, kDevBadId);
                         continue;
@@ -294,7 +303,7 @@ __global__ void __launch_bounds__(256) group_count_kernel(const int32_t* __restr
     __syncthreads();
     for (int p = threadIdx.x; p < nt * k; p += blockDim.x) {
         const int e = ids[(size_t) t0 * k + p];
-        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+        if (e >= 0 && e < E && !repeats_earlier(ids, (size_t) t0 * k + p, k, e)) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) cc[(size_t) c * E + e] = cnt[e];
@@ -354,7 +363,7 @@ __global__ void __launch_bounds__(256) group_assign_kernel(const int32_t* __rest
         const int tl = p / k;
         const size_t i = (size_t) t0 * k + p;
         const int e = ids[i];
-        if (e < 0 || e >= E) {
+        if (e < 0 || e >= E || repeats_earlier(ids, i, k, e)) {
             slot[i] = -1;
             if (!(skip_negative && e < 0)) atomicOr(&g_smoe_status, kDevBadId);
             continue;

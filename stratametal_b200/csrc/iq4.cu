@@ -33,9 +33,9 @@ __device__ __forceinline__ int iq4_sumi(const uint8_t* qs, const int8_t* q, int 
 
 template <int TYPE>
 __global__ void __launch_bounds__(256) iq4_mmvq_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ x,
-                                                       int n_in, int n_out, float* __restrict__ y) {
+                                                       int n_in, int n_out, float* __restrict__ y, int c0) {
     const int lane = threadIdx.x & 31;
-    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), c = blockIdx.y;
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), c = c0 + (int) blockIdx.y;
     if (r >= n_out) return;
     const size_t rb = TYPE == kIQ4_NL ? (size_t) (n_in / 32) * 18 : (size_t) (n_in / 256) * 136;
     const uint8_t* row = w + (size_t) r * rb;
@@ -70,11 +70,16 @@ __global__ void __launch_bounds__(256) iq4_mmvq_kernel(const uint8_t* __restrict
 
 cudaError_t launch_iq4_mmvq(int type, const uint8_t* w, const uint8_t* x, int n_in, int n_out, int n_col,
                             float* y, cudaStream_t s) {
-    const dim3 grid((unsigned) ((n_out + 7) / 8), (unsigned) n_col);
-    if (type == kIQ4_NL) iq4_mmvq_kernel<kIQ4_NL><<<grid, 256, 0, s>>>(w, x, n_in, n_out, y);
-    else if (type == kIQ4_XS) iq4_mmvq_kernel<kIQ4_XS><<<grid, 256, 0, s>>>(w, x, n_in, n_out, y);
-    else return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    if (type != kIQ4_NL && type != kIQ4_XS) return cudaErrorInvalidValue;
+    // columns in launches of at most 65535 (the grid's y limit)
+    for (int c0 = 0; c0 < n_col; c0 += 65535) {
+        const dim3 grid((unsigned) ((n_out + 7) / 8), (unsigned) min(65535, n_col - c0));
+        if (type == kIQ4_NL) iq4_mmvq_kernel<kIQ4_NL><<<grid, 256, 0, s>>>(w, x, n_in, n_out, y, c0);
+        else iq4_mmvq_kernel<kIQ4_XS><<<grid, 256, 0, s>>>(w, x, n_in, n_out, y, c0);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 }  // namespace smoe

@@ -15,6 +15,7 @@ Distributions (the choices the configs leave open are marked *
 """
 from __future__ import annotations
 
+import functools
 import math
 from dataclasses import dataclass, field
 
@@ -122,6 +123,7 @@ def bf16_bits(v: torch.Tensor) -> torch.Tensor:
 # Zipf routing calibration (cfg1)
 # ---------------------------------------------------------------------------------------------------
 
+@functools.lru_cache(maxsize=8)
 def zipf_row_scales(n_expert: int, k: int, s: float = 1.1, seed: int = 110, cap: float = 0.45,
                     iters: int = 40, n_sim: int = 4096) -> np.ndarray:
     """Factors f[rank] for router rows so that the chance a token selects the rank-r expert follows
@@ -149,6 +151,7 @@ def zipf_row_scales(n_expert: int, k: int, s: float = 1.1, seed: int = 110, cap:
         freq = np.bincount(top.ravel(), minlength=n_expert) / n_sim
         f *= np.clip((q / np.maximum(freq, 0.5 / n_sim)) ** 0.5, 0.5, 2.0)
         f /= np.exp(np.log(f).mean())
+    f.flags.writeable = False  # cached: shared by every caller
     return f
 
 
@@ -186,12 +189,10 @@ class Layer:
         return self.tensors[name]
 
 
-def make_layer(spec: LayerSpec, index: int, device="cpu", experts: range | None = None) -> Layer:
-    """Generate layer `index` of `spec` on `device`.  `experts` limits the routed planes to a subset
-    (an expert-parallel shard); the default generates all n_expert."""
-    H, F, E = spec.n_embd, spec.n_ff, spec.n_expert
+def router_weights(spec: LayerSpec, index: int, device="cpu") -> torch.Tensor:
+    """Layer `index`'s ffn_gate_inp (bf16 bits [n_expert, n_embd]) alone, as make_layer generates it."""
+    H, E = spec.n_embd, spec.n_expert
     base = _mix_py(spec.seed, index)
-    L = Layer(spec, index)
     w = normal(_mix_py(base, T_ROUTER), E * H, device).view(E, H) * 0.02
     if spec.zipf is not None:
         f = zipf_row_scales(E, spec.k, spec.zipf)
@@ -199,7 +200,16 @@ def make_layer(spec: LayerSpec, index: int, device="cpu", experts: range | None 
         scale = np.empty(E)
         scale[perm] = f  # expert perm[r] gets the rank-r factor
         w = w * torch.from_numpy(scale).to(device=device, dtype=torch.float64).view(E, 1)
-    L.tensors["ffn_gate_inp.weight"] = bf16_bits(w).contiguous()
+    return bf16_bits(w).contiguous()
+
+
+def make_layer(spec: LayerSpec, index: int, device="cpu", experts: range | None = None) -> Layer:
+    """Generate layer `index` of `spec` on `device`.  `experts` limits the routed planes to a subset
+    (an expert-parallel shard); the default generates all n_expert."""
+    H, F, E = spec.n_embd, spec.n_ff, spec.n_expert
+    base = _mix_py(spec.seed, index)
+    L = Layer(spec, index)
+    L.tensors["ffn_gate_inp.weight"] = router_weights(spec, index, device)
     ex = experts if experts is not None else range(E)
     for name, tid, t, rows, n_in in (("ffn_gate_exps.weight", T_GATE, spec.gu_type, F, H),
                                      ("ffn_up_exps.weight", T_UP, spec.gu_type, F, H),

@@ -158,6 +158,22 @@ static int run_gpu() {
     cudaMemcpy(a.data(), out, a.size() * 4, cudaMemcpyDeviceToHost);
     cudaMemcpy(b.data(), c2, b.size() * 4, cudaMemcpyDeviceToHost);
     EXPECT(std::memcmp(a.data(), b.data(), a.size() * 4) == 0);
+    // layers on different streams would race on the stack's ping-pong buffers: refused
+    cudaStream_t s2;
+    smoe::check_cuda(cudaStreamCreate(&s2), "stream");
+    {
+        std::vector<smoe::FfnExec> mixed;
+        mixed.push_back(smoe::FfnExec::load(L, 16, true, s));
+        mixed.push_back(smoe::FfnExec::load(L, 16, true, s2));
+        bool refused = false;
+        try {
+            smoe::Stack bad(std::move(mixed), {}, 1e-6f);
+        } catch (const smoe::Error& e) {
+            refused = e.status == SMOE_INVALID_ARG;
+        }
+        EXPECT(refused);
+    }
+    cudaStreamDestroy(s2);
     EXPECT(smoe_device_status(1) == 0);
     std::printf("run: %s\n", fails ? "FAIL" : "ok");
     return fails;

@@ -162,6 +162,36 @@ def test_group_stable(cuda, T, E, k):
     assert np.array_equal(src.cpu().numpy(), order // k)
 
 
+@pytest.mark.parametrize("T", [5, 300])  # one CTA; the any-size two-pass CTA
+def test_group_refuses_a_repeated_expert(cuda, T):
+    # a token whose ids name one expert twice: the second pair gets no row (slot -1) and BAD_ID is recorded;
+    # every other pair is grouped as if the repeat were absent
+    E, k = 64, 6
+    rng = np.random.default_rng(T)
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32)
+    ids[3, 4] = ids[3, 1]
+    scratch = torch.empty(api.moe_group_scratch_bytes(T, k, E), dtype=torch.uint8, device=cuda)
+    slot = torch.empty(T * k, dtype=torch.int32, device=cuda)
+    src = torch.empty(T * k, dtype=torch.int32, device=cuda)
+    api.device_status(clear=True)
+    api.moe_group(dev(ids, cuda), T, k, E, scratch, slot, src)
+    torch.cuda.synchronize()
+    assert api.device_status() == 2
+    got = slot.cpu().numpy()
+    bad = 3 * k + 4
+    assert got[bad] == -1
+    keep = np.ones(T * k, bool)
+    keep[bad] = False
+    flat = ids.ravel()
+    counts = scratch.cpu().numpy().view(np.int32)[:E]
+    assert np.array_equal(counts, np.bincount(flat[keep], minlength=E))
+    order = np.nonzero(keep)[0][np.argsort(flat[keep], kind="stable")]
+    want = np.full(T * k, -1)
+    want[order] = np.arange(order.size)
+    assert np.array_equal(got, want)
+    assert np.array_equal(src.cpu().numpy()[:order.size], order // k)
+
+
 @pytest.mark.parametrize("rows,cols,resid,weighted", [(1, 2048, True, False), (16, 2048, True, True),
                                                       (5, 1000, False, True)])
 def test_add_rms_norm(cuda, rows, cols, resid, weighted):

@@ -19,8 +19,8 @@ def inc_values(name: str) -> list[int]:
 
 
 def ref_header() -> Path | None:
-    m = re.search(r"^REF_ROOT \?= (\S+)", (ROOT / "oracle" / "Makefile").read_text(), re.M)
-    root = os.environ.get("REF_ROOT", m.group(1) if m else "")
+    # the Makefile's default: a checkout named `reference` beside this repository
+    root = os.environ.get("REF_ROOT", str(ROOT.parent / "reference"))
     p = Path(root) / "metal" / "include" / "strata" / "metal" / "iq_grids.hpp"
     return p if root and p.exists() else None
 
