@@ -32,7 +32,8 @@ typedef enum {
     SMOE_DEVICE_TIMEOUT = 4
 } smoe_status;
 
-enum { SMOE_Q2_0 = 42, SMOE_IQ2_S = 22 };
+/* ggml block formats (type ids) the layer and the stage entry points take. */
+enum { SMOE_Q2_0 = 42, SMOE_IQ2_S = 22, SMOE_IQ4_NL = 20, SMOE_IQ4_XS = 23, SMOE_IQ3_XXS = 18, SMOE_IQ3_S = 21 };
 
 /* Message of the last non-OK status returned on this thread ("" after an OK call). */
 const char* smoe_last_error(void);
@@ -45,7 +46,8 @@ unsigned smoe_device_status(int clear);
 /* ---- geometry ------------------------------------------------------------------------------------ */
 
 /* iq_row_bytes (metal/include/strata/metal/iq.hpp:41, iq.mm:124-129): bytes of one row of n values; 0 for an
- * unsupported type or a bad multiple.  Q2_0: 18 B / 64 values; IQ2_S: 82 B / 256. */
+ * unsupported type or a bad multiple.  Q2_0: 18 B / 64 values; IQ2_S: 82 B / 256; IQ4_NL: 18 B / 32; IQ4_XS:
+ * 136 B / 256; IQ3_XXS: 98 B / 256; IQ3_S: 110 B / 256 (iq.mm:99-122). */
 size_t smoe_row_bytes(int ggml_type, int64_t n);
 /* iq_q8_1_bytes (iq.hpp:43, iq.mm:131-134): 36 B per 32 values; 0 unless n is a positive multiple of 32. */
 size_t smoe_q8_1_bytes(int64_t n);
@@ -82,9 +84,9 @@ smoe_status smoe_iq_quantize_q8_1(const float* x, int64_t n, uint8_t* y, void* s
 /* iq_mmvq (iq.hpp:50-51, iq.mm:148-169; CUDA contract include/strata/kernels/iq_kernels.hpp:30):
  * y[c * n_out + r] = W[r] . x[c] for n_col q8_1 columns, W n_out rows of ggml_type over n_in values.
  * The sum of a row follows the reference's 32-lane order (iq.metal:459-514) and is bitwise its host
- * reference (iq_parity.cpp:275-292).  Types: Q2_0 (42), IQ2_S (22), and at this entry point only IQ4_NL (20,
- * 18 B / 32 values) and IQ4_XS (23, 136 B / 256; iq_parity.cpp:196-222).  Every type: n_in at most 4096, n_out
- * and n_col at most 2^31 - 1, w 16-byte and x_q8 4-byte aligned. */
+ * reference (iq_parity.cpp:275-292).  Types: Q2_0 (42), IQ2_S (22), IQ4_NL (20), IQ4_XS (23), IQ3_XXS (18) and
+ * IQ3_S (21) (iq.metal:516-549, host dots iq_parity.cpp:125-222).  Every type: n_in at most 4096, n_out and
+ * n_col at most 2^31 - 1, w 16-byte and x_q8 4-byte aligned. */
 smoe_status smoe_iq_mmvq(int ggml_type, const uint8_t* w, const uint8_t* x_q8, int64_t n_in, int64_t n_out,
                          int64_t n_col, float* y, void* stream);
 
@@ -127,7 +129,7 @@ smoe_status smoe_moe_group_noalloc(const int32_t* ids, int n_tok, int k, int n_e
  * at gate + e * n_ff * smoe_row_bytes(gu_type, n_embd). */
 typedef struct smoe_layer {
     int n_embd, n_ff, n_expert, k;
-    int gu_type, d_type;              /* routed gate/up type (Q2_0 or IQ2_S), down type (Q2_0) */
+    int gu_type, d_type;              /* routed gate/up and down types: any SMOE_* format above */
     const uint16_t* router;           /* ffn_gate_inp.weight       [n_expert][n_embd] bf16 */
     const uint8_t* gate;              /* ffn_gate_exps.weight      [n_expert][n_ff rows] */
     const uint8_t* up;                /* ffn_up_exps.weight        [n_expert][n_ff rows] */
@@ -179,10 +181,12 @@ smoe_status smoe_add_rms_norm(float* x, const float* residual, const float* w, i
  * n_embd and n_ff each 512, 1024 or 2048).  The SIMT, fused and int8 tensor-core kernels evaluate the
  * reference's q8_1 integer contract in the reference's summation order (bit for bit); the fp16 tensor-core
  * kernels evaluate the same products from an exact fp16 hi/lo split of the q8_1 activation with f32
- * accumulation, so their results agree up to the order of the f32 additions.  Process-wide. */
+ * accumulation, so their results agree up to the order of the f32 additions.  Process-wide.  Layers with any
+ * matrix in a format other than Q2_0 / IQ2_S always take the any-format kernels (path 5: the reference's row dot
+ * per format, grouped by expert, bit for bit), whatever the setting. */
 smoe_status smoe_set_expert_path(int path);
 /* The path smoe_moe_forward takes for this layer and batch: 1 SIMT, 2 fp16 tensor cores, 3 fused single-token
- * kernel, 4 int8 tensor cores, -1 invalid layer. */
+ * kernel, 4 int8 tensor cores, 5 any-format kernels, -1 invalid layer. */
 int smoe_expert_path_for(const smoe_layer* L, int n_tokens);
 
 /* Validates the layer's geometry and types: SMOE_OK when smoe_moe_forward can run it. */
@@ -235,7 +239,7 @@ size_t smoe_ep_scratch_bytes(const smoe_layer* L, const smoe_ep* ep);
  * one device runs phase 1 of every rank, then 2 of every rank, then 4, so that no kernel ever waits for one
  * launched after it.  Waits are bounded: a rank that does not take part makes the others record
  * SMOE_DEVICE_TIMEOUT in the status word within seconds.  Layers whose shared expert types differ from the
- * routed ones, and n_embd not a multiple of 128, are SMOE_UNSUPPORTED. */
+ * routed ones, formats other than Q2_0 / IQ2_S, and n_embd not a multiple of 128, are SMOE_UNSUPPORTED. */
 smoe_status smoe_ep_forward(const smoe_layer* L, const smoe_ep* ep, const float* x, int n_tokens, float* out,
                             void* scratch, size_t scratch_bytes, const smoe_trace* trace, int phases, void* stream);
 

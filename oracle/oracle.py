@@ -17,10 +17,10 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 Q2_0 = 42
 IQ2_S = 22
-IQ4_NL = 20  # the stage entry point smoe_iq_mmvq only (not the layer path)
-IQ4_XS = 23  # the stage entry point smoe_iq_mmvq only
-IQ3_XXS = 18  # oracle only
-IQ3_S = 21  # oracle only
+IQ4_NL = 20
+IQ4_XS = 23
+IQ3_XXS = 18
+IQ3_S = 21
 
 _f32p = C.POINTER(C.c_float)
 _u8p = C.POINTER(C.c_uint8)

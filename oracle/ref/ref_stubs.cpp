@@ -3,8 +3,9 @@
 // The parity .cpp files compiled beside this name Metal launchers and the shared-buffer class in code
 // paths this build never runs (their renamed main()).  Every launcher here throws.  The block geometry
 // helpers are real, because the host reference ref_expert() sizes its rows with them; their values are
-// the GGUF block sizes of metal/src/iq.mm:99-131 for the two formats this build uses (Q2_0 64 values /
-// 18 bytes, IQ2_S 256 / 82) and the q8_1 block (32 values / 36 bytes).
+// the GGUF block sizes of metal/src/iq.mm:99-131 for the six formats this build takes (Q2_0 64 values /
+// 18 bytes, IQ2_S 256 / 82, IQ4_NL 32 / 18, IQ4_XS 256 / 136, IQ3_XXS 256 / 98, IQ3_S 256 / 110) and the q8_1
+// block (32 values / 36 bytes).
 #include "strata/metal/bytes.hpp"
 #include "strata/metal/device.hpp"
 #include "strata/metal/iq.hpp"
@@ -35,9 +36,15 @@ void* Bytes::handle() const { return nullptr; }
 
 [[noreturn]] static void no_device() { throw MetalError("no Metal device in this build"); }
 
-bool iq_type_supported(int t) noexcept { return t == kQ2_0 || t == kIq2S; }
-int iq_block_values(int t) { return t == kQ2_0 ? 64 : t == kIq2S ? 256 : 0; }
-size_t iq_block_bytes(int t) { return t == kQ2_0 ? 18 : t == kIq2S ? 82 : 0; }
+bool iq_type_supported(int t) noexcept {
+    return t == kQ2_0 || t == kIq2S || t == kIq4Nl || t == kIq4Xs || t == kIq3Xxs || t == kIq3S;
+}
+int iq_block_values(int t) {
+    return t == kQ2_0 ? 64 : t == kIq4Nl ? 32 : (t == kIq2S || t == kIq4Xs || t == kIq3Xxs || t == kIq3S) ? 256 : 0;
+}
+size_t iq_block_bytes(int t) {
+    return t == kQ2_0 ? 18 : t == kIq2S ? 82 : t == kIq4Nl ? 18 : t == kIq4Xs ? 136 : t == kIq3Xxs ? 98 : t == kIq3S ? 110 : 0;
+}
 size_t iq_row_bytes(int t, int64_t n) {
     const int v = iq_block_values(t);
     if (v == 0 || n <= 0 || n % v) throw MetalError("iq_row_bytes: bad type or length");

@@ -31,13 +31,14 @@ smoe_status cuda_fail(cudaError_t e, const char* where) {
     return fail(SMOE_CUDA_ERROR, std::string(where) + ": " + cudaGetErrorString(e));
 }
 
-int block_values(int t) { return t == kQ2_0 ? 64 : t == kIQ2_S ? 256 : 0; }
-size_t block_bytes(int t) { return t == kQ2_0 ? 18 : t == kIQ2_S ? 82 : 0; }
+// Every block format of the reference's MMVQ family: Q2_0, IQ2_S, IQ4_NL, IQ4_XS, IQ3_XXS, IQ3_S (iqx.cu).
+size_t row_bytes(int t, int64_t n) { return gx_row_bytes(t, n); }
 
-size_t row_bytes(int t, int64_t n) {
-    const int v = block_values(t);
-    if (v == 0 || n <= 0 || n % v) return 0;
-    return (size_t) (n / v) * block_bytes(t);
+// Layers with a routed or shared matrix outside Q2_0 / IQ2_S take the any-format path (iqx.cu).
+bool any_format(const smoe_layer* L) {
+    auto fast = [](int t) { return t == kQ2_0 || t == kIQ2_S; };
+    return !fast(L->gu_type) || !fast(L->d_type) ||
+           (L->has_shared && (!fast(L->sg_type) || !fast(L->su_type) || !fast(L->sd_type)));
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -51,6 +52,7 @@ struct Layout {
     size_t chunk;             // per-(64-token chunk, expert) counts of the many-CTA grouping
     size_t bar;               // grid barrier words of the single-token fused kernel
     size_t rsplit;            // fp64 partial sums of the few-token router GEMM
+    size_t hq;                // q8_1 blocks of h per slot (the any-format path)
     size_t total;
 };
 
@@ -123,6 +125,8 @@ Layout layout_of(const smoe_layer* L, int T) {
         o.xh = at; at += up256((size_t) 2 * T * H * 2);
         o.hh = at; at += up256(rows * 2 * F * 2);
     }
+    o.hq = at;
+    if (any_format(L)) at += up256(rows * (F / 32) * kQ8Block);
     o.total = at;
     return o;
 }
@@ -135,7 +139,8 @@ smoe_status check_layer(const smoe_layer* L) {
     if (L->n_expert > kMaxExperts) return fail(SMOE_INVALID_ARG, "layer: n_expert exceeds 1024");
     if (L->k > L->n_expert) return fail(SMOE_INVALID_ARG, "layer: k exceeds n_expert");
     if (!row_bytes(L->gu_type, L->n_embd) || !row_bytes(L->d_type, L->n_ff))
-        return fail(SMOE_UNSUPPORTED, "layer: routed types must be Q2_0 or IQ2_S with whole blocks per row");
+        return fail(SMOE_UNSUPPORTED, "layer: routed types must be Q2_0, IQ2_S, IQ4_NL, IQ4_XS, IQ3_XXS or IQ3_S "
+                                      "with whole blocks per row");
     if (L->n_ff % 32 || L->n_embd % 64) return fail(SMOE_INVALID_ARG, "layer: n_ff % 32 and n_embd % 64 must be 0");
     if (L->n_embd > 4096 || L->n_ff > 4096) return fail(SMOE_UNSUPPORTED, "layer: n_embd and n_ff are at most 4096");
     if (!L->router || !L->gate || !L->up || !L->down) return fail(SMOE_INVALID_ARG, "layer: a routed plane is null");
@@ -143,7 +148,8 @@ smoe_status check_layer(const smoe_layer* L) {
         return fail(SMOE_INVALID_ARG, "layer: planes must be 16-byte aligned");
     if (L->has_shared) {
         if (!row_bytes(L->sg_type, L->n_embd) || !row_bytes(L->su_type, L->n_embd) || !row_bytes(L->sd_type, L->n_ff))
-            return fail(SMOE_UNSUPPORTED, "layer: shared types must be Q2_0 or IQ2_S with whole blocks per row");
+            return fail(SMOE_UNSUPPORTED, "layer: shared types must be Q2_0, IQ2_S, IQ4_NL, IQ4_XS, IQ3_XXS or IQ3_S "
+                                          "with whole blocks per row");
         if (L->sg_type != L->su_type) return fail(SMOE_UNSUPPORTED, "layer: shared gate and up types differ");
         if (!L->sgate || !L->sup || !L->sdown || !L->gate_inp_shexp)
             return fail(SMOE_INVALID_ARG, "layer: a shared plane is null");
@@ -208,6 +214,7 @@ smoe_status check_ep(const smoe_layer* L, const smoe_ep* ep) {
     if (L->n_embd % 128) return fail(SMOE_UNSUPPORTED, "ep: n_embd must be a multiple of 128");
     if (L->has_shared && (L->sg_type != L->gu_type || L->su_type != L->gu_type || L->sd_type != L->d_type))
         return fail(SMOE_UNSUPPORTED, "ep: the shared expert's types must equal the routed ones");
+    if (any_format(L)) return fail(SMOE_UNSUPPORTED, "ep: expert parallelism takes Q2_0 and IQ2_S layers");
     for (int p = 0; p < ep->world; p++)
         if (!ep->areas[p] || !aligned(ep->areas[p], 256)) return fail(SMOE_INVALID_ARG, "ep: an area is null or unaligned");
     return SMOE_OK;
@@ -230,6 +237,7 @@ smoe_status smoe_set_expert_path(int path) {
 
 int smoe_expert_path_for(const smoe_layer* L, int n_tokens) {
     if (check_layer(L) != SMOE_OK || n_tokens <= 0) return -1;
+    if (any_format(L)) return 5;
     return use_decode(L, n_tokens) ? 3 : use_tc(L, n_tokens) ? 2 : use_tq(L, n_tokens) ? 4 : 1;
 }
 
@@ -334,25 +342,19 @@ smoe_status smoe_iq_mmvq(int ggml_type, const uint8_t* w, const uint8_t* x_q8, i
     // iq.mm:150-158
     if (n_in == 0 || n_out == 0 || n_col == 0) return ok();
     if (n_in < 0 || n_out < 0 || n_col < 0) return fail(SMOE_INVALID_ARG, "iq_mmvq: negative size");
-    if (ggml_type == kIQ4_NL || ggml_type == kIQ4_XS) {  // iq4.cu: this entry point only, not the layer path
-        if (n_in % (ggml_type == kIQ4_NL ? 32 : 256))
-            return fail(SMOE_INVALID_ARG, "iq_mmvq: n_in is not a whole number of blocks");
-        if (n_in > 4096) return fail(SMOE_UNSUPPORTED, "iq_mmvq: n_in is at most 4096");
-        if (n_out > 0x7fffffff || n_col > 0x7fffffff) return fail(SMOE_INVALID_ARG, "iq_mmvq: size does not fit in int");
-        if (!stream) return fail(SMOE_INVALID_ARG, "iq_mmvq: a non-null stream is required");
-        if (!w || !x_q8 || !y || !aligned(w, 16) || !aligned(x_q8, 4))
-            return fail(SMOE_INVALID_ARG, "iq_mmvq: w must be 16-byte and x 4-byte aligned");
-        const cudaError_t e = launch_iq4_mmvq(ggml_type, w, x_q8, (int) n_in, (int) n_out, (int) n_col, y,
-                                              (cudaStream_t) stream);
-        return e == cudaSuccess ? ok() : cuda_fail(e, "iq_mmvq");
-    }
-    if (!block_values(ggml_type)) return fail(SMOE_UNSUPPORTED, "iq_mmvq: type is not Q2_0, IQ2_S, IQ4_NL or IQ4_XS");
+    if (!gx_type_ok(ggml_type))
+        return fail(SMOE_UNSUPPORTED, "iq_mmvq: type is not Q2_0, IQ2_S, IQ4_NL, IQ4_XS, IQ3_XXS or IQ3_S");
     if (!row_bytes(ggml_type, n_in)) return fail(SMOE_INVALID_ARG, "iq_mmvq: n_in is not a whole number of blocks");
     if (n_in > 4096) return fail(SMOE_UNSUPPORTED, "iq_mmvq: n_in is at most 4096");
     if (n_out > 0x7fffffff || n_col > 0x7fffffff) return fail(SMOE_INVALID_ARG, "iq_mmvq: size does not fit in int");
     if (!stream) return fail(SMOE_INVALID_ARG, "iq_mmvq: a non-null stream is required");
     if (!w || !x_q8 || !y || !aligned(w, 16) || !aligned(x_q8, 4))
         return fail(SMOE_INVALID_ARG, "iq_mmvq: w must be 16-byte and x 4-byte aligned");
+    if (ggml_type != kQ2_0 && ggml_type != kIQ2_S) {  // iqx.cu
+        const cudaError_t e = launch_gx_mmvq(ggml_type, w, x_q8, (int) n_in, (int) n_out, (int) n_col, y,
+                                             (cudaStream_t) stream);
+        return e == cudaSuccess ? ok() : cuda_fail(e, "iq_mmvq");
+    }
     GroupView g{};
     g.single_cols = (int) n_col;
     const Matrix m{w, 0, ggml_type};
@@ -502,6 +504,36 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
                                      E, s, base + lo.rsplit);
     if (e == cudaSuccess) e = mark(0, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: router");
+    if (any_format(L)) {
+        // any block format (iqx.cu): the q8_1 blocks of x, grouping, gate/up rows, SwiGLU + q8_1 of h, down rows;
+        // the shared expert in launches of its own (its types may differ from the routed ones)
+        e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, nullptr, 0);
+        if (e == cudaSuccess) e = mark(1, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: top-k");
+        e = launch_group(ids, T, K, E, tabs, slot, slot_tok, s, &sc, reinterpret_cast<int32_t*>(base + lo.chunk));
+        if (e == cudaSuccess) e = mark(2, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: dispatch");
+        Work wk{};
+        wk.sched = sc;
+        wk.slot_token = slot_tok;
+        wk.max_entries = sched_capacity(E, T, K);
+        wk.shared_base = T * K;
+        wk.shared_slots = sh ? T : 0;
+        const int64_t gu_stride = (int64_t) F * (int64_t) row_bytes(L->gu_type, H);
+        const int64_t d_stride = (int64_t) H * (int64_t) row_bytes(L->d_type, F);
+        uint8_t* hq = base + lo.hq;
+        e = launch_gx_gate_up(Matrix{L->gate, gu_stride, L->gu_type}, Matrix{L->up, gu_stride, L->gu_type}, wk, 0, xq,
+                              gu, H, F, s);
+        if (e == cudaSuccess && sh)
+            e = launch_gx_gate_up(Matrix{L->sgate, 0, L->sg_type}, Matrix{L->sup, 0, L->su_type}, wk, 1, xq, gu, H, F, s);
+        if (e == cudaSuccess) e = launch_gx_swiglu(gu, hq, rows, F, s);
+        if (e == cudaSuccess) e = mark(3, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: gate/up (any format)");
+        e = launch_gx_down(Matrix{L->down, d_stride, L->d_type}, wk, 0, hq, parts, F, H, s);
+        if (e == cudaSuccess && sh) e = launch_gx_down(Matrix{L->sdown, 0, L->sd_type}, wk, 1, hq, parts, F, H, s);
+        if (e == cudaSuccess) e = mark(4, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: down (any format)");
+    } else {
     const bool tc = use_tc(L, T);
     // the q8_1 image of x in the reference's block format is only an output of the trace: the expert kernels
     // read their own layouts (xa for the SIMT kernels, xh for the tensor-core kernels)
@@ -596,6 +628,7 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     }
     e = mark(4, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: stage event");
+    }
     }
     e = launch_combine(parts, slot, w, sh ? parts + (int64_t) T * K * H : nullptr, sh ? sh_logit : nullptr, out,
                        trace ? trace->shared : nullptr, H, K, T, H, s);

@@ -17,8 +17,10 @@ namespace smoe {
 
 constexpr int kQ2_0 = 42;
 constexpr int kIQ2_S = 22;
-constexpr int kIQ4_NL = 20;  // stage entry point smoe_iq_mmvq only
-constexpr int kIQ4_XS = 23;  // stage entry point smoe_iq_mmvq only
+constexpr int kIQ4_NL = 20;   // these four: the any-format layer path and the stage entry point (iqx.cu)
+constexpr int kIQ4_XS = 23;
+constexpr int kIQ3_XXS = 18;
+constexpr int kIQ3_S = 21;
 constexpr int kQ8Block = 36;
 
 // Status word shared by all kernels of this library (one per device).  A kernel that gives up on a

@@ -107,9 +107,11 @@ struct Matrix {
 };
 
 // y[slot][r] = down_e[r] . act[slot] for every slot, y row stride y_stride floats; act rows n_in / 32 blocks.
-// ---- iq4.cu ---- (IQ4_NL / IQ4_XS rows against q8_1 columns, the reference's row_dot order)
-cudaError_t launch_iq4_mmvq(int type, const uint8_t* w, const uint8_t* x, int n_in, int n_out, int n_col,
-                            float* y, cudaStream_t s);
+// ---- iqx.cu ---- (every block format against q8_1 columns, the reference's row_dot order)
+bool gx_type_ok(int type);
+size_t gx_row_bytes(int type, int64_t n);
+cudaError_t launch_gx_mmvq(int type, const uint8_t* w, const uint8_t* x, int n_in, int n_out, int n_col,
+                           float* y, cudaStream_t s);
 cudaError_t launch_expert_down(Matrix down, Matrix sdown, GroupView g, const uint8_t* act, int act_by_token,
                                float* y, int64_t y_stride, int n_in, int n_out, cudaStream_t s);
 
@@ -149,6 +151,15 @@ cudaError_t launch_layer_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix su
 cudaError_t launch_swiglu_ka(const float* gu, KAct ha, int64_t rows, int n_ff, int down_q2, cudaStream_t s);
 cudaError_t launch_layer_down(Matrix down, Matrix sdown, Work w, KAct ha, float* y, int n_ff, int n_embd,
                               cudaStream_t s);
+
+// The any-format layer path (iqx.cu): gate/up rows into gu[slot][gate n_ff | up n_ff], SwiGLU + q8_1 of h into
+// hq[slot][n_ff / 32] (q8_1 blocks), down rows into y[slot][n_embd]; xq holds the q8_1 blocks of every token.
+// shared_only 1 runs the shared expert's slots with the given (shared) matrices, 0 the routed work list.
+cudaError_t launch_gx_gate_up(Matrix gate, Matrix up, Work w, int shared_only, const uint8_t* xq, float* gu,
+                              int n_embd, int n_ff, cudaStream_t s);
+cudaError_t launch_gx_swiglu(const float* gu, uint8_t* h, int64_t rows, int n_ff, cudaStream_t s);
+cudaError_t launch_gx_down(Matrix down, Work w, int shared_only, const uint8_t* hq, float* y, int n_ff, int n_embd,
+                           cudaStream_t s);
 
 // ---- tc.cu ---- (Q2_0 weights; n_embd and n_ff multiples of 512; work list built with chunk kTcChunk)
 // xh: hi/lo fp16 image of the q8_1 activation, rows [0, T) hi and [T, 2T) lo.

@@ -6,7 +6,7 @@
 #include "combine.cu"
 #include "tc.cu"
 #include "tq.cu"
-#include "iq4.cu"
+#include "iqx.cu"
 #include "elementwise.cu"
 #include "decode.cu"
 #include "ep.cu"

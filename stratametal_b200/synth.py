@@ -24,7 +24,13 @@ import torch
 
 Q2_0 = 42
 IQ2_S = 22
+IQ4_NL = 20
+IQ4_XS = 23
+IQ3_XXS = 18
+IQ3_S = 21
 M32 = 0xFFFFFFFF
+# (values, bytes) per block of each format
+BLOCKS = {Q2_0: (64, 18), IQ2_S: (256, 82), IQ4_NL: (32, 18), IQ4_XS: (256, 136), IQ3_XXS: (256, 98), IQ3_S: (256, 110)}
 
 # tensor ids inside a layer's key
 T_ROUTER, T_GINP, T_GATE, T_UP, T_DOWN, T_SGATE, T_SUP, T_SDOWN, T_X = range(1, 10)
@@ -90,13 +96,11 @@ def fp16_bytes(v: torch.Tensor) -> torch.Tensor:
 
 
 def row_bytes(t: int, n: int) -> int:
-    if t == Q2_0:
-        assert n % 64 == 0
-        return n // 64 * 18
-    if t == IQ2_S:
-        assert n % 256 == 0
-        return n // 256 * 82
-    raise ValueError(f"type {t}")
+    if t not in BLOCKS:
+        raise ValueError(f"type {t}")
+    v, b = BLOCKS[t]
+    assert n % v == 0
+    return n // v * b
 
 
 def quant_matrix(t: int, key: int, rows: int, n_in: int, device, d_sigma: float = 0.05) -> torch.Tensor:
@@ -106,10 +110,16 @@ def quant_matrix(t: int, key: int, rows: int, n_in: int, device, d_sigma: float 
         d = fp16_bytes(normal(_mix_py(key, 1), nb, device).abs() * d_sigma)
         qs = random_bytes(_mix_py(key, 2), nb * 16, device).view(nb, 16)
         return torch.cat([d, qs], dim=1).reshape(-1)
-    if t == IQ2_S:
-        nb = rows * (n_in // 256)
+    if t in BLOCKS:
+        # every other format: fp16 d then uniform bytes (every byte pattern is a valid block: grid indices, signs
+        # and sub-scales span their whole fields).  IQ2_S: qs[32] signs[32] qh[8] scales[8]; IQ4_NL: qs[16];
+        # IQ4_XS: scales_h, scales_l[4], qs[128]; IQ3_XXS: qs[64], sign/scale words[8]; IQ3_S: qs[64] qh[8]
+        # signs[32] scales[4]
+        v, b = BLOCKS[t]
+        nb = rows * (n_in // v)
         d = fp16_bytes(normal(_mix_py(key, 1), nb, device).abs() * d_sigma)
-        rest = random_bytes(_mix_py(key, 2), nb * 80, device).view(nb, 80)  # qs[32] signs[32] qh[8] scales[8]
+        nr = (b - 2 + 3) // 4 * 4
+        rest = random_bytes(_mix_py(key, 2), nb * nr, device).view(nb, nr)[:, :b - 2]
         return torch.cat([d, rest], dim=1).reshape(-1)
     raise ValueError(f"type {t}")
 

@@ -149,6 +149,22 @@ def main():
         g[f"dot_{name}_w"] = w
         g[f"dot_{name}_x"] = xq
         g[f"dot_{name}_y"] = ref_rows(t, w, xq, n_in, n_out)
+    # the reference's expert pairs of other formats (iq_parity.cpp:504-539), with the f32 tokens kept so the whole
+    # block can be driven through them: 2 tokens, the second -0.5 x + 0.25; their own generator as above
+    rp = np.random.default_rng(504)
+    for name, gt, dt, H, F in (("iq2s_iq4nl", O.IQ2_S, O.IQ4_NL, 256, 64), ("iq3xxs_q2", O.IQ3_XXS, O.Q2_0, 256, 64),
+                               ("iq3s_iq4nl", O.IQ3_S, O.IQ4_NL, 256, 64), ("iq4xs_q2", O.IQ4_XS, O.Q2_0, 256, 64),
+                               ("iq3s_iq4nl_wide", O.IQ3_S, O.IQ4_NL, 1280, 128)):
+        blob = np.concatenate([rand_rows(rp, gt, 2 * F, H), rand_rows(rp, dt, H, F)])
+        xx = rp.standard_normal((2, H)).astype(np.float32)
+        xx[1] = -0.5 * xx[0] + 0.25
+        xq = ref_q8(xx.ravel())
+        y = np.empty(2 * H, np.float32)
+        R.ref_expert_q8(gt, dt, H, F, P(blob, u8p), blob.size, P(xq, u8p), 2, P(y, f32p))
+        g[f"pair_{name}_blob"] = blob
+        g[f"pair_{name}_x"] = xx
+        g[f"pair_{name}_y"] = y
+        g[f"pair_{name}_geom"] = np.array([gt, dt, H, F], np.int32)
     out = Path(__file__).with_name("golden.npz")
     np.savez_compressed(out, **g)
     print(f"wrote {out} ({out.stat().st_size} bytes, {len(g)} arrays)")

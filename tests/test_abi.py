@@ -91,6 +91,14 @@ def test_layer_check(L):
     assert L.smoe_layer_check(C.byref(layer_struct(gu_type=14))) == 2
     assert L.smoe_layer_check(C.byref(layer_struct(gate=258))) == 1            # misaligned plane
     assert L.smoe_layer_check(C.byref(layer_struct(gu_type=22))) == 0
+    # the other formats of the reference's expert packs take the any-format path (5)
+    for gu, d in ((21, 20), (18, 42), (23, 42), (22, 20)):
+        assert L.smoe_layer_check(C.byref(layer_struct(gu_type=gu, d_type=d))) == 0
+        assert L.smoe_expert_path_for(C.byref(layer_struct(gu_type=gu, d_type=d)), 8) == 5
+    assert L.smoe_expert_path_for(C.byref(layer_struct()), 64) in (1, 4)
+    assert L.smoe_row_bytes(18, 512) == 196 and L.smoe_row_bytes(21, 256) == 110 and L.smoe_row_bytes(20, 64) == 36
+    assert L.smoe_layer_check(C.byref(layer_struct(gu_type=20, n_embd=2112))) == 0   # IQ4_NL: 32-value blocks
+    assert L.smoe_layer_check(C.byref(layer_struct(gu_type=21, n_embd=2112))) == 2   # IQ3_S: not whole blocks
     assert L.smoe_moe_scratch_bytes(C.byref(layer_struct()), 64) > 64 * 11 * 2048 * 4
     # zero tokens: OK before any launch
     assert L.smoe_moe_forward(C.byref(layer_struct()), None, 0, None, None, 0, None, None) == 0

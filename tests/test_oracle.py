@@ -233,3 +233,23 @@ def test_iq4_fields_are_observable(golden):
             for o in range(0, hz.size, bs):
                 hz[o + 2] = hz[o + 3] = 0
             assert O.rel_l1(want, O.mmvq(t, hz, xq, n_in, want.size, 1)[0]) > 0.05
+
+
+PAIRS = ["iq2s_iq4nl", "iq3xxs_q2", "iq3s_iq4nl", "iq4xs_q2", "iq3s_iq4nl_wide"]
+
+
+def pair_layer(golden, name):
+    """The reference's expert pair as a one-expert, top-1 layer without a shared expert: the router must pick
+    expert 0 with weight 1, so the block's output is the expert's output (golden pair_*, iq_parity.cpp:504-539)."""
+    gt, dt, H, F = (int(v) for v in golden[f"pair_{name}_geom"])
+    blob = golden[f"pair_{name}_blob"]
+    ngu = F * O.row_bytes(gt, H)
+    router = np.full(H, 0x3C00, np.uint16)  # any bf16 row
+    return O.HostLayer(H, F, 1, 1, gt, dt, router, blob[:ngu], blob[ngu:2 * ngu], blob[2 * ngu:], None)
+
+
+@pytest.mark.parametrize("name", PAIRS)
+def test_expert_pairs_through_the_layer(golden, name):
+    # the oracle's block over the other formats reproduces the reference's ref_expert bit for bit
+    got = O.moe_layer(pair_layer(golden, name), golden[f"pair_{name}_x"])
+    assert np.array_equal(got.ravel().view(np.uint32), golden[f"pair_{name}_y"].view(np.uint32))
