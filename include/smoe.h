@@ -202,6 +202,109 @@ size_t smoe_moe_scratch_bytes(const smoe_layer* L, int max_tokens);
 smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, float* out, void* scratch,
                              size_t scratch_bytes, const smoe_trace* trace, void* stream);
 
+/* ---- the Strata pack's planar S2 experts and the grouped decode API over them ---------------------------------
+ * Blob layout (include/strata/kernels/cpu/expert.hpp:34-51, with n_embd = H and n_ff = F parameters instead of the
+ * artifact's fixed 2560 / 640): the 2F gate/up code rows interleaved (row 2r = gate r, 2r + 1 = up r), H / 4 bytes
+ * each; the H down code rows, F / 4 bytes each; the fp16 scales of the gate/up rows (H / 64 per row) and of the
+ * down rows (F / 64 per row).  Two-bit codes, four per byte, first value in the low bits; a weight is
+ * (code - 1) * d of its 64-value block (s2_expert_grouped.hpp:68-71).  Every row is the reference's row_dot order
+ * over 32-value partials (iq_parity.cpp:275-292), so a blob computes exactly what the GGUF Q2_0 rows it was packed
+ * from compute on the same activation bytes.  Activations are ggml Q8_0 blocks (34 B: fp16 d, 32 int8); with
+ * x_scales (n_embd / 32 fp32 per token) those scales replace d for the gate/up dots and the intermediate is
+ * quantized with fp32 scales too (s2_expert_grouped.hpp:59-66).  Blobs and slots are 16-byte aligned. */
+
+/* BLOB (expert.hpp:45) for this geometry; 0 unless n_embd and n_ff are positive multiples of 64. */
+size_t smoe_s2_blob_bytes(int n_embd, int n_ff);
+/* One expert's GGUF Q2_0 rows (gate and up: n_ff rows over n_embd; down: n_embd rows over n_ff) -> its S2 blob
+ * (the pack's re-layout of the same codes and scales). */
+smoe_status smoe_s2_pack_expert(const uint8_t* gate, const uint8_t* up, const uint8_t* down, int n_embd, int n_ff,
+                                uint8_t* blob, void* stream);
+/* quantize_q8_0 (include/strata/kernels/quantize_act.hpp:20-22; host rule metal/src/sgemv.mm:145-172): d32 =
+ * amax / 127 stored as fp16, q = rint(x / d32) in double, clamped to [-128, 127]; zero blocks are 34 zero bytes.
+ * With scales non-NULL, quantize_q8_0_scaled (quantize_act.hpp:24-30): the same blocks' d, scales[b] = d32 and q
+ * rounded half away from zero in float (the CPU contract), clamped to [-127, 127].  n % 32 == 0. */
+smoe_status smoe_quantize_q8_0(const float* x, uint8_t* blocks, float* scales, int64_t n, void* stream);
+/* moe_hit_grouped_scratch_bytes (s2_expert_grouped.hpp:30-35): caller-owned scratch of the grouped / hit calls for
+ * up to cap_entries entries (or hits). */
+size_t smoe_moe_grouped_scratch_bytes(int64_t cap_entries, int64_t n_embd, int64_t n_ff);
+/* moe_grouped_s2 (s2_expert_grouped.hpp:96-102): group g's blob at device address grp_ptr[g], its entries
+ * [grp_start[g], grp_start[g + 1]); entry i reads activation row ent_tok[i] of x_q8_0 (and x_scales) and writes the
+ * n_embd floats of out row ent_dst[i].  n_groups[0] (device) is the group count, at most cap_groups; every row of a
+ * blob is read once for all of its entries.  Counts past their capacities are clamped and record status 2. */
+smoe_status smoe_moe_grouped_s2(const unsigned long long* grp_ptr, const int32_t* grp_start, const int32_t* n_groups,
+                                const int32_t* ent_dst, const int32_t* ent_tok, int64_t cap_groups, int64_t cap_entries,
+                                int n_embd, int n_ff, const uint8_t* x_q8_0, const float* x_scales, void* scratch,
+                                float* out, void* stream);
+/* moe_group_resident (s2_expert_grouped.hpp:103-107): the groups of moe_grouped_s2 when every expert is resident at
+ * base + id * blob_bytes: groups are the distinct ids of ids[n] in ascending order, a group's entries its routing
+ * indices in order (dst = index, tok = index / k_per_tok); counts[0] = groups, counts[1] = entries.  n <= 1024;
+ * negative ids are skipped.  grp_start holds n + 1 ints. */
+smoe_status smoe_moe_group_resident(const int32_t* ids, int n, int k_per_tok, const uint8_t* base, int64_t blob_bytes,
+                                    unsigned long long* grp_ptr, int32_t* grp_start, int32_t* counts, int32_t* ent_dst,
+                                    int32_t* ent_tok, void* stream);
+/* moe_hit_select / moe_hit_select_multi (s2_expert_grouped.hpp:80-86, 108-109): the routing entries of ids[n]
+ * whose expert is resident (res_row[e] = slot, or -1), in routing order: slot[c], dst[c] = the entry's index, and
+ * count[0] = the hits.  n <= 1024. */
+smoe_status smoe_moe_hit_select(const int32_t* ids, const int32_t* res_row, int n, int n_expert, int32_t* slot,
+                                int32_t* dst, int32_t* count, void* stream);
+/* moe_hit_grouped_s2_dev / _multi (s2_expert_grouped.hpp:86-89, 110-112): hit h < d_count[0] (at most cap) is the
+ * blob at blob_base + slot_index[h] * blob_bytes and writes out row dst_index[h]; it reads activation row
+ * dst_index[h] / k_per_token, or row 0 for every hit when k_per_token is 0 (one token). */
+smoe_status smoe_moe_hit_grouped_s2(const uint8_t* blob_base, const int32_t* slot_index, const int32_t* dst_index,
+                                    const int32_t* d_count, int64_t cap, int64_t blob_bytes, int n_embd, int n_ff,
+                                    const uint8_t* x_q8_0, const float* x_scales, int k_per_token, void* scratch,
+                                    float* out, void* stream);
+/* moe_hit_add (s2_expert_grouped.hpp:90-91): parts[dst[h]] += hit_out[dst[h]] (n_embd floats) for h < count[0]. */
+smoe_status smoe_moe_hit_add(float* parts, const float* hit_out, const int32_t* dst, const int32_t* count, int64_t cap,
+                             int64_t n_embd, void* stream);
+
+/* ---- streaming routed experts from the pack on disk into HBM (include/smoe_stream.hpp holds the C++ classes) ----
+ * The pack's expert file (metal/src/pack.cpp:367-416): pack_dir/native_experts.txt, header "# strata native
+ * experts vN ... (n_expert E)" (N <= 4) and one line per layer "layer gu_type d_type offset blob_bytes", over
+ * pack_dir/experts.bin (layers back to back, a layer's experts back to back); experts.bin is mapped read-only.
+ * Set-up, not the token path. */
+smoe_status smoe_native_experts_open(const char* pack_dir, void** handle);
+void smoe_native_experts_close(void* handle);
+/* pick_native_expert (pack.cpp:368-416): the formats, file offset and size of (layer, expert)'s blob, and a host
+ * pointer to its bytes inside the mapping (any output may be NULL). */
+smoe_status smoe_native_experts_pick(const void* handle, int64_t layer, int64_t expert, int* gu_type, int* d_type,
+                                     uint64_t* file_off, uint64_t* blob_bytes, const uint8_t** host_blob);
+/* The VRAM expert tier (include/strata/core/expert_cache.hpp:72-150): n_slots x blob_bytes of device memory,
+ * checked against the free memory and allocated here, once (set-up); a (layer, expert) -> slot table on the host
+ * and on the device; a slot is claimed once and never evicted; with per_layer != 0 layer l only takes slots
+ * [l q, (l + 1) q), q = n_slots / n_layers (the last layer the remainder).  blob_bytes % 16 == 0. */
+smoe_status smoe_expert_cache_open(int64_t n_slots, int64_t n_layers, int64_t n_expert, int64_t blob_bytes,
+                                   int per_layer, void** handle);
+void smoe_expert_cache_close(void* handle);
+/* admit + fill_slot (expert_cache.hpp:133-137, 168-171): *slot = the expert's slot; a new one is filled from host
+ * memory (copied through pinned staging, so the source may be reused at once) and published in the device table,
+ * both on `stream`.  *slot = -1 when the cache is full (nothing queued). */
+smoe_status smoe_expert_cache_ensure(void* handle, int64_t layer, int64_t expert, const uint8_t* host_blob,
+                                     int64_t bytes, void* stream, int32_t* slot);
+/* slot_of (expert_cache.hpp:130-131): the slot, or -1 (also for a layer or expert out of range). */
+int32_t smoe_expert_cache_slot_of(const void* handle, int64_t layer, int64_t expert);
+/* The slot arena's device base (slot s at base + s * blob_bytes) and one layer's device residency row
+ * (int32 [n_expert]: slot or -1), the res_row smoe_moe_hit_select reads; NULL for a bad handle or layer. */
+uint8_t* smoe_expert_cache_arena(const void* handle);
+const int32_t* smoe_expert_cache_row(const void* handle, int64_t layer);
+
+/* ---- the model boundary: a MoE layer read from a GGUF file by tensor name (include/smoe_gguf.hpp) ------------
+ * FfnExec::load (metal/src/layer_exec.cpp:369-452, expert_spans :109-123) over the reference's tensor names
+ * blk.<L>.ffn_gate_inp / ffn_{gate,up,down}_exps / ffn_{gate,up,down}_shexp / ffn_gate_inp_shexp .weight
+ * (metal/include/strata/metal/layer_tensors.hpp:48).  GGUF v2 / v3, mapped read-only; set-up, not the token path. */
+smoe_status smoe_gguf_open(const char* path, void** handle);
+void smoe_gguf_close(void* handle);
+/* A tensor by its full name: ggml type, shape ne[0..3] (ne[0] fastest), bytes and a host pointer into the mapping
+ * (any output may be NULL). */
+smoe_status smoe_gguf_tensor(const void* handle, const char* name, int* type, int64_t* ne4, uint64_t* bytes,
+                             const uint8_t** data);
+/* Uploads layer `layer`'s MoE planes (allocates device memory: set-up) and fills *out with them: geometry from the
+ * shapes (gate ne = {n_embd, n_ff, n_expert}), k from <general.architecture>.expert_used_count unless k > 0, the
+ * router as bf16 (an F32 router is rounded to nearest even).  Each expert plane must hold exactly n_expert experts
+ * of whole rows.  *owner keeps the device memory until smoe_gguf_free_layer(*owner). */
+smoe_status smoe_gguf_load_layer(const void* handle, int layer, int with_shared, int k, smoe_layer* out, void** owner);
+void smoe_gguf_free_layer(void* owner);
+
 /* ---- Expert parallelism over the GPUs of one node (no reference counterpart: the reference reaches a second
  * GPU only through its peer / remote expert tiers, include/strata/core/peer_experts.hpp:35-104, which this
  * replaces for the MoE block).  Rank r of `world` holds the router and the shared expert whole and the routed

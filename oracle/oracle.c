@@ -679,3 +679,124 @@ void orc_add_rms_norm(const float* x, const float* residual, const float* w, int
         }
     }
 }
+
+/* ---- the Strata pack's planar S2 experts (include/strata/kernels/cpu/expert.hpp:34-51) -------------------------
+ * One expert of geometry (H, F) in one blob: the 2F gate/up code rows interleaved (row 2r gate r, 2r + 1 up r),
+ * H / 4 bytes each; then the H down code rows, F / 4 bytes each; then the fp16 scales of the gate/up rows (H / 64
+ * per row, same row order) and of the down rows (F / 64 per row).  Codes are 2 bits, four per byte, first value in
+ * the low bits (the GGUF Q2_0 qs order, dequant.hpp:69-78); a weight is (code - 1) * d of its 64-value block.  The
+ * pack is therefore a lossless re-layout of the GGUF Q2_0 planes, and orc_s2_pack performs it. */
+size_t orc_s2_blob_bytes(int H, int F) { return (size_t) 3 * H * F / 64 * 18; }
+
+static void s2_offsets(int H, int F, size_t* gu_codes, size_t* d_codes, size_t* gu_scales, size_t* d_scales) {
+    *gu_codes = 0;
+    *d_codes = (size_t) 2 * F * (H / 4);
+    *gu_scales = *d_codes + (size_t) H * (F / 4);
+    *d_scales = *gu_scales + (size_t) 2 * F * (H / 64) * 2;
+}
+
+/* One GGUF Q2_0 row of n values -> its codes (n / 4 bytes) and scales (n / 64 fp16) in the planar form. */
+static void s2_put_row(const uint8_t* row, int n, uint8_t* codes, uint8_t* scales) {
+    for (int b = 0; b < n / 64; b++) {
+        memcpy(scales + 2 * b, row + (size_t) b * 18, 2);
+        memcpy(codes + 16 * b, row + (size_t) b * 18 + 2, 16);
+    }
+}
+
+void orc_s2_pack(const uint8_t* gate, const uint8_t* up, const uint8_t* down, int H, int F, uint8_t* blob) {
+    size_t oc, od, os, ods;
+    s2_offsets(H, F, &oc, &od, &os, &ods);
+    const size_t rgu = orc_row_bytes(ORC_Q2_0, H), rd = orc_row_bytes(ORC_Q2_0, F);
+    for (int r = 0; r < F; r++) {
+        s2_put_row(gate + (size_t) r * rgu, H, blob + oc + (size_t) (2 * r) * (H / 4),
+                   blob + os + (size_t) (2 * r) * (H / 64) * 2);
+        s2_put_row(up + (size_t) r * rgu, H, blob + oc + (size_t) (2 * r + 1) * (H / 4),
+                   blob + os + (size_t) (2 * r + 1) * (H / 64) * 2);
+    }
+    for (int j = 0; j < H; j++)
+        s2_put_row(down + (size_t) j * rd, F, blob + od + (size_t) j * (F / 4), blob + ods + (size_t) j * (F / 64) * 2);
+}
+
+/* quantize_q8_0 (metal/src/sgemv.mm:145-172, the GPU contract of include/strata/kernels/quantize_act.hpp:20-22):
+ * per 32 values amax, d32 = amax / 127 in float, stored as fp16; q = rint((double) x / (double) d32) clamped to
+ * [-128, 127]; an all-zero block is 34 zero bytes.  With `scales` (quantize_q8_0_scaled, quantize_act.hpp:24-30:
+ * the same blocks plus the CPU's fp32 scale and its rounding rule): scales[b] = d32 and q is rounded half away
+ * from zero (the CPU activation contract, expert.hpp:53-58), clamped to [-127, 127]. */
+void orc_quant_q8_0(const float* x, int64_t n, uint8_t* blocks, float* scales) {
+    for (int64_t b = 0; b < n / 32; b++) {
+        const float* xb = x + b * 32;
+        uint8_t* o = blocks + b * 34;
+        float amax = 0.0f;
+        for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(xb[i]));
+        if (scales) scales[b] = amax / 127.0f;
+        if (amax == 0.0f) {
+            memset(o, 0, 34);
+            continue;
+        }
+        const float d32 = amax / 127.0f;
+        const uint16_t d16 = orc_f16_from_f32(d32);
+        o[0] = (uint8_t) d16;
+        o[1] = (uint8_t) (d16 >> 8);
+        for (int i = 0; i < 32; i++) {
+            double q;
+            if (scales) {
+                q = roundf(xb[i] / d32);
+                if (q > 127.0) q = 127.0;
+                if (q < -127.0) q = -127.0;
+            } else {
+                q = rint((double) xb[i] / (double) d32);
+                if (q > 127.0) q = 127.0;
+                if (q < -128.0) q = -128.0;
+            }
+            o[2 + i] = (uint8_t) (int8_t) q;
+        }
+    }
+}
+
+/* One planar Q2_0 row (codes, fp16 scales) of n values against Q8_0 blocks: the reference's row_dot order
+ * (iq_parity.cpp:275-292) over 32-value partials (d_w * d_x) * sum (code - 1) q, d_x the block's fp16 d or, with
+ * x_scales, the fp32 scale. */
+static float s2_row_dot(const uint8_t* codes, const uint8_t* sc, int n, const uint8_t* xq, const float* xs) {
+    float lane[32], nxt[32];
+    memset(lane, 0, sizeof lane);
+    for (int k = 0; k < n / 32; k++) {
+        int32_t sumi = 0;
+        const uint8_t* xb = xq + (size_t) k * 34;
+        for (int i = 0; i < 32; i++) {
+            const int code = (codes[8 * k + i / 4] >> (2 * (i % 4))) & 3;
+            sumi += (code - 1) * (int32_t) (int8_t) xb[2 + i];
+        }
+        const float dx = xs ? xs[k] : orc_f32_from_f16(rd16(xb));
+        const float d = orc_f32_from_f16(rd16(sc + 2 * (k / 2))) * dx;
+        lane[k & 31] += d * (float) sumi;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        for (int l = 0; l < 32; l++) nxt[l] = lane[l] + lane[l ^ o];
+        memcpy(lane, nxt, sizeof lane);
+    }
+    return lane[0];
+}
+
+/* One S2 expert for one token (the chain of include/strata/kernels/s2_expert_grouped.hpp:11-16): gate and up rows
+ * against x (Q8_0 blocks, optional fp32 scales), h = silu(g) * u, h quantized in the same contract as x (fp16 d
+ * without scales, fp32 scales with them), down rows -> out[H]. */
+void orc_s2_expert(const uint8_t* blob, int H, int F, const uint8_t* xq, const float* xs, float* out) {
+    size_t oc, od, os, ods;
+    s2_offsets(H, F, &oc, &od, &os, &ods);
+    float* h = (float*) malloc(sizeof(float) * (size_t) F);
+    uint8_t* hq = (uint8_t*) malloc((size_t) F / 32 * 34);
+    float* hs = xs ? (float*) malloc(sizeof(float) * (size_t) F / 32) : NULL;
+    for (int r = 0; r < F; r++) {
+        const float g = s2_row_dot(blob + oc + (size_t) (2 * r) * (H / 4), blob + os + (size_t) (2 * r) * (H / 64) * 2,
+                                   H, xq, xs);
+        const float u = s2_row_dot(blob + oc + (size_t) (2 * r + 1) * (H / 4),
+                                   blob + os + (size_t) (2 * r + 1) * (H / 64) * 2, H, xq, xs);
+        h[r] = silu_mul(g, u);
+    }
+    orc_quant_q8_0(h, F, hq, hs);
+    for (int j = 0; j < H; j++)
+        out[j] = s2_row_dot(blob + od + (size_t) j * (F / 4), blob + ods + (size_t) j * (F / 64) * 2, F, hq, hs);
+    free(h);
+    free(hq);
+    free(hs);
+}

@@ -103,6 +103,14 @@ void orc_add_rms_norm(const float* x, const float* residual, const float* w, int
                       float* out);
 
 /* Trap variants for the tests (variant 1: Q2_0 codes without the -1, iq_parity.cpp:225-248 minus_one=false). */
+/* The Strata pack's planar S2 experts (expert.hpp:34-51): blob size, GGUF Q2_0 -> S2 re-layout of one expert,
+ * the Q8_0 activation rule (sgemv.mm:145-172; with `scales`, the fp32-scale variant of quantize_act.hpp:24-30) and
+ * one expert for one token over Q8_0 activations. */
+size_t orc_s2_blob_bytes(int H, int F);
+void orc_s2_pack(const uint8_t* gate, const uint8_t* up, const uint8_t* down, int H, int F, uint8_t* blob);
+void orc_quant_q8_0(const float* x, int64_t n, uint8_t* blocks, float* scales);
+void orc_s2_expert(const uint8_t* blob, int H, int F, const uint8_t* xq, const float* xs, float* out);
+
 float orc_row_dot_variant(int type, const uint8_t* row, const uint8_t* col_q8, int n_in, int variant);
 
 #ifdef __cplusplus

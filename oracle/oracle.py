@@ -89,6 +89,11 @@ def lib() -> C.CDLL:
         L.orc_route.argtypes = [_f32p, C.c_int, C.c_int, _i32p, _f32p]
         L.orc_router.argtypes = [_f32p, C.c_int, _u16p, C.c_int, C.c_int, C.c_int, _f32p, _i32p, _f32p]
         L.orc_router.restype = None
+        L.orc_s2_blob_bytes.restype = C.c_size_t
+        L.orc_s2_blob_bytes.argtypes = [C.c_int, C.c_int]
+        L.orc_s2_pack.argtypes = [_u8p, _u8p, _u8p, C.c_int, C.c_int, _u8p]
+        L.orc_quant_q8_0.argtypes = [_f32p, C.c_int64, _u8p, _f32p]
+        L.orc_s2_expert.argtypes = [_u8p, C.c_int, C.c_int, _u8p, _f32p, _f32p]
         L.orc_combine.argtypes = [_f32p, _f32p, _f32p, _f32p, C.c_int, C.c_int]
         L.orc_dequant_row.argtypes = [C.c_int, _u8p, C.c_int, _f32p]
         L.orc_add_rms_norm.argtypes = [_f32p, _f32p, _f32p, C.c_int64, C.c_int64, C.c_float, _f32p]
@@ -181,6 +186,37 @@ def router(router_bf16: np.ndarray, x: np.ndarray, k: int) -> tuple[np.ndarray, 
     lib().orc_router(_ptr(x, _f32p), T, _ptr(r, _u16p), E, H, k, _ptr(logits, _f32p), _ptr(ids, _i32p),
                      _ptr(w, _f32p))
     return logits, ids, w
+
+
+def s2_blob_bytes(H: int, F: int) -> int:
+    return int(lib().orc_s2_blob_bytes(H, F))
+
+
+def s2_pack(gate: np.ndarray, up: np.ndarray, down: np.ndarray, H: int, F: int) -> np.ndarray:
+    """One expert's GGUF Q2_0 gate / up / down rows -> the pack's planar S2 blob."""
+    g, u, d = (np.ascontiguousarray(a, np.uint8) for a in (gate, up, down))
+    blob = np.empty(s2_blob_bytes(H, F), np.uint8)
+    lib().orc_s2_pack(_ptr(g, _u8p), _ptr(u, _u8p), _ptr(d, _u8p), H, F, _ptr(blob, _u8p))
+    return blob
+
+
+def quant_q8_0(x: np.ndarray, scaled: bool = False):
+    """Q8_0 blocks of x (34 B per 32 values); with scaled=True also the fp32 scales (the CPU contract)."""
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    y = np.empty(x.size // 32 * 34, np.uint8)
+    sc = np.empty(x.size // 32, np.float32) if scaled else None
+    lib().orc_quant_q8_0(_ptr(x, _f32p), x.size, _ptr(y, _u8p), None if sc is None else _ptr(sc, _f32p))
+    return (y, sc) if scaled else y
+
+
+def s2_expert(blob: np.ndarray, H: int, F: int, xq: np.ndarray, xs: np.ndarray | None = None) -> np.ndarray:
+    """One S2 expert on one token's Q8_0 activation row (and fp32 scales)."""
+    b = np.ascontiguousarray(blob, np.uint8)
+    q = np.ascontiguousarray(xq, np.uint8)
+    s = None if xs is None else np.ascontiguousarray(xs, np.float32)
+    out = np.empty(H, np.float32)
+    lib().orc_s2_expert(_ptr(b, _u8p), H, F, _ptr(q, _u8p), None if s is None else _ptr(s, _f32p), _ptr(out, _f32p))
+    return out
 
 
 def combine(parts: np.ndarray, w: np.ndarray, shared: np.ndarray | None) -> np.ndarray:

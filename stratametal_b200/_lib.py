@@ -58,6 +58,33 @@ SIGNATURES = {
     "smoe_rms_norm_weighted": (C.c_int, [_vp, _vp, C.c_int64, C.c_int64, C.c_float, _vp]),
     "smoe_add_rms_norm": (C.c_int, [_vp, _vp, _vp, C.c_int64, C.c_int64, C.c_float, _vp]),
     "smoe_set_expert_path": (C.c_int, [C.c_int]),
+    "smoe_s2_blob_bytes": (C.c_size_t, [C.c_int, C.c_int]),
+    "smoe_s2_pack_expert": (C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, _vp, _vp]),
+    "smoe_quantize_q8_0": (C.c_int, [_vp, _vp, _vp, C.c_int64, _vp]),
+    "smoe_moe_grouped_scratch_bytes": (C.c_size_t, [C.c_int64, C.c_int64, C.c_int64]),
+    "smoe_moe_grouped_s2": (C.c_int, [_vp, _vp, _vp, _vp, _vp, C.c_int64, C.c_int64, C.c_int, C.c_int, _vp, _vp,
+                                      _vp, _vp, _vp]),
+    "smoe_moe_group_resident": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int64, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "smoe_moe_hit_select": (C.c_int, [_vp, _vp, C.c_int, C.c_int, _vp, _vp, _vp, _vp]),
+    "smoe_moe_hit_grouped_s2": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int64, C.c_int64, C.c_int, C.c_int, _vp, _vp,
+                                          C.c_int, _vp, _vp, _vp]),
+    "smoe_moe_hit_add": (C.c_int, [_vp, _vp, _vp, _vp, C.c_int64, C.c_int64, _vp]),
+    "smoe_native_experts_open": (C.c_int, [C.c_char_p, C.POINTER(_vp)]),
+    "smoe_native_experts_close": (None, [_vp]),
+    "smoe_native_experts_pick": (C.c_int, [_vp, C.c_int64, C.c_int64, C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                           C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(_vp)]),
+    "smoe_expert_cache_open": (C.c_int, [C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int, C.POINTER(_vp)]),
+    "smoe_expert_cache_close": (None, [_vp]),
+    "smoe_expert_cache_ensure": (C.c_int, [_vp, C.c_int64, C.c_int64, _vp, C.c_int64, _vp, C.POINTER(C.c_int32)]),
+    "smoe_expert_cache_slot_of": (C.c_int32, [_vp, C.c_int64, C.c_int64]),
+    "smoe_expert_cache_arena": (_vp, [_vp]),
+    "smoe_expert_cache_row": (_vp, [_vp, C.c_int64]),
+    "smoe_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_vp)]),
+    "smoe_gguf_close": (None, [_vp]),
+    "smoe_gguf_tensor": (C.c_int, [_vp, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_int64), C.POINTER(C.c_uint64),
+                                   C.POINTER(_vp)]),
+    "smoe_gguf_load_layer": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(SmoeLayer), C.POINTER(_vp)]),
+    "smoe_gguf_free_layer": (None, [_vp]),
     "smoe_expert_path_for": (C.c_int, [C.POINTER(SmoeLayer), C.c_int]),
     "smoe_layer_check": (C.c_int, [C.POINTER(SmoeLayer)]),
     "smoe_moe_scratch_bytes": (C.c_size_t, [C.POINTER(SmoeLayer), C.c_int]),

@@ -185,3 +185,169 @@ def expert_path_for(m: "MoeLayer", n_tokens: int) -> int:
     cores, 3 fused single-token kernel, 4 int8 tensor cores."""
     import ctypes as C
     return int(lib().smoe_expert_path_for(C.byref(m.c), n_tokens))
+
+
+# ---- the pack's planar S2 experts, the grouped / hit decode API, and expert streaming -------------------------------
+def s2_blob_bytes(n_embd: int, n_ff: int) -> int:
+    return int(lib().smoe_s2_blob_bytes(n_embd, n_ff))
+
+
+def s2_pack_expert(gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor, n_embd: int, n_ff: int,
+                   blob: torch.Tensor) -> None:
+    """One expert's GGUF Q2_0 rows (device) -> its planar S2 blob (device)."""
+    check(lib().smoe_s2_pack_expert(_p(gate), _p(up), _p(down), n_embd, n_ff, _p(blob), _s()))
+
+
+def quantize_q8_0(x: torch.Tensor, n: int, blocks: torch.Tensor, scales: torch.Tensor | None = None) -> None:
+    check(lib().smoe_quantize_q8_0(_p(x), _p(blocks), _p(scales), n, _s()))
+
+
+def moe_grouped_scratch_bytes(cap_entries: int, n_embd: int, n_ff: int) -> int:
+    return int(lib().smoe_moe_grouped_scratch_bytes(cap_entries, n_embd, n_ff))
+
+
+def moe_grouped_s2(grp_ptr, grp_start, n_groups, ent_dst, ent_tok, cap_groups: int, cap_entries: int, n_embd: int,
+                   n_ff: int, x_q8_0, x_scales, scratch, out) -> None:
+    check(lib().smoe_moe_grouped_s2(_p(grp_ptr), _p(grp_start), _p(n_groups), _p(ent_dst), _p(ent_tok), cap_groups,
+                                    cap_entries, n_embd, n_ff, _p(x_q8_0), _p(x_scales), _p(scratch), _p(out), _s()))
+
+
+def moe_group_resident(ids, n: int, k_per_tok: int, base: int, blob_bytes: int, grp_ptr, grp_start, counts, ent_dst,
+                       ent_tok) -> None:
+    check(lib().smoe_moe_group_resident(_p(ids), n, k_per_tok, base, blob_bytes, _p(grp_ptr), _p(grp_start),
+                                        _p(counts), _p(ent_dst), _p(ent_tok), _s()))
+
+
+def moe_hit_select(ids, res_row: int, n: int, n_expert: int, slot, dst, count) -> None:
+    """res_row: a device address (an ExpertCache row, or a tensor's data_ptr())."""
+    check(lib().smoe_moe_hit_select(_p(ids), res_row, n, n_expert, _p(slot), _p(dst), _p(count), _s()))
+
+
+def moe_hit_grouped_s2(blob_base: int, slot_index, dst_index, d_count, cap: int, blob_bytes: int, n_embd: int, n_ff: int,
+                       x_q8_0, x_scales, k_per_token: int, scratch, out) -> None:
+    check(lib().smoe_moe_hit_grouped_s2(blob_base, _p(slot_index), _p(dst_index), _p(d_count), cap, blob_bytes, n_embd,
+                                        n_ff, _p(x_q8_0), _p(x_scales), k_per_token, _p(scratch), _p(out), _s()))
+
+
+def moe_hit_add(parts, hit_out, dst, count, cap: int, n_embd: int) -> None:
+    check(lib().smoe_moe_hit_add(_p(parts), _p(hit_out), _p(dst), _p(count), cap, n_embd, _s()))
+
+
+class NativeExperts:
+    """The pack's expert file (native_experts.txt over a mapped experts.bin): pick(layer, expert)."""
+
+    def __init__(self, pack_dir: str):
+        import ctypes as C
+        h = C.c_void_p()
+        check(lib().smoe_native_experts_open(str(pack_dir).encode(), C.byref(h)))
+        self.h = h
+
+    def pick(self, layer: int, expert: int) -> dict:
+        import ctypes as C
+        gu, d = C.c_int(), C.c_int()
+        off, nb = C.c_uint64(), C.c_uint64()
+        ptr = C.c_void_p()
+        check(lib().smoe_native_experts_pick(self.h, layer, expert, C.byref(gu), C.byref(d), C.byref(off),
+                                             C.byref(nb), C.byref(ptr)))
+        return {"gu_type": gu.value, "d_type": d.value, "file_off": off.value, "blob_bytes": nb.value,
+                "host_blob": ptr.value}
+
+    def close(self) -> None:
+        if self.h:
+            lib().smoe_native_experts_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass
+
+
+class ExpertCache:
+    """The VRAM expert tier: ensure(layer, expert, host_ptr, nbytes) -> slot (or -1 when full)."""
+
+    def __init__(self, n_slots: int, n_layers: int, n_expert: int, blob_bytes: int, per_layer: bool = False):
+        import ctypes as C
+        h = C.c_void_p()
+        check(lib().smoe_expert_cache_open(n_slots, n_layers, n_expert, blob_bytes, 1 if per_layer else 0, C.byref(h)))
+        self.h, self.blob_bytes = h, blob_bytes
+
+    def ensure(self, layer: int, expert: int, host_ptr: int, nbytes: int) -> int:
+        import ctypes as C
+        slot = C.c_int32()
+        check(lib().smoe_expert_cache_ensure(self.h, layer, expert, host_ptr, nbytes, _s(), C.byref(slot)))
+        return slot.value
+
+    def slot_of(self, layer: int, expert: int) -> int:
+        return int(lib().smoe_expert_cache_slot_of(self.h, layer, expert))
+
+    def arena(self) -> int:
+        return int(lib().smoe_expert_cache_arena(self.h))
+
+    def row(self, layer: int) -> int:
+        return int(lib().smoe_expert_cache_row(self.h, layer) or 0)
+
+    def close(self) -> None:
+        if self.h:
+            torch.cuda.synchronize()
+            lib().smoe_expert_cache_close(self.h)
+            self.h = None
+
+
+class GgufModel:
+    """A GGUF file mapped read-only (smoe_gguf_*): tensors by name, and MoE layers uploaded to the device."""
+
+    def __init__(self, path):
+        import ctypes as C
+        h = C.c_void_p()
+        check(lib().smoe_gguf_open(str(path).encode(), C.byref(h)))
+        self.h = h
+
+    def tensor(self, name: str) -> dict:
+        import ctypes as C
+        t, nb, ptr = C.c_int(), C.c_uint64(), C.c_void_p()
+        ne = (C.c_int64 * 4)()
+        check(lib().smoe_gguf_tensor(self.h, name.encode(), C.byref(t), ne, C.byref(nb), C.byref(ptr)))
+        return {"type": t.value, "ne": tuple(ne), "bytes": nb.value, "data": ptr.value}
+
+    def load_layer(self, layer: int, with_shared: bool = True, k: int = 0) -> "GgufMoeLayer":
+        return GgufMoeLayer(self, layer, with_shared, k)
+
+    def close(self) -> None:
+        if self.h:
+            lib().smoe_gguf_close(self.h)
+            self.h = None
+
+
+class GgufMoeLayer:
+    """One MoE layer uploaded from a GGUF model (the device planes are owned here); forward as MoeLayer."""
+
+    def __init__(self, model: GgufModel, layer: int, with_shared: bool, k: int, max_tokens: int = 64,
+                 device: torch.device | str = "cuda"):
+        import ctypes as C
+        self.c = SmoeLayer()
+        owner = C.c_void_p()
+        check(lib().smoe_gguf_load_layer(model.h, layer, 1 if with_shared else 0, k, C.byref(self.c), C.byref(owner)))
+        self.owner = owner
+        self.device = torch.device(device)
+        self.max_tokens = max_tokens
+        nbytes = int(lib().smoe_moe_scratch_bytes(C.byref(self.c), max_tokens))
+        self.scratch = torch.empty(nbytes + 256, dtype=torch.uint8, device=self.device)
+        self.scratch_ptr = self.scratch.data_ptr() + (-self.scratch.data_ptr()) % 256
+        self.scratch_bytes = nbytes
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        import ctypes as C
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty(T, self.c.n_embd, dtype=torch.float32, device=self.device)
+        check(lib().smoe_moe_forward(C.byref(self.c), _p(x), T, _p(out), self.scratch_ptr, self.scratch_bytes, None,
+                                     _s()))
+        return out
+
+    def close(self) -> None:
+        if self.owner:
+            torch.cuda.synchronize()
+            lib().smoe_gguf_free_layer(self.owner)
+            self.owner = None

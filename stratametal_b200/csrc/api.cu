@@ -649,6 +649,111 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     return ok();
 }
 
+// ---- the pack's planar S2 experts and the grouped / hit decode API ---------------------------------------------
+static bool s2_geom_ok(int H, int F) { return H > 0 && F > 0 && H % 64 == 0 && F % 64 == 0 && H <= 16384 && F <= 16384; }
+
+size_t smoe_s2_blob_bytes(int n_embd, int n_ff) { return s2_geom_ok(n_embd, n_ff) ? s2_blob_bytes(n_embd, n_ff) : 0; }
+
+smoe_status smoe_s2_pack_expert(const uint8_t* gate, const uint8_t* up, const uint8_t* down, int n_embd, int n_ff,
+                                uint8_t* blob, void* stream) {
+    if (!s2_geom_ok(n_embd, n_ff)) return fail(SMOE_INVALID_ARG, "s2_pack_expert: n_embd and n_ff must be positive multiples of 64");
+    if (!stream) return fail(SMOE_INVALID_ARG, "s2_pack_expert: a non-null stream is required");
+    if (!gate || !up || !down || !blob || !aligned(blob, 16))
+        return fail(SMOE_INVALID_ARG, "s2_pack_expert: null plane, or blob not 16-byte aligned");
+    const cudaError_t e = launch_s2_pack(gate, up, down, n_embd, n_ff, blob, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "s2_pack_expert");
+}
+
+smoe_status smoe_quantize_q8_0(const float* x, uint8_t* blocks, float* scales, int64_t n, void* stream) {
+    if (n < 0) return fail(SMOE_INVALID_ARG, "quantize_q8_0: negative length");
+    if (n == 0) return ok();
+    if (n % 32) return fail(SMOE_INVALID_ARG, "quantize_q8_0: length must be a multiple of 32");
+    if (!stream) return fail(SMOE_INVALID_ARG, "quantize_q8_0: a non-null stream is required");
+    if (!x || !blocks || !aligned(blocks, 2)) return fail(SMOE_INVALID_ARG, "quantize_q8_0: null buffer or odd address");
+    const cudaError_t e = launch_quant_q8_0(x, n, blocks, scales, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "quantize_q8_0");
+}
+
+size_t smoe_moe_grouped_scratch_bytes(int64_t cap_entries, int64_t n_embd, int64_t n_ff) {
+    if (cap_entries <= 0 || cap_entries > (1 << 20) || !s2_geom_ok((int) n_embd, (int) n_ff)) return 0;
+    return s2_scratch_bytes(cap_entries, (int) n_embd, (int) n_ff);
+}
+
+static smoe_status s2_common(int H, int F, int64_t cap, const uint8_t* xq, void* scratch, float* out, void* stream,
+                             const char* who) {
+    if (!s2_geom_ok(H, F)) return fail(SMOE_INVALID_ARG, std::string(who) + ": n_embd and n_ff must be positive multiples of 64");
+    if (cap > (1 << 20)) return fail(SMOE_INVALID_ARG, std::string(who) + ": capacity above 2^20");
+    if (!stream) return fail(SMOE_INVALID_ARG, std::string(who) + ": a non-null stream is required");
+    if (!xq || !scratch || !out || !aligned(xq, 2) || !aligned(scratch, 256))
+        return fail(SMOE_INVALID_ARG, std::string(who) + ": null buffer, x not 2-byte or scratch not 256-byte aligned");
+    return SMOE_OK;
+}
+
+smoe_status smoe_moe_grouped_s2(const unsigned long long* grp_ptr, const int32_t* grp_start, const int32_t* n_groups,
+                                const int32_t* ent_dst, const int32_t* ent_tok, int64_t cap_groups, int64_t cap_entries,
+                                int n_embd, int n_ff, const uint8_t* x_q8_0, const float* x_scales, void* scratch,
+                                float* out, void* stream) {
+    if (cap_groups < 0 || cap_entries < 0) return fail(SMOE_INVALID_ARG, "moe_grouped_s2: negative capacity");
+    if (cap_groups == 0 || cap_entries == 0) return ok();
+    smoe_status st = s2_common(n_embd, n_ff, std::max(cap_groups, cap_entries), x_q8_0, scratch, out, stream, "moe_grouped_s2");
+    if (st != SMOE_OK) return st;
+    if (!grp_ptr || !grp_start || !n_groups || !ent_dst || !ent_tok) return fail(SMOE_INVALID_ARG, "moe_grouped_s2: null list");
+    const cudaError_t e = launch_s2_grouped(grp_ptr, grp_start, n_groups, ent_dst, ent_tok, (int) cap_groups,
+                                            (int) cap_entries, n_embd, n_ff, x_q8_0, x_scales, scratch, out,
+                                            (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "moe_grouped_s2");
+}
+
+smoe_status smoe_moe_group_resident(const int32_t* ids, int n, int k_per_tok, const uint8_t* base, int64_t blob_bytes,
+                                    unsigned long long* grp_ptr, int32_t* grp_start, int32_t* counts, int32_t* ent_dst,
+                                    int32_t* ent_tok, void* stream) {
+    if (n < 0 || k_per_tok < 0 || blob_bytes < 0) return fail(SMOE_INVALID_ARG, "moe_group_resident: negative size");
+    if (n > 1024) return fail(SMOE_INVALID_ARG, "moe_group_resident: at most 1024 routing entries");
+    if (!stream) return fail(SMOE_INVALID_ARG, "moe_group_resident: a non-null stream is required");
+    if (!ids && n > 0) return fail(SMOE_INVALID_ARG, "moe_group_resident: null ids");
+    if (!base || !grp_ptr || !grp_start || !counts || !ent_dst || !ent_tok)
+        return fail(SMOE_INVALID_ARG, "moe_group_resident: null output");
+    const cudaError_t e = launch_s2_group_resident(ids, n, k_per_tok, base, blob_bytes, grp_ptr, grp_start, counts,
+                                                   ent_dst, ent_tok, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "moe_group_resident");
+}
+
+smoe_status smoe_moe_hit_select(const int32_t* ids, const int32_t* res_row, int n, int n_expert, int32_t* slot,
+                                int32_t* dst, int32_t* count, void* stream) {
+    if (n < 0 || n_expert < 0) return fail(SMOE_INVALID_ARG, "moe_hit_select: negative size");
+    if (n > 1024) return fail(SMOE_INVALID_ARG, "moe_hit_select: at most 1024 routing entries");
+    if (!stream) return fail(SMOE_INVALID_ARG, "moe_hit_select: a non-null stream is required");
+    if ((!ids && n > 0) || !res_row || !slot || !dst || !count) return fail(SMOE_INVALID_ARG, "moe_hit_select: null buffer");
+    const cudaError_t e = launch_s2_hit_select(ids, res_row, n, n_expert, slot, dst, count, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "moe_hit_select");
+}
+
+smoe_status smoe_moe_hit_grouped_s2(const uint8_t* blob_base, const int32_t* slot_index, const int32_t* dst_index,
+                                    const int32_t* d_count, int64_t cap, int64_t blob_bytes, int n_embd, int n_ff,
+                                    const uint8_t* x_q8_0, const float* x_scales, int k_per_token, void* scratch,
+                                    float* out, void* stream) {
+    if (cap < 0 || k_per_token < 0) return fail(SMOE_INVALID_ARG, "moe_hit_grouped_s2: negative size");
+    if (cap == 0) return ok();
+    smoe_status st = s2_common(n_embd, n_ff, cap, x_q8_0, scratch, out, stream, "moe_hit_grouped_s2");
+    if (st != SMOE_OK) return st;
+    if (!blob_base || !slot_index || !dst_index || !d_count) return fail(SMOE_INVALID_ARG, "moe_hit_grouped_s2: null list");
+    if (blob_bytes < (int64_t) s2_blob_bytes(n_embd, n_ff) || blob_bytes % 16 || !aligned(blob_base, 16))
+        return fail(SMOE_INVALID_ARG, "moe_hit_grouped_s2: slots must hold a blob and be 16-byte aligned");
+    const cudaError_t e = launch_s2_hits(blob_base, slot_index, dst_index, d_count, (int) cap, blob_bytes, n_embd, n_ff,
+                                         x_q8_0, x_scales, k_per_token, scratch, out, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "moe_hit_grouped_s2");
+}
+
+smoe_status smoe_moe_hit_add(float* parts, const float* hit_out, const int32_t* dst, const int32_t* count, int64_t cap,
+                             int64_t n_embd, void* stream) {
+    if (cap < 0 || n_embd < 0) return fail(SMOE_INVALID_ARG, "moe_hit_add: negative size");
+    if (cap == 0 || n_embd == 0) return ok();
+    if (!stream) return fail(SMOE_INVALID_ARG, "moe_hit_add: a non-null stream is required");
+    if (!parts || !hit_out || !dst || !count) return fail(SMOE_INVALID_ARG, "moe_hit_add: null buffer");
+    const cudaError_t e = launch_s2_hit_add(parts, hit_out, dst, count, (int) cap, n_embd, (cudaStream_t) stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "moe_hit_add");
+}
+
 size_t smoe_ep_area_bytes(const smoe_layer* L, int max_tokens, int world) {
     // geometry only (n_embd, k): the area does not depend on the planes
     if (!L || L->n_embd <= 0 || L->n_embd % 128 || L->k <= 0 || L->k > kMaxK || max_tokens < 1 || world < 1 ||

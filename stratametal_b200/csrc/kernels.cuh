@@ -181,6 +181,26 @@ cudaError_t launch_tq_gate_up(Matrix gate, Matrix up, Matrix sgate, Matrix sup, 
 cudaError_t launch_tq_down(Matrix down, Matrix sdown, Work w, int n_expert, KAct ha, float* y, int n_ff, int n_embd,
                            cudaStream_t s);
 
+// ---- s2.cu ---- (the pack's planar S2 experts and the grouped / hit decode API over them)
+size_t s2_blob_bytes(int H, int F);
+size_t s2_scratch_bytes(int64_t cap, int H, int F);
+cudaError_t launch_s2_pack(const uint8_t* gate, const uint8_t* up, const uint8_t* down, int H, int F, uint8_t* blob,
+                           cudaStream_t s);
+cudaError_t launch_quant_q8_0(const float* x, int64_t n, uint8_t* y, float* scales, cudaStream_t s);
+cudaError_t launch_s2_grouped(const unsigned long long* grp_ptr, const int32_t* grp_start, const int32_t* n_groups,
+                              const int32_t* ent_dst, const int32_t* ent_tok, int cap_groups, int cap_entries, int H,
+                              int F, const uint8_t* xq, const float* xs, void* scratch, float* out, cudaStream_t s);
+cudaError_t launch_s2_group_resident(const int32_t* ids, int n, int k_per_tok, const uint8_t* base, int64_t blob,
+                                     unsigned long long* grp_ptr, int32_t* grp_start, int32_t* counts, int32_t* ent_dst,
+                                     int32_t* ent_tok, cudaStream_t s);
+cudaError_t launch_s2_hit_select(const int32_t* ids, const int32_t* res_row, int n, int n_expert, int32_t* slot,
+                                 int32_t* dst, int32_t* count, cudaStream_t s);
+cudaError_t launch_s2_hits(const uint8_t* base, const int32_t* slot_index, const int32_t* dst_index,
+                           const int32_t* d_count, int cap, int64_t blob_bytes, int H, int F, const uint8_t* xq,
+                           const float* xs, int k_per_token, void* scratch, float* out, cudaStream_t s);
+cudaError_t launch_s2_hit_add(float* parts, const float* hit_out, const int32_t* dst, const int32_t* count, int cap,
+                              int64_t H, cudaStream_t s);
+
 // ---- elementwise.cu ----
 // x[r] = rms_norm(x[r] + residual[r]) * w (residual and w may be null): the host rule of rms_ref.
 cudaError_t launch_add_rms_norm(float* x, const float* residual, const float* w, int64_t rows, int64_t cols,

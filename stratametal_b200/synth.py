@@ -16,6 +16,7 @@ Distributions (the choices the configs leave open are marked *
 from __future__ import annotations
 
 import functools
+import struct
 import math
 from dataclasses import dataclass, field
 
@@ -253,3 +254,94 @@ def config_spec(cfg: int, seed: int | None = None) -> tuple[LayerSpec, int]:
     if cfg == 4:
         return LayerSpec(gu_type=IQ2_S, seed=seed or 20244), 8
     raise ValueError(cfg)
+
+
+def write_native_pack(pack_dir, layers: list[list[np.ndarray]], gu_type: int, d_type: int, version: int = 4) -> None:
+    """A pack's expert file: experts.bin = every layer's expert blobs back to back (layers in order), and
+    native_experts.txt with the header and one "layer gu_type d_type offset blob_bytes" line per layer (the format
+    metal/src/pack.cpp:367-416 reads).  layers[l][e] is expert e's blob (uint8) of layer l."""
+    from pathlib import Path
+    d = Path(pack_dir)
+    d.mkdir(parents=True, exist_ok=True)
+    n_expert = len(layers[0])
+    lines = [f"# strata native experts v{version} (n_expert {n_expert})"]
+    off = 0
+    with open(d / "experts.bin", "wb") as f:
+        for li, blobs in enumerate(layers):
+            assert len(blobs) == n_expert and len({b.size for b in blobs}) == 1
+            lines.append(f"{li} {gu_type} {d_type} {off} {blobs[0].size}")
+            for b in blobs:
+                f.write(np.ascontiguousarray(b, np.uint8).tobytes())
+            off += blobs[0].size * n_expert
+    (d / "native_experts.txt").write_text("\n".join(lines) + "\n")
+
+
+GGUF_BF16, GGUF_F32 = 30, 0
+
+
+def _gguf_str(s: str) -> bytes:
+    b = s.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def _gguf_value(v) -> bytes:
+    if isinstance(v, bool):
+        return struct.pack("<IB", 7, int(v))
+    if isinstance(v, int):
+        return struct.pack("<IQ", 10, v) if v >= 2 ** 32 else struct.pack("<II", 4, v)
+    if isinstance(v, float):
+        return struct.pack("<If", 6, v)
+    if isinstance(v, str):
+        return struct.pack("<I", 8) + _gguf_str(v)
+    if isinstance(v, list):  # arrays of strings or of int32
+        if all(isinstance(x, str) for x in v):
+            return struct.pack("<IIQ", 9, 8, len(v)) + b"".join(_gguf_str(x) for x in v)
+        return struct.pack("<IIQ", 9, 5, len(v)) + b"".join(struct.pack("<i", x) for x in v)
+    raise TypeError(type(v))
+
+
+def write_gguf(path, tensors: list, meta: dict, alignment: int = 32, version: int = 3) -> None:
+    """A GGUF file: the header, the metadata `meta` (int, float, bool, str, list of str or int), then each tensor
+    (name, ggml type, ne tuple with ne[0] fastest, raw bytes) at an aligned offset of the data section."""
+    kv = dict(meta)
+    if alignment != 32:
+        kv["general.alignment"] = alignment
+    head = struct.pack("<IIQQ", 0x46554747, version, len(tensors), len(kv))
+    head += b"".join(_gguf_str(k) + _gguf_value(v) for k, v in kv.items())
+    off, infos, datas = 0, [], []
+    for name, ttype, ne, data in tensors:
+        infos.append(_gguf_str(name) + struct.pack("<I", len(ne)) + b"".join(struct.pack("<Q", n) for n in ne) +
+                     struct.pack("<IQ", ttype, off))
+        data = bytes(data)
+        pad = (-len(data)) % alignment
+        datas.append(data + bytes(pad))
+        off += len(data) + pad
+    head += b"".join(infos)
+    head += bytes((-len(head)) % alignment)
+    with open(path, "wb") as f:
+        f.write(head)
+        for d in datas:
+            f.write(d)
+
+
+def layer_gguf_tensors(lay: Layer, index: int, router_f32: bool = False) -> list:
+    """The MoE tensors of a synthetic layer under the names of layer `index` of a GGUF model (blk.<L>.<name>)."""
+    sp = lay.spec
+    H, F, E = sp.n_embd, sp.n_ff, sp.n_expert
+    t = {k: v.cpu().numpy() for k, v in lay.tensors.items()}
+    pre = f"blk.{index}."
+    r = t["ffn_gate_inp.weight"].view(np.uint16)
+    if router_f32:  # stored as f32 (its bf16 values exactly)
+        rt, rb = GGUF_F32, (r.astype(np.uint32) << 16).view(np.float32).tobytes()
+    else:
+        rt, rb = GGUF_BF16, r.tobytes()
+    out = [(pre + "ffn_gate_inp.weight", rt, (H, E), rb),
+           (pre + "ffn_gate_exps.weight", sp.gu_type, (H, F, E), t["ffn_gate_exps.weight"].tobytes()),
+           (pre + "ffn_up_exps.weight", sp.gu_type, (H, F, E), t["ffn_up_exps.weight"].tobytes()),
+           (pre + "ffn_down_exps.weight", sp.d_type, (F, H, E), t["ffn_down_exps.weight"].tobytes())]
+    if sp.has_shared:
+        out += [(pre + "ffn_gate_shexp.weight", sp.sg_type, (H, F), t["ffn_gate_shexp.weight"].tobytes()),
+                (pre + "ffn_up_shexp.weight", sp.su_type, (H, F), t["ffn_up_shexp.weight"].tobytes()),
+                (pre + "ffn_down_shexp.weight", sp.sd_type, (F, H), t["ffn_down_shexp.weight"].tobytes()),
+                (pre + "ffn_gate_inp_shexp.weight", GGUF_BF16, (H,), t["ffn_gate_inp_shexp.weight"].view(np.uint16).tobytes())]
+    return out

@@ -39,3 +39,16 @@ def test_cpp_ffn_exec_and_stack(exe):
     r = subprocess.run([str(exe), "run"], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "run: ok" in r.stdout
+
+
+def test_cpp_residency_rules(tmp_path):
+    # host only: the admission rules of the VRAM expert tier (include/smoe_stream.hpp)
+    out = tmp_path / "stream_test"
+    cmd = ["g++", "-std=c++17", "-O2", "-I", str(ROOT / "include"), "-I", str(CUDA / "include"),
+           str(ROOT / "tests" / "cpp" / "stream_test.cpp"), "-o", str(out), "-L", str(CUDA / "lib64"), "-lcudart",
+           str(_lib.lib_path()), f"-Wl,-rpath,{_lib.lib_path().parent}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(out)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "residency: ok" in r.stdout

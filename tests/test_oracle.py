@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
+from stratametal_b200 import synth
 
 
 def bits(a):
@@ -253,3 +254,21 @@ def test_expert_pairs_through_the_layer(golden, name):
     # the oracle's block over the other formats reproduces the reference's ref_expert bit for bit
     got = O.moe_layer(pair_layer(golden, name), golden[f"pair_{name}_x"])
     assert np.array_equal(got.ravel().view(np.uint32), golden[f"pair_{name}_y"].view(np.uint32))
+
+
+def test_s2_expert_is_the_gguf_expert():
+    # An S2 blob is a re-layout of GGUF Q2_0 rows, and its rows are evaluated in the reference's row_dot order: on
+    # the same int8 activations and scales it gives the reference's own GGUF expert chain (the one-expert block
+    # below, pinned bitwise to ref_expert by test_expert_pairs_through_the_layer) bit for bit.  The Q8_0 and q8_1
+    # rules round the same values the same way except at exact half-way ties, which these inputs do not hit.
+    H, F = 512, 128
+    rows = [synth.quant_matrix(42, k, n_out, n_in, "cpu").numpy() for k, n_out, n_in in ((1, F, H), (2, F, H), (3, H, F))]
+    x = np.random.default_rng(77).standard_normal((1, H)).astype(np.float32)
+    q80, q81 = O.quant_q8_0(x), O.quant_q8_1(x.ravel())
+    for b in range(H // 32):
+        assert np.array_equal(q80[b * 34:b * 34 + 2], q81[b * 36:b * 36 + 2])
+        assert np.array_equal(q80[b * 34 + 2:b * 34 + 34], q81[b * 36 + 4:b * 36 + 36])
+    s2 = O.s2_expert(O.s2_pack(*rows, H, F), H, F, q80)
+    layer = O.HostLayer(H, F, 1, 1, O.Q2_0, O.Q2_0, np.full(H, 0x3C00, np.uint16), rows[0], rows[1], rows[2], None)
+    gguf = O.moe_layer(layer, x).ravel()
+    assert np.array_equal(s2.view(np.uint32), gguf.view(np.uint32))
