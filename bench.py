@@ -49,6 +49,7 @@ KERNEL_OF_STAGE = {"router_gemv": "bf16_gemv_kernel", "router_topk_q8": "router_
                    "expert_down": "layer_down_kernel", "combine": "combine_kernel"}
 KERNEL_OF_STAGE_TC = dict(KERNEL_OF_STAGE, expert_gate_up="tc_expert_kernel<0>", expert_down="tc_expert_kernel<1>")
 KERNEL_OF_STAGE_TQ = dict(KERNEL_OF_STAGE, expert_gate_up="tq_expert_kernel<0>", expert_down="tq_expert_kernel<1>")
+FUSED_KERNEL = "decode_stack_kernel"
 # sub-records: name -> (config, tokens per step, single-layer configs: distinct layers x batches rotated)
 SUBS = {"cfg0_b1": (0, 1, (16, 1)), "cfg2_prefill4096": (2, 4096, (2, 1)), "cfg3_stack48_b1": (3, 1, None),
         "cfg3_stack48_b16": (3, 16, None), "cfg4_iq2s_b8": (4, 8, (4, 4))}
@@ -394,7 +395,13 @@ def measure(args, ws, rank, local, clk, cfg, T_req, rot):
     def forward_once(li, b, dst):
         layers[li].forward(xs[b], dst)
 
+    # the batch-1 stack runs as one persistent launch per 48 layers (smoe_stack_decode) when its layers qualify
+    stack_kernel = stack and fused and not ep_mode
+    stack_scratch = torch.empty(1 << 20, dtype=torch.uint8, device=dev) if stack_kernel else None
+
     def stack_once():
+        if stack_kernel:
+            return api.stack_decode(layers, xs[0], sbuf[(n_layers - 1) & 1], RMS_EPS, scratch=stack_scratch)
         cur = xs[0]
         for li in range(n_layers):
             nxt = sbuf[li & 1]
@@ -493,8 +500,9 @@ def measure(args, ws, rank, local, clk, cfg, T_req, rot):
         step_bytes = float(sum((d + 1) * E_BYTES for d in Ds))
         D_mean = float(np.mean(Ds))
         expert_gbs = step_bytes / (ms_step * 1e-3) / 1e9 * (ws if ep_mode else 1)
-        roof = {"bound": "hbm", "kernel": f"whole {n_layers}-layer stack (CUDA graph"
-                + (f", {ws} ranks" if ep_mode else "") + ")",
+        roof = {"bound": "hbm", "kernel": ("decode_stack_kernel (the whole stack, one launch)" if stack_kernel else
+                                           f"whole {n_layers}-layer stack (CUDA graph"
+                                           + (f", {ws} ranks" if ep_mode else "") + ")"),
                 "achieved": expert_gbs, "peak": hbm_peak * (ws if ep_mode else 1), "peak_kind": peak_kind,
                 "unit": "GB/s", "frac": expert_gbs / (hbm_peak * (ws if ep_mode else 1)), "traffic": None,
                 "algorithmic_bytes_per_launch": step_bytes, "ms_per_launch": ms_step,
@@ -528,7 +536,7 @@ def measure(args, ws, rank, local, clk, cfg, T_req, rot):
         kos = KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE_TQ if tq else KERNEL_OF_STAGE
         if 2 <= T <= 64:
             kos = dict(kos, router_gemv="router_gemm_kernel + router_reduce_kernel (split K)")
-        kname = "decode_layer_kernel" if fused else kos[dominant]
+        kname = FUSED_KERNEL if fused else kos[dominant]
         if tc and dominant in ("expert_gate_up", "expert_down"):
             flops = flop_gu if dominant == "expert_gate_up" else flop_dn
             achieved = flops / (dom_ms * 1e-3) / 1e12
@@ -590,6 +598,8 @@ def measure(args, ws, rank, local, clk, cfg, T_req, rot):
     if ep_mode:  # router, top-k, dispatch, receive, grouping over the ws * T received rows, experts, wait, combine
         per_fwd = router_l + 1 + 1 + 1 + (3 if ws * T > 256 else 1) + (2 if tc or tq else 3) + 1 + 1
     launches_per_step = n_layers * (per_fwd + 1) if stack else per_fwd
+    if stack_kernel:
+        launches_per_step = (n_layers + 47) // 48
 
     cfgd = config_dict(args.gpus, cfg, spec, T_all, D_mean, n_layers, n_batches, stack)
     if ep_mode:
@@ -604,7 +614,9 @@ def measure(args, ws, rank, local, clk, cfg, T_req, rot):
                           "reference's order" if tq
                      else "int8 x int2 dot (q8_1 contract), f32/f64 sums"),
            "expert_path": ("fp16 tensor cores (tcgen05)" if tc else "int8 tensor cores (tcgen05 kind::i8)" if tq
-                           else "fused single-token kernel (one cooperative launch)" if fused else "SIMT"),
+                           else "fused single-token stack kernel (one cooperative launch for the 48 layers)"
+                           if stack_kernel else "fused single-token kernel (one cooperative launch)" if fused
+                           else "SIMT"),
            "config": cfgd,
            "timing": "CUDA events around CUDA-graph replays (one captured forward per step"
                      + (", the whole 48-layer stack" if stack else "") + ")",

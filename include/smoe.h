@@ -176,8 +176,8 @@ smoe_status smoe_add_rms_norm(float* x, const float* residual, const float* w, i
  * the int8 tensor-core kernels (path 4) when the layer qualifies, the SIMT kernels otherwise;
  * 1 the SIMT kernels always; 2 the fp16 tensor-core kernels whenever the layer qualifies (every routed and
  * shared matrix Q2_0, n_embd and n_ff multiples of 512); 3 the fused single-token kernel whenever the batch is
- * one token and the layer qualifies (every matrix Q2_0, n_embd a multiple of 256, n_ff and n_expert at most
- * 512), automatic otherwise; 4 the int8 tensor-core kernels whenever the layer qualifies (every matrix Q2_0,
+ * one token and the layer qualifies (every matrix Q2_0, n_embd a multiple of 512 and at most 4096, n_ff a
+ * multiple of 128 and at most 1024, n_expert at most 512), automatic otherwise; 4 the int8 tensor-core kernels whenever the layer qualifies (every matrix Q2_0,
  * n_embd and n_ff each 512, 1024 or 2048).  The SIMT, fused and int8 tensor-core kernels evaluate the
  * reference's q8_1 integer contract in the reference's summation order (bit for bit); the fp16 tensor-core
  * kernels evaluate the same products from an exact fp16 hi/lo split of the q8_1 activation with f32
@@ -304,6 +304,16 @@ smoe_status smoe_gguf_tensor(const void* handle, const char* name, int* type, in
  * of whole rows.  *owner keeps the device memory until smoe_gguf_free_layer(*owner). */
 smoe_status smoe_gguf_load_layer(const void* handle, int layer, int with_shared, int k, smoe_layer* out, void** owner);
 void smoe_gguf_free_layer(void* owner);
+
+/* ---- the batch-1 layer stack in one launch -------------------------------------------------------------------
+ * Session::forward's layer walk (metal/src/forward.cpp:554-565) with the MoE half only, for one token:
+ * x = rms_norm_weighted(MoE_l(x) + x, norm_w[l]) for l = 0 .. n_layers - 1 (eps; norm_w NULL or any entry NULL: unit
+ * weight), out = the last x.  Equals n_layers calls of smoe_moe_forward each followed by smoe_add_rms_norm, bit for
+ * bit, in one persistent cooperative launch per 48 layers.  Every layer: one geometry, every matrix Q2_0, n_embd a
+ * multiple of 512, n_ff a multiple of 128 (SMOE_UNSUPPORTED otherwise).  x and out may be the same buffer. */
+size_t smoe_stack_decode_scratch_bytes(const smoe_layer* L);
+smoe_status smoe_stack_decode(const smoe_layer* layers, int n_layers, const float* const* norm_w, float eps,
+                              const float* x, float* out, void* scratch, size_t scratch_bytes, void* stream);
 
 /* ---- Expert parallelism over the GPUs of one node (no reference counterpart: the reference reaches a second
  * GPU only through its peer / remote expert tiers, include/strata/core/peer_experts.hpp:35-104, which this

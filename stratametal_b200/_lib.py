@@ -85,6 +85,9 @@ SIGNATURES = {
                                    C.POINTER(_vp)]),
     "smoe_gguf_load_layer": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(SmoeLayer), C.POINTER(_vp)]),
     "smoe_gguf_free_layer": (None, [_vp]),
+    "smoe_stack_decode_scratch_bytes": (C.c_size_t, [C.POINTER(SmoeLayer)]),
+    "smoe_stack_decode": (C.c_int, [C.POINTER(SmoeLayer), C.c_int, C.POINTER(_vp), C.c_float, _vp, _vp, _vp,
+                                    C.c_size_t, _vp]),
     "smoe_expert_path_for": (C.c_int, [C.POINTER(SmoeLayer), C.c_int]),
     "smoe_layer_check": (C.c_int, [C.POINTER(SmoeLayer)]),
     "smoe_moe_scratch_bytes": (C.c_size_t, [C.POINTER(SmoeLayer), C.c_int]),

@@ -351,3 +351,19 @@ class GgufMoeLayer:
             torch.cuda.synchronize()
             lib().smoe_gguf_free_layer(self.owner)
             self.owner = None
+
+
+def stack_decode(layers: list, x: torch.Tensor, out: torch.Tensor, eps: float = 1e-6,
+                 norm_w: list | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
+    """smoe_stack_decode: one token through every layer (x = rms_norm(MoE_l(x) + x)) in one launch per 48 layers.
+    layers: MoeLayer objects of one geometry."""
+    import ctypes as C
+    n = len(layers)
+    arr = (SmoeLayer * n)(*[m.c for m in layers])
+    nbytes = int(lib().smoe_stack_decode_scratch_bytes(C.byref(layers[0].c)))
+    if scratch is None:
+        scratch = torch.empty(nbytes + 256, dtype=torch.uint8, device=x.device)
+    ptr = scratch.data_ptr() + (-scratch.data_ptr()) % 256
+    nw = None if norm_w is None else (C.c_void_p * n)(*[None if w is None else w.data_ptr() for w in norm_w])
+    check(lib().smoe_stack_decode(arr, n, nw, eps, _p(x), _p(out), ptr, nbytes, _s()))
+    return out

@@ -50,7 +50,7 @@ struct Layout {
     size_t xq, xa, xa2, logits, sh_logit, ids, w, slot, slot_token, tables, sched, gu, ha, parts;
     size_t sched_tc, xh, hh;  // the tensor-core path (0 bytes when the layer does not qualify)
     size_t chunk;             // per-(64-token chunk, expert) counts of the many-CTA grouping
-    size_t bar;               // grid barrier words of the single-token fused kernel
+    size_t dec;               // the single-token fused kernel: logits, h, v and its grid barrier words
     size_t rsplit;            // fp64 partial sums of the few-token router GEMM
     size_t hq;                // q8_1 blocks of h per slot (the any-format path)
     size_t total;
@@ -117,7 +117,7 @@ Layout layout_of(const smoe_layer* L, int T) {
     o.ha = at; at += up256(ka_bytes((int64_t) rows, (int) (F / 32)));
     o.parts = at; at += up256(rows * H * 4);
     o.chunk = at; at += group_chunk_bytes(T, (int) E);
-    o.bar = at; at += 256;
+    o.dec = at; at += up256(decode_scratch_bytes((int) H, (int) F, (int) E, (int) K));
     o.rsplit = at; at += router_split_bytes(std::min(T, kRouterGemmMinTokens), (int) E + 1, (int) H);
     o.sched_tc = o.xh = o.hh = at;
     if (tc_qualifies(L)) {
@@ -462,41 +462,26 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
 
     if (use_decode(L, T)) {
         // one token: the whole block in one cooperative launch
-        DecodeArgs da{};
-        da.x = x;
-        da.out = out;
-        da.router = L->router;
-        da.ginp = sh ? L->gate_inp_shexp : nullptr;
-        da.gate = Matrix{L->gate, (int64_t) F * (int64_t) row_bytes(L->gu_type, H), L->gu_type};
-        da.up = Matrix{L->up, da.gate.expert_stride, L->gu_type};
-        da.down = Matrix{L->down, (int64_t) H * (int64_t) row_bytes(L->d_type, F), L->d_type};
-        da.sgate = Matrix{L->sgate, 0, L->sg_type};
-        da.sup = Matrix{L->sup, 0, L->su_type};
-        da.sdown = Matrix{L->sdown, 0, L->sd_type};
-        da.H = H;
-        da.F = F;
-        da.E = E;
-        da.k = K;
-        da.has_shared = sh ? 1 : 0;
-        da.logits = logits;
-        da.sh_logit = sh_logit;
-        da.ids = ids;
-        da.w = w;
-        da.ha = ha.base;
-        da.xq = trace && trace->xq ? trace->xq : nullptr;
-        da.parts = trace ? trace->parts : nullptr;
-        da.shared_out = trace ? trace->shared : nullptr;
-        da.bar = reinterpret_cast<unsigned*>(base + lo.bar);
-        cudaError_t e = launch_decode_layer(da, s);
+        DecodeHost dh{};
+        dh.layers = L;
+        dh.n_layers = 1;
+        dh.norm = 0;
+        dh.x = x;
+        dh.out = out;
+        dh.scratch = base + lo.dec;
+        if (trace) {
+            dh.ids = trace->ids;
+            dh.w = trace->weights;
+            dh.xq = trace->xq;
+            dh.parts = trace->parts;
+            dh.shared_out = trace->shared;
+        }
+        cudaError_t e = launch_decode(dh, s);
         for (int st = 0; st < SMOE_STAGES && e == cudaSuccess; st++) e = mark(st, s);
         if (e != cudaSuccess) return cuda_fail(e, "moe_forward: fused single-token kernel");
-        if (trace) {
-            if (trace->logits) e = cudaMemcpyAsync(trace->logits, logits, (size_t) E * 4, cudaMemcpyDeviceToDevice, s);
-            if (e == cudaSuccess && trace->ids) e = cudaMemcpyAsync(trace->ids, ids, (size_t) K * 4, cudaMemcpyDeviceToDevice, s);
-            if (e == cudaSuccess && trace->weights)
-                e = cudaMemcpyAsync(trace->weights, w, (size_t) K * 4, cudaMemcpyDeviceToDevice, s);
-            if (e != cudaSuccess) return cuda_fail(e, "moe_forward: trace");
-        }
+        if (trace && trace->logits)
+            e = cudaMemcpyAsync(trace->logits, base + lo.dec, (size_t) E * 4, cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return cuda_fail(e, "moe_forward: trace");
         return ok();
     }
 
@@ -645,6 +630,57 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
             e = cudaMemcpyAsync(trace->xq, xq, (size_t) T * (H / 32) * kQ8Block, cudaMemcpyDeviceToDevice, s);
         if (e == cudaSuccess && trace->parts) e = launch_gather_parts(parts, slot, trace->parts, H, K, T, s);
         if (e != cudaSuccess) return cuda_fail(e, "moe_forward: trace");
+    }
+    return ok();
+}
+
+// ---- the batch-1 layer stack in one launch -------------------------------------------------------------------
+static smoe_status check_stack(const smoe_layer* layers, int n_layers) {
+    if (!layers || n_layers < 1) return fail(SMOE_INVALID_ARG, "stack_decode: no layers");
+    const smoe_layer& L0 = layers[0];
+    for (int l = 0; l < n_layers; l++) {
+        const smoe_status st = check_layer(&layers[l]);
+        if (st != SMOE_OK) return st;
+        const smoe_layer& L = layers[l];
+        if (L.n_embd != L0.n_embd || L.n_ff != L0.n_ff || L.n_expert != L0.n_expert || L.k != L0.k ||
+            L.has_shared != L0.has_shared)
+            return fail(SMOE_INVALID_ARG, "stack_decode: the layers differ in geometry");
+        if (!decode_qualifies(L.n_embd, L.n_ff, L.n_expert, L.k, L.gu_type, L.d_type, L.has_shared, L.sg_type,
+                              L.su_type, L.sd_type))
+            return fail(SMOE_UNSUPPORTED, "stack_decode: a layer does not qualify for the fused single-token kernel "
+                                          "(every matrix Q2_0, n_embd a multiple of 512, n_ff a multiple of 128)");
+    }
+    return SMOE_OK;
+}
+
+size_t smoe_stack_decode_scratch_bytes(const smoe_layer* L) {
+    if (check_layer(L) != SMOE_OK) return 0;
+    return decode_scratch_bytes(L->n_embd, L->n_ff, L->n_expert, L->k);
+}
+
+smoe_status smoe_stack_decode(const smoe_layer* layers, int n_layers, const float* const* norm_w, float eps,
+                              const float* x, float* out, void* scratch, size_t scratch_bytes, void* stream) {
+    smoe_status st = check_stack(layers, n_layers);
+    if (st != SMOE_OK) return st;
+    if (!(eps >= 0.f)) return fail(SMOE_INVALID_ARG, "stack_decode: eps must be >= 0");
+    if (!stream) return fail(SMOE_INVALID_ARG, "stack_decode: a non-null stream is required");
+    if (!x || !out || !scratch || !aligned(scratch, 256))
+        return fail(SMOE_INVALID_ARG, "stack_decode: null buffer or scratch not 256-byte aligned");
+    if (scratch_bytes < decode_scratch_bytes(layers[0].n_embd, layers[0].n_ff, layers[0].n_expert, layers[0].k))
+        return fail(SMOE_INVALID_ARG, "stack_decode: scratch is too small");
+    // launches of at most kDecodeMaxLayers layers; each after the first reads the previous one's output
+    for (int l0 = 0; l0 < n_layers; l0 += kDecodeMaxLayers) {
+        DecodeHost dh{};
+        dh.layers = layers + l0;
+        dh.n_layers = std::min(kDecodeMaxLayers, n_layers - l0);
+        dh.norm_w = norm_w ? norm_w + l0 : nullptr;
+        dh.norm = 1;
+        dh.eps = eps;
+        dh.x = l0 == 0 ? x : out;
+        dh.out = out;
+        dh.scratch = scratch;
+        const cudaError_t e = launch_decode(dh, (cudaStream_t) stream);
+        if (e != cudaSuccess) return cuda_fail(e, "stack_decode");
     }
     return ok();
 }

@@ -1,384 +1,645 @@
-// decode.cu - one token through one MoE layer in a single cooperative launch (batch-1 decode, configs[0] and the
-// configs[3] stack at batch 1).  At one token every stage of the block is a few microseconds of latency and a
-// few megabytes of bytes, so the seven launches of the general path cost more than their work; here the whole
-// block is three phases of one persistent kernel separated by two grid barriers:
+// decode.cu - one token through one MoE layer, or through a stack of layers (x = rms_norm(MoE_l(x) + x) per layer),
+// in a single persistent cooperative launch: batch-1 decode (configs[0] and the configs[3] stack at batch 1).
 //
-//   phase 0  router logits (warp per expert row, fp64 accumulation); every CTA writes the activation's q8_1
-//            image into its shared memory; the CTAs past the router rows take the shared expert's
-//            (32-row block) items, which need no routing: 32 gate and 32 up row dots, SwiGLU and the q8_1 rule
-//            of that block of h
-//   phase 1  every CTA ranks the logits itself (route_cta), starts its phase-2 down rows towards L2, then CTAs
-//            take the routed (expert slot, 32-row block) items
-//   phase 2  CTAs take ranges of output rows: for each row the down dot of every slot (one per half-warp: at
-//            n_ff <= 512 the partials fill lanes 0..15, so the xor-16 level of the reference's butterfly adds
-//            zeros and the 16-lane butterfly gives the same bits), then the combine of the row in router order
-//            (fp64) plus the gated shared expert
+// At one token every stage of the block is microseconds of latency over a few megabytes, so the block is laid out
+// as three phases per layer with grid barriers between them, one CTA per SM (G CTAs):
 //
-// Every dot follows the reference's order (partial k of 32 values to lane k & 31, in-lane sums in k order, xor
-// butterfly 16..1), the activations use the q8_1 rule and the combine the host's fp64 router-order sum, so the
-// output equals the general path's bit for bit.  The grid barriers share an arrival counter in the caller's
-// scratch, zeroed by the host before the launch; every wait is bounded (kWaitLimitNs) and a timeout records
-// kDevTimeout and ends the CTA.  The launch is cooperative, so every CTA is resident.
+//   A  (x known)        every CTA holds x in shared memory; CTA c computes router rows [c R / G, (c + 1) R / G)
+//                       (R = n_expert + 1 with the shared gate row, fp64 sums) from rows it copied into shared memory
+//                       during the previous layer, and quantizes its share of x's q8_1 blocks into a global table.
+//   B  (logits known)   every CTA ranks the logits itself (sixteen warp-local top-k, then one merge), copies its work
+//                       items - whole 32-row blocks of h: 32 gate and 32 up rows of one slot's expert - and its down
+//                       rows (output rows [c H / G, (c + 1) H / G) of every slot) into shared memory, forms the routing
+//                       weights while they arrive, computes h = silu(g) * u of its items and writes each block's q8_1
+//                       image once (the shared expert's items were copied during the previous layer).
+//   C  (h known)        every CTA copies the q8_1 images of h, computes its down rows for every slot and combines them
+//                       per output row in router order (fp64) with the gated shared expert; in a stack it writes
+//                       v = y + x, meets the others once more, and every CTA forms the next x = rms_norm(v) over the
+//                       whole row itself (the RMSNorm kernel's exact reduction tree).
+//
+// Data other CTAs wrote (logits, the q8_1 images of x and h, v) is copied into shared memory with one cp.async.cg each (through L2, every
+// load in flight at once): the same addresses are rewritten every layer, and a line kept in this SM's L1 from the
+// previous layer would be stale.
+//
+// Every dot is the reference's order (partial k of 32 values on lane k & 31, in-lane sums in k order, xor
+// butterfly 16..1), the activations follow the q8_1 rule, the routing route_warp's arithmetic and the combine
+// the host's fp64 router-order sum, so the results equal the general path's (and the oracle's) bit for bit.
+//
+// Grid barrier: an arrival count in the caller's scratch, zeroed on the stream before each launch; barrier n of the
+// launch completes when the count reaches n x the grid (bounded waits: kWaitLimitNs, after which the CTA records
+// kDevTimeout and leaves).
 #include "common.cuh"
 #include "kernels.cuh"
 #include "q8.cuh"
+
+#include <algorithm>
 
 namespace smoe {
 
 constexpr int kDecThreads = 512;  // 16 warps
 constexpr int kDecWarps = kDecThreads / 32;
-constexpr int kDecMaxRows = 32;   // output rows per CTA in phase 2 (n_embd <= 4096 over >= 128 CTAs)
-constexpr int kDecMaxBlocks = 128;  // q8_1 blocks of the activation (n_embd <= 4096)
+constexpr int kDecMaxDownRows = 32;    // output rows per CTA
+constexpr int kDecMaxSlots = kMaxK + 1;
+constexpr int kDecMaxExperts = 512;  // sixteen routing keys per lane of the ranking warp
 
-struct DecodeArgs {
-    const float* x;
-    float* out;
-    const uint16_t* router;
-    const uint16_t* ginp;  // shared-expert gate vector (null without a shared expert)
-    Matrix gate, up, down, sgate, sup, sdown;
-    int H, F, E, k, has_shared;
-    float* logits;       // [E]
-    float* sh_logit;     // [1]
-    int32_t* ids;        // [k]
-    float* w;            // [k]
-    uint8_t* ha;         // (k + 1) x F / 32 blocks of h
-    uint8_t* xq;         // optional q8_1 image of x (trace)
-    float* parts;        // optional [k][H] routed outputs in router order (trace)
-    float* shared_out;   // optional [H] gated shared expert (trace)
-    unsigned* bar;       // [2] arrival count, generation: zero before the launch
+struct DecLayer {
+    const uint16_t* router;  // [E][H] bf16
+    const uint16_t* ginp;    // [H] bf16 shared gate row (null without a shared expert)
+    const uint8_t *gate, *up, *down;
+    const uint8_t *sgate, *sup, *sdown;
+    const float* norm_w;     // [H] RMSNorm weight after this layer (null: unit)
+    int bulk;  // bit 0: gate/up rows by bulk copies (16-byte aligned planes), bit 1: down rows (and 16-byte rows)
 };
 
-// All CTAs meet; false when the wait ran out (the caller then ends the CTA).  bar[0] counts arrivals over the
-// whole launch (zeroed by the host before it): barrier number n of the launch completes when it reaches
-// n * gridDim.x.  One release add per CTA, acquire loads while waiting.
-__device__ __forceinline__ bool grid_barrier(unsigned* bar, unsigned n) {
+struct DecodeArgs {
+    DecLayer layers[kDecodeMaxLayers];
+    int n_layers;
+    int H, F, E, k, has_shared;
+    int norm;       // 1: x = rms_norm(MoE(x) + x) after every layer; 0: out = MoE(x) (one layer)
+    float eps;
+    const float* x;
+    float* out;
+    float* logits;  // [E + 1]
+    uint8_t* xa;    // [H / 32][48] q8_1 image of x
+    uint8_t* hq;    // [(k + 1) F / 32][48] q8_1 images of h
+    float* vbuf;    // [H]
+    unsigned* bar;  // [1]: arrivals over the launch (zero at launch)
+    // single-layer trace (null otherwise)
+    int32_t* ids;
+    float* w;
+    float* sh_logit;
+    uint8_t* xq;
+    float* parts;
+    float* shared_out;
+};
+
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// All CTAs meet at barrier number n (1, 2, ... within the launch); false when this CTA's wait ran out (recorded in
+// the status word).  bar[0] counts arrivals over the whole launch (zeroed before it): barrier n completes when it
+// reaches n * gridDim.x.  One release add per CTA, acquire loads with a short back-off while waiting.
+__device__ __forceinline__ bool dec_grid_sync(unsigned* bar, unsigned n) {
     __syncthreads();
     int ok = 1;
     if (threadIdx.x == 0) {
         const unsigned target = n * gridDim.x;
         unsigned v;
         asm volatile("atom.add.release.gpu.u32 %0, [%1], 1;" : "=r"(v) : "l"(bar) : "memory");
-        v += 1;
-        if (v < target) {
+        if (v + 1 < target) {
             const uint64_t t0 = global_timer_ns();
-            do {
-                asm volatile("ld.acquire.gpu.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
-                if (v >= target) break;
+            while (ld_acquire(bar) < target) {
                 if (global_timer_ns() - t0 > kWaitLimitNs) {
                     ok = 0;
                     atomicOr(&g_smoe_status, kDevTimeout);
                     break;
                 }
-            } while (true);
+                __nanosleep(20);
+            }
         }
     }
     return __syncthreads_and(ok) != 0;
 }
 
-// decode_q2 for a row in global memory: the code words come from 2-byte loads inside the 18-byte block (the
-// shared-memory version reads whole aligned words, which can reach 4 bytes past the last row of a plane).
-__device__ __forceinline__ void decode_q2_global(const uint8_t* __restrict__ row, int k, Dec& w) {
-    const uint8_t* blk = row + (k >> 1) * 18;
-    w.d = f16_to_f32(*reinterpret_cast<const uint16_t*>(blk));
-    const uint16_t* q = reinterpret_cast<const uint16_t*>(blk + 2 + 8 * (k & 1));
-    const uint32_t w0 = (uint32_t) q[0] | ((uint32_t) q[1] << 16);
-    const uint32_t w1 = (uint32_t) q[2] | ((uint32_t) q[3] << 16);
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        w.c[j] = (w0 >> (2 * j)) & 0x03030303u;
-        w.c[4 + j] = (w1 >> (2 * j)) & 0x03030303u;
+// Global -> shared memory copy of `bytes` by the whole CTA: cp.async of 16-byte pieces when both ends and the size
+// allow them, of 4-byte pieces when they allow those, else plain byte copies (complete on return).  The caller
+// commits the group and waits for it.
+__device__ __forceinline__ void dec_stage(uint8_t* dst, const uint8_t* src, uint32_t bytes) {
+    const uintptr_t al = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | bytes;
+    if ((al & 15u) == 0) {
+        for (uint32_t o = threadIdx.x * 16u; o < bytes; o += kDecThreads * 16u)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst + o)), "l"(src + o) : "memory");
+    } else if ((al & 3u) == 0) {
+        for (uint32_t o = threadIdx.x * 4u; o < bytes; o += kDecThreads * 4u)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst + o)), "l"(src + o) : "memory");
+    } else {
+        for (uint32_t o = threadIdx.x; o < bytes; o += kDecThreads) dst[o] = src[o];
     }
-    w.ls = 0;
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Four row dots of n_in values against the same n_in / 32 activation blocks, in the reference's order (partial
-// kk on lane kk & 31, in-lane sums in kk order, xor butterfly 16..1; every lane returns the sums).  All loads of
-// a partial position are issued before its math, so a warp keeps more of them in flight.
-__device__ __forceinline__ void row_dot4_warp(const uint8_t* const (&rows)[4], const uint8_t* __restrict__ act,
-                                              int n_in, int lane, float (&v)[4]) {
-#pragma unroll
-    for (int q = 0; q < 4; q++) v[q] = 0.f;
-    for (int kk = lane; kk < n_in / 32; kk += 32) {
-        Dec d[4];
-#pragma unroll
-        for (int q = 0; q < 4; q++) decode_q2_global(rows[q], kk, d[q]);
-        const ActRegs ar = load_act(act + (size_t) kk * kKaBlock);
-#pragma unroll
-        for (int q = 0; q < 4; q++) v[q] = __fadd_rn(v[q], partial_layer<kQ2_0>(d[q], ar));
+// Q2_0 row of n values (in shared memory) against a q8_1 image (KAct layout, in shared memory): the reference's
+// row dot, every lane returning the sum.
+__device__ __forceinline__ float dec_row_dot(const uint8_t* row, const uint8_t* act, int n, int lane) {
+    float v = 0.f;
+    for (int kk = lane; kk < n / 32; kk += 32) {
+        Dec d;
+        decode_q2(row, kk, d);
+        v = __fadd_rn(v, partial_layer<kQ2_0>(d, load_act(act + (size_t) kk * kKaBlock)));
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// The k largest logits of l[0..E) in route_warp's order (key descending, lower index first among equal keys), by
+// one warp.  Lane j holds experts j + 32 i packed as (route_key << 32 | ~index), so one unsigned 64-bit comparison
+// orders keys and breaks ties by index (0 marks past E), sorts its C values descending with a bitonic network, then
+// k rounds each take the warp's largest head (xor-butterfly max) and advance the winning lane's list.
+template <int C>
+__device__ __forceinline__ void dec_topk_warp(const float* __restrict__ l, int E, int k, int32_t* s_ids, int lane) {
+    uint64_t v[C];
 #pragma unroll
-        for (int q = 0; q < 4; q++) v[q] = __fadd_rn(v[q], __shfl_xor_sync(0xffffffffu, v[q], o));
+    for (int i = 0; i < C; i++) {
+        const int e = lane + 32 * i;
+        v[i] = e < E ? ((uint64_t) route_key(l[e]) << 32) | (uint64_t) (~(uint32_t) e) : 0ull;
+    }
+#pragma unroll
+    for (int sz = 2; sz <= C; sz <<= 1)
+#pragma unroll
+        for (int j = sz >> 1; j > 0; j >>= 1)
+#pragma unroll
+            for (int i = 0; i < C; i++) {
+                const int q = i ^ j;
+                if (q > i) {
+                    const uint64_t x = v[i], y = v[q];
+                    const bool sw = (i & sz) == 0 ? x < y : x > y;
+                    v[i] = sw ? y : x;
+                    v[q] = sw ? x : y;
+                }
+            }
+    for (int r = 0; r < k; r++) {
+        uint64_t m = v[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint64_t y = __shfl_xor_sync(0xffffffffu, m, o);
+            m = y > m ? y : m;
+        }
+        if (v[0] == m) {  // the winner (values are unique through their index part)
+#pragma unroll
+            for (int i = 0; i + 1 < C; i++) v[i] = v[i + 1];
+            v[C - 1] = 0ull;
+        }
+        if (lane == 0) s_ids[r] = (int32_t) ~(uint32_t) m;
+    }
 }
 
-// route_warp's result computed by a whole CTA of kDecThreads threads (E <= kDecThreads): thread t holds logit t.
-// The order (logit descending, lower index first) comes from a bitonic sort of (logit, index) - partners closer
-// than 32 exchange by shuffle, farther ones through shared memory.  p = exp(l - max) in fp64 is evaluated once per
-// expert; its sum is taken in route_warp's order (lane l adds p[l], p[l + 32], ... in turn, then the xor
-// butterfly), and the weights of the chosen as route_warp forms them, so the two give the same bits.
-__device__ __forceinline__ bool rank_before(float va, int ia, float vb, int ib) {
-    return va > vb || (va == vb && ia < ib);
-}
-
-__device__ __forceinline__ void route_cta(const float* __restrict__ l, int E, int k, int32_t* s_ids, float* s_w) {
-    __shared__ float sv[kDecThreads];
-    __shared__ int si[kDecThreads];
-    __shared__ double sp[kDecThreads];
-    __shared__ float s_red[kDecWarps];
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    float v = t < E ? l[t] : -INFINITY;
-    int ix = t;
-    float m = v;
+// route_warp's softmax terms, by warps 1.. of the CTA while warp 0 ranks: p[e] = exp(l[e] - max) in fp64 and their
+// sum in route_warp's order (lane j adds p[j + 32 i] in i order, then the xor butterfly).  Named barrier 1 joins
+// those warps only.
+__device__ __forceinline__ void dec_softmax_terms(const float* __restrict__ l, int E, double* s_p, float* s_red,
+                                                  double* s_sum) {
+    constexpr int nt = kDecThreads - 32;
+    const int t = (int) threadIdx.x - 32, lane = t & 31, w = t >> 5;
+    float m = -INFINITY;
+    for (int e = t; e < E; e += nt) m = fmaxf(m, l[e]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) s_red[warp] = m;
-    __syncthreads();
+    if (lane == 0) s_red[w] = m;
+    asm volatile("bar.sync 1, %0;" ::"n"(nt) : "memory");
     float mx = s_red[0];
 #pragma unroll
-    for (int i = 1; i < kDecWarps; i++) mx = fmaxf(mx, s_red[i]);
-    if (t < E) sp[t] = exp((double) v - (double) mx);
-    // bitonic sort of (v, ix), final order: rank_before
-    for (int kk = 2; kk <= kDecThreads; kk <<= 1) {
-        for (int j = kk >> 1; j > 0; j >>= 1) {
-            float pv;
-            int pi;
-            if (j >= 32) {
-                __syncthreads();
-                sv[t] = v;
-                si[t] = ix;
-                __syncthreads();
-                pv = sv[t ^ j];
-                pi = si[t ^ j];
-            } else {
-                pv = __shfl_xor_sync(0xffffffffu, v, j);
-                pi = __shfl_xor_sync(0xffffffffu, ix, j);
-            }
-            const bool first = ((t & j) == 0) == ((t & kk) == 0);  // this position keeps the earlier of the two
-            const bool mine_first = rank_before(v, ix, pv, pi);
-            if (first != mine_first) {
-                v = pv;
-                ix = pi;
-            }
-        }
-    }
-    __syncthreads();
-    sv[t] = v;
-    si[t] = ix;
-    __syncthreads();
-    if (warp == 0) {
+    for (int i = 1; i < kDecWarps - 1; i++) mx = fmaxf(mx, s_red[i]);
+    for (int e = t; e < E; e += nt) s_p[e] = exp((double) l[e] - (double) mx);
+    asm volatile("bar.sync 1, %0;" ::"n"(nt) : "memory");
+    if (w == 0) {
         double part = 0.0;
-        for (int e = lane; e < E; e += 32) part += sp[e];
+        for (int e = lane; e < E; e += 32) part += s_p[e];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        const double sum = part;
-        const double pn0 = lane < k ? sp[si[lane]] / sum : 0.0;
-        const double pn1 = 32 + lane < k ? sp[si[32 + lane]] / sum : 0.0;
-        double chosen = 0.0;
-        for (int i = 0; i < k; i++) chosen += __shfl_sync(0xffffffffu, i < 32 ? pn0 : pn1, i & 31);
-        chosen = fmax(chosen, 6.103515625e-05);
-        if (lane < k) {
-            s_ids[lane] = si[lane];
-            s_w[lane] = (float) ((double) (float) pn0 / chosen);
-        }
-        if (32 + lane < k) {
-            s_ids[32 + lane] = si[32 + lane];
-            s_w[32 + lane] = (float) ((double) (float) pn1 / chosen);
-        }
+        if (lane == 0) *s_sum = part;
     }
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+// route_warp's weights for the ranked ids, by one warp: w_i = (float)((double)(float)(p_i / sum) / max(sum of the
+// chosen in rank order, 2^-14)).
+__device__ __forceinline__ void dec_weights(int k, const int32_t* s_ids, const double* s_p, double sum, float* s_w,
+                                            int lane) {
+    const double pn0 = lane < k ? s_p[s_ids[lane]] / sum : 0.0;
+    const double pn1 = 32 + lane < k ? s_p[s_ids[32 + lane]] / sum : 0.0;
+    double chosen = 0.0;
+    for (int i = 0; i < k; i++) chosen += __shfl_sync(0xffffffffu, i < 32 ? pn0 : pn1, i & 31);
+    chosen = fmax(chosen, 6.103515625e-05);
+    if (lane < k) s_w[lane] = (float) ((double) (float) pn0 / chosen);
+    if (32 + lane < k) s_w[32 + lane] = (float) ((double) (float) pn1 / chosen);
+}
 
-__global__ void __launch_bounds__(kDecThreads, 1) decode_layer_kernel(DecodeArgs a) {
+// the range [c n / G, (c + 1) n / G) of this CTA
+__device__ __forceinline__ void dec_range(int n, int& lo, int& hi) {
+    lo = (int) ((int64_t) blockIdx.x * n / gridDim.x);
+    hi = (int) ((int64_t) (blockIdx.x + 1) * n / gridDim.x);
+}
+
+struct DecSmem {
+    float* x;          // [H]
+    uint8_t* xa;       // [H / 32][48] q8_1 image of x (copied from the global table in phase B)
+    uint8_t* router;   // [rr][H] bf16: this CTA's router rows
+    uint8_t* items;    // [nit][64][row bytes over H]: per item its 32 gate rows, then its 32 up rows
+    uint8_t* down;     // [slots][dr][row bytes over F]; the stack's v = MoE(x) + x [H] in the norm
+    float* v;
+    uint8_t* ha;       // [slots * F / 32][48] q8_1 images of h
+    double* p;         // [E] routing exps
+    float* logits;     // [E + 1]
+    float* hv;         // [nit][32] h of this CTA's items
+    int rr, nit, dr;   // per-CTA maxima: router rows, items, down rows
+};
+
+struct DecCounts {
+    int rr, nit, dr;
+};
+SMOE_HD DecCounts dec_counts(int H, int F, int E, int k, int G) {
+    return DecCounts{(E + 1 + G - 1) / G, ((k + 1) * (F / 32) + G - 1) / G, (H + G - 1) / G};
+}
+
+static size_t dec_up(size_t n) { return (n + 127) & ~(size_t) 127; }
+
+size_t decode_smem_bytes(int H, int F, int E, int k, int grid) {
+    const size_t rbh = (size_t) (H / 64) * 18, rbf = (size_t) (F / 64) * 18;
+    const DecCounts c = dec_counts(H, F, E, k, grid);
+    return dec_up((size_t) H * 4) + dec_up((size_t) H / 32 * kKaBlock) + dec_up((size_t) c.rr * H * 2) +
+           dec_up((size_t) c.nit * 64 * rbh) + dec_up(std::max((size_t) (k + 1) * c.dr * rbf, (size_t) H * 4)) +
+           dec_up((size_t) (k + 1) * (F / 32) * kKaBlock) + dec_up((size_t) E * 8) + dec_up((size_t) (E + 1) * 4) +
+           dec_up((size_t) c.nit * 32 * 4) + 128;
+}
+
+__device__ __forceinline__ DecSmem dec_smem(uint8_t* base, int H, int F, int E, int k) {
+    const size_t rbh = (size_t) (H / 64) * 18, rbf = (size_t) (F / 64) * 18;
+    const DecCounts c = dec_counts(H, F, E, k, gridDim.x);
+    auto up = [](size_t n) { return (n + 127) & ~(size_t) 127; };
+    DecSmem s;
+    s.rr = c.rr;
+    s.nit = c.nit;
+    s.dr = c.dr;
+    uint8_t* p = base;
+    s.x = reinterpret_cast<float*>(p);
+    p += up((size_t) H * 4);
+    s.xa = p;
+    p += up((size_t) H / 32 * kKaBlock);
+    s.router = p;
+    p += up((size_t) c.rr * H * 2);
+    s.items = p;
+    p += up((size_t) c.nit * 64 * rbh);
+    s.down = p;
+    s.v = reinterpret_cast<float*>(p);
+    p += up(max((size_t) (k + 1) * c.dr * rbf, (size_t) H * 4));
+    s.ha = p;
+    p += up((size_t) (k + 1) * (F / 32) * kKaBlock);
+    s.p = reinterpret_cast<double*>(p);
+    p += up((size_t) E * 8);
+    s.logits = reinterpret_cast<float*>(p);
+    p += up((size_t) (E + 1) * 4);
+    s.hv = reinterpret_cast<float*>(p);
+    return s;
+}
+
+// The gate and up rows of item `it` (slot it / nb, 32-row block it % nb) of expert e (routed) or of the shared expert.
+__device__ __forceinline__ void dec_stage_item(const DecodeArgs& a, const DecLayer& L, const DecSmem& s, int j, int it,
+                                               int e) {
+    const int nb = a.F / 32;
+    const size_t rbh = (size_t) (a.H / 64) * 18;
+    const int slot = it / nb, blk = it % nb;
+    const int64_t stride = (int64_t) a.F * (int64_t) rbh;
+    const uint8_t* g = slot < a.k ? L.gate + (int64_t) e * stride : L.sgate;
+    const uint8_t* u = slot < a.k ? L.up + (int64_t) e * stride : L.sup;
+    uint8_t* dst = s.items + (size_t) j * 64 * rbh;
+    dec_stage(dst, g + (size_t) blk * 32 * rbh, (uint32_t) (32 * rbh));
+    dec_stage(dst + 32 * rbh, u + (size_t) blk * 32 * rbh, (uint32_t) (32 * rbh));
+}
+
+// a layer's routing-independent rows: this CTA's router rows and its shared-expert items
+__device__ __forceinline__ void dec_stage_static(const DecodeArgs& a, const DecLayer& L, const DecSmem& s) {
+    const int H = a.H;
+    int r0, r1;
+    dec_range(a.E + (a.has_shared ? 1 : 0), r0, r1);
+    for (int r = r0; r < r1; r++) {
+        const uint16_t* src = r < a.E ? L.router + (size_t) r * H : L.ginp;
+        dec_stage(s.router + (size_t) (r - r0) * H * 2, reinterpret_cast<const uint8_t*>(src), (uint32_t) H * 2);
+    }
+    int i0, i1;
+    dec_range((a.k + (a.has_shared ? 1 : 0)) * (a.F / 32), i0, i1);
+    for (int it = i0; it < i1; it++)
+        if (it / (a.F / 32) == a.k) dec_stage_item(a, L, s, it - i0, it, 0);
+}
+
+__global__ void __launch_bounds__(kDecThreads, 1) decode_stack_kernel(const __grid_constant__ DecodeArgs a) {
+    extern __shared__ __align__(128) uint8_t dec_sm[];
     __shared__ int32_t s_ids[kMaxK];
     __shared__ float s_w[kMaxK];
-    __shared__ float s_g[32], s_u[32];
-    __shared__ float s_parts[kDecMaxRows][kMaxK + 1];
-    __shared__ __align__(16) uint8_t s_xa[kDecMaxBlocks * kKaBlock];  // this CTA's copy of the activation image
+    __shared__ float s_red[kDecWarps];
+    __shared__ float s_parts[kDecMaxDownRows][kDecMaxSlots + 1];
+    __shared__ double s_part[8];
+    __shared__ double s_den;
+    __shared__ float s_sig;
+    __shared__ double s_sum;
+    __shared__ __align__(8) uint64_t s_mb[2];  // bulk copies: [0] this CTA's routed items, [1] its down rows
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int gw = blockIdx.x * kDecWarps + warp, nw = gridDim.x * kDecWarps;
     const int H = a.H, F = a.F, E = a.E, K = a.k;
     const int nslot = K + (a.has_shared ? 1 : 0);
-    const int nb = F / 32;
-    const int rbg = (H / 64) * 18;
+    const int nb = F / 32, nbx = H / 32;
+    const size_t rbh = (size_t) (H / 64) * 18, rbf = (size_t) (F / 64) * 18;
+    const int64_t d_stride = (int64_t) H * (int64_t) rbf;
+    const DecSmem s = dec_smem(dec_sm, H, F, E, K);
+    int r0, r1, i0, i1, j0, j1, x0, x1;
+    dec_range(E + (a.has_shared ? 1 : 0), r0, r1);
+    dec_range(nslot * nb, i0, i1);
+    dec_range(H, j0, j1);
+    dec_range(nbx, x0, x1);
+    const int nj = j1 - j0;
+    bool ok = true;
+    unsigned nbar = 0;  // grid barriers passed in this launch
 
-    // gate and up rows of one 32-row block of slot s, SwiGLU, the q8_1 block of h (warp w: rows 2w, 2w + 1)
-    auto gate_up_item = [&](int s, int b, const uint8_t* gb, const uint8_t* ub) {
-        const uint8_t* rows[4];
+    uint32_t ph[2] = {0u, 0u};  // phases of s_mb[0] / s_mb[1] completed so far
+    bool pend[2] = {false, false};  // a phase with copies in flight that nobody has waited for
+    if (threadIdx.x == 0) {
+        mbar_init(&s_mb[0], 1);
+        mbar_init(&s_mb[1], 1);
+        fence_mbar_init();
+    }
+    for (int i = threadIdx.x; i < H; i += kDecThreads) s.x[i] = a.x[i];
+    dec_stage_static(a, a.layers[0], s);
+    cp_commit();
+
+    for (int l = 0; l < a.n_layers && ok; l++) {
+        const DecLayer& L = a.layers[l];
+        // ---------------- phase A: router rows, this CTA's blocks of x's q8_1 image ----------------
+        cp_wait<0>();
+        __syncthreads();
+        if (warp < r1 - r0) {  // one router row per warp: fp64 sum of bf16(x) * w, rounded once
+            const uint16_t* wr = reinterpret_cast<const uint16_t*>(s.router + (size_t) warp * H * 2);
+            double acc = 0.0;
+            for (int c = lane * 8; c < H; c += 256) {
+                const uint4 wv = *reinterpret_cast<const uint4*>(wr + c);
+                const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-        for (int q = 0; q < 4; q++) rows[q] = (q < 2 ? gb : ub) + (size_t) (b * 32 + 2 * warp + (q & 1)) * rbg;
-        float v[4];
-        row_dot4_warp(rows, s_xa, H, lane, v);
-        if (lane == 0) {
-            s_g[2 * warp] = v[0];
-            s_g[2 * warp + 1] = v[1];
-            s_u[2 * warp] = v[2];
-            s_u[2 * warp + 1] = v[3];
+                for (int q = 0; q < 4; q++) {
+                    acc = fma((double) bf16_round(s.x[c + 2 * q]), (double) __uint_as_float(wu[q] << 16), acc);
+                    acc = fma((double) bf16_round(s.x[c + 2 * q + 1]), (double) __uint_as_float(wu[q] & 0xFFFF0000u), acc);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0) a.logits[r0 + warp] = (float) acc;
+        } else if (warp >= kDecWarps - (x1 - x0)) {
+            const int b = x0 + (warp - (kDecWarps - (x1 - x0)));
+            quant_ka_warp(s.x[b * 32 + lane], a.xa + (size_t) b * kKaBlock, lane, true);
+        }
+        if (a.xq && blockIdx.x == 0)
+            for (int b = warp; b < nbx; b += kDecWarps) quant_q8_1_warp(s.x[b * 32 + lane], a.xq + (size_t) b * kQ8Block, lane);
+        if (!(ok = dec_grid_sync(a.bar, ++nbar))) break;
+
+        // ---------------- phase B: routing, this CTA's items of h ----------------
+        // the logits and x's image in one copy each through L2 (other CTAs wrote them; this SM's L1 may hold the
+        // previous layer's)
+        dec_stage(reinterpret_cast<uint8_t*>(s.logits), reinterpret_cast<const uint8_t*>(a.logits), (uint32_t) (E + 1) * 4);
+        dec_stage(s.xa, a.xa, (uint32_t) nbx * kKaBlock);
+        cp_commit();
+        cp_wait<0>();
+        __syncthreads();
+        // warp 0 ranks; the others form the softmax terms and the shared gate meanwhile
+        if (warp == 0) {
+            dec_topk_warp<kDecMaxExperts / 32>(s.logits, E, K, s_ids, lane);
+        } else {
+            if (threadIdx.x == 32 && a.has_shared) {
+                const float e = (float) exp(-(double) s.logits[E]);
+                s_sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+            }
+            dec_softmax_terms(s.logits, E, s.p, s_red, &s_sum);
         }
         __syncthreads();
-        if (warp == 0)
-            quant_ka_warp(silu_mul(s_g[lane], s_u[lane]), a.ha + ((size_t) s * nb + b) * kKaBlock, lane, true);
+        // this CTA's routed items and its down rows of every slot: bulk copies issued by warp 0's lanes, completing on
+        // s_mb[0] / s_mb[1], where the planes allow them (16-byte aligned); cp.async otherwise
+        const bool items_bulk = (L.bulk & 1) != 0, down_bulk = (L.bulk & 2) != 0;
+        const int n_routed = max(0, min(i1, K * nb) - i0);  // the items [i0, i0 + n_routed) are routed slots'
+        if (warp == 0 && (items_bulk || down_bulk)) {
+            fence_proxy_async();  // this CTA's earlier reads of the buffers before the copies overwrite them
+            if (lane == 0) {
+                if (items_bulk) mbar_expect_tx(&s_mb[0], (uint32_t) (n_routed * 64 * rbh));
+                if (down_bulk) mbar_expect_tx(&s_mb[1], (uint32_t) (nslot * nj * rbf));
+            }
+            __syncwarp();
+            const int n_ic = items_bulk ? 2 * n_routed : 0, n_dc = down_bulk && nj > 0 ? nslot : 0;
+            const int64_t stride = (int64_t) F * (int64_t) rbh;
+            for (int c = lane; c < n_ic + n_dc; c += 32) {
+                if (c < n_ic) {  // item i0 + c / 2: its 32 gate (c even) or up (c odd) rows
+                    const int it = i0 + c / 2, slot = it / nb, blk = it % nb;
+                    const int64_t off = (int64_t) s_ids[slot] * stride + (int64_t) blk * 32 * (int64_t) rbh;
+                    bulk_g2s(s.items + (size_t) (c / 2) * 64 * rbh + (size_t) (c & 1) * 32 * rbh,
+                             ((c & 1) ? L.up : L.gate) + off, (uint32_t) (32 * rbh), &s_mb[0]);
+                } else {
+                    const int sl = c - n_ic;
+                    const uint8_t* plane = sl < K ? L.down + (int64_t) s_ids[sl] * d_stride : L.sdown;
+                    bulk_g2s(s.down + (size_t) sl * s.dr * rbf, plane + (size_t) j0 * rbf, (uint32_t) (nj * rbf),
+                             &s_mb[1]);
+                }
+            }
+        }
+        if (!items_bulk)
+            for (int it = i0; it < i0 + n_routed; it++) dec_stage_item(a, L, s, it - i0, it, s_ids[it / nb]);
+        if (!down_bulk)
+            for (int sl = 0; sl < nslot && nj > 0; sl++) {
+                const uint8_t* plane = sl < K ? L.down + (int64_t) s_ids[sl] * d_stride : L.sdown;
+                dec_stage(s.down + (size_t) sl * s.dr * rbf, plane + (size_t) j0 * rbf, (uint32_t) (nj * rbf));
+            }
+        cp_commit();
+        // the routing weights while the rows arrive
+        if (warp == 1) dec_weights(K, s_ids, s.p, s_sum, s_w, lane);
         __syncthreads();
-    };
+        if (blockIdx.x == 0 && threadIdx.x < K) {
+            if (a.ids) a.ids[threadIdx.x] = s_ids[threadIdx.x];
+            if (a.w) a.w[threadIdx.x] = s_w[threadIdx.x];
+        }
+        if (a.sh_logit && blockIdx.x == 0 && threadIdx.x == 0 && a.has_shared) a.sh_logit[0] = s.logits[E];
+        pend[0] = items_bulk;
+        pend[1] = down_bulk;
+        if (!items_bulk) cp_wait<0>();
+        if (!(ok = __syncthreads_and(!items_bulk || mbar_wait_bounded(&s_mb[0], ph[0] & 1u, kWaitLimitNs)) != 0)) {
+            if (threadIdx.x == 0) atomicOr(&g_smoe_status, kDevTimeout);
+            break;
+        }
+        if (items_bulk) ph[0]++, pend[0] = false;
+        for (int u = warp; u < (i1 - i0) * 32; u += kDecWarps) {  // one row pair per warp
+            const int j = u / 32, pr = u % 32;
+            const uint8_t* item = s.items + (size_t) j * 64 * rbh;
+            const float g = dec_row_dot(item + (size_t) pr * rbh, s.xa, H, lane);
+            const float uu = dec_row_dot(item + (size_t) (32 + pr) * rbh, s.xa, H, lane);
+            if (lane == 0) s.hv[u] = silu_mul(g, uu);
+        }
+        __syncthreads();
+        if (warp < i1 - i0) quant_ka_warp(s.hv[warp * 32 + lane], a.hq + (size_t) (i0 + warp) * kKaBlock, lane, true);
+        if (!(ok = dec_grid_sync(a.bar, ++nbar))) break;
 
-    // ---- phase 0: the activation image (every CTA, in shared memory), router logits (fp64), and the shared
-    // expert's gate/up, which does not depend on the routing ----
-    const int router_rows = E + (a.has_shared ? 1 : 0);
-    for (int r = gw; r < router_rows; r += nw) {
-        const uint16_t* wr = r < E ? a.router + (size_t) r * H : a.ginp;
-        double acc = 0.0;
-#pragma unroll 8
-        for (int c = lane * 8; c < H; c += 256) {
-            const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + c));
-            const float4 x0 = __ldg(reinterpret_cast<const float4*>(a.x + c));
-            const float4 x1 = __ldg(reinterpret_cast<const float4*>(a.x + c + 4));
-            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+        // ---------------- phase C: down rows, combine (and the stack's add + RMSNorm) ----------------
+        dec_stage(s.ha, a.hq, (uint32_t) (nslot * nb) * kKaBlock);  // every slot's h image, through L2
+        cp_commit();
+        if (l + 1 < a.n_layers) dec_stage_static(a, a.layers[l + 1], s);  // the next layer's static rows
+        cp_commit();
+        cp_wait<1>();  // h (and the down rows when they came by cp.async)
+        if (!(ok = __syncthreads_and(!down_bulk || mbar_wait_bounded(&s_mb[1], ph[1] & 1u, kWaitLimitNs)) != 0)) {
+            if (threadIdx.x == 0) atomicOr(&g_smoe_status, kDevTimeout);
+            break;
+        }
+        if (down_bulk) ph[1]++, pend[1] = false;
+        const int n_dots = nj * nslot;
+        if (F <= 512) {  // one half-warp per dot: at most 16 partials, the xor-16 level would add zeros
+            const int hl = lane & 15, half = lane >> 4;
+            for (int u2 = warp; 2 * u2 < n_dots; u2 += kDecWarps) {
+                const int u = 2 * u2 + half;
+                const bool valid = u < n_dots;
+                const int jl = valid ? u / nslot : 0, sl = valid ? u % nslot : 0;
+                float v = 0.f;
+                if (valid && hl < nb) {
+                    Dec d;
+                    decode_q2(s.down + ((size_t) sl * s.dr + jl) * rbf, hl, d);
+                    v = partial_layer<kQ2_0>(d, load_act(s.ha + ((size_t) sl * nb + hl) * kKaBlock));
+                }
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                acc = fma((double) bf16_round(xv[2 * q]), (double) __uint_as_float(wu[q] << 16), acc);
-                acc = fma((double) bf16_round(xv[2 * q + 1]), (double) __uint_as_float(wu[q] & 0xFFFF0000u), acc);
+                for (int o = 8; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+                if (valid && hl == 0) s_parts[jl][sl] = v;
+            }
+        } else {  // one warp per dot
+            for (int u = warp; u < n_dots; u += kDecWarps) {
+                const int jl = u / nslot, sl = u % nslot;
+                const float v = dec_row_dot(s.down + ((size_t) sl * s.dr + jl) * rbf, s.ha + (size_t) sl * nb * kKaBlock,
+                                            F, lane);
+                if (lane == 0) s_parts[jl][sl] = v;
             }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) {
-            if (r < E) a.logits[r] = (float) acc;
-            else a.sh_logit[0] = (float) acc;
-        }
-    }
-    // the activation image of this CTA (x is read from L2 by every CTA: all loads first)
-    {
-        float xi[kDecMaxBlocks / kDecWarps];
-#pragma unroll
-        for (int i = 0; i < kDecMaxBlocks / kDecWarps; i++) {
-            const int b = warp + kDecWarps * i;
-            xi[i] = b < H / 32 ? a.x[b * 32 + lane] : 0.f;
-        }
-#pragma unroll
-        for (int i = 0; i < kDecMaxBlocks / kDecWarps; i++) {
-            const int b = warp + kDecWarps * i;
-            if (b < H / 32) {
-                quant_ka_warp(xi[i], s_xa + (size_t) b * kKaBlock, lane, true);
-                if (a.xq && blockIdx.x == 0) quant_q8_1_warp(xi[i], a.xq + (size_t) b * kQ8Block, lane);
+        __syncthreads();
+        if ((int) threadIdx.x < nj) {
+            const int jl = threadIdx.x, j = j0 + jl;
+            double acc = 0.0;
+            for (int i = 0; i < K; i++) {
+                acc += (double) s_w[i] * (double) s_parts[jl][i];
+                if (a.parts) a.parts[(size_t) i * H + j] = s_parts[jl][i];
             }
-        }
-    }
-    __syncthreads();
-    // CTAs past the router rows take the shared expert's blocks (if there are enough CTAs; else phase 1 does)
-    const int r0 = (router_rows + kDecWarps - 1) / kDecWarps;
-    const bool shared_early = a.has_shared && (int) gridDim.x > r0;
-    if (shared_early)
-        for (int it = (int) blockIdx.x - r0; it >= 0 && it < nb; it += (int) gridDim.x - r0)
-            gate_up_item(K, it, a.sgate.base, a.sup.base);
-    if (!grid_barrier(a.bar, 1)) return;
-
-    // ---- phase 1: routing (every CTA), routed gate/up + SwiGLU + q8_1 per (slot, 32-row block) ----
-    route_cta(a.logits, E, K, s_ids, s_w);
-    __syncthreads();
-    if (blockIdx.x == 0)
-        for (int i = threadIdx.x; i < K; i += blockDim.x) {
-            a.ids[i] = s_ids[i];
-            a.w[i] = s_w[i];
-        }
-    // start this CTA's phase-2 down rows on their way to L2
-    const int rows_per = (H + gridDim.x - 1) / gridDim.x;
-    const int j0 = blockIdx.x * rows_per, nj = max(0, min(rows_per, H - j0));
-    const int rbd = (F / 64) * 18;
-    for (int u = threadIdx.x; u < nslot * nj; u += blockDim.x) {
-        const int s = u % nslot, jl = u / nslot;
-        const uint8_t* row = (s >= K ? a.sdown.base : a.down.base + (int64_t) s_ids[s] * a.down.expert_stride) +
-                             (size_t) (j0 + jl) * rbd;
-        for (int off = 0; off < rbd; off += 128) prefetch_l2(row + off);
-    }
-    const int n_items = (shared_early ? K : nslot) * nb;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int s = item / nb, b = item % nb;
-        const bool sh = s >= K;
-        gate_up_item(s, b, sh ? a.sgate.base : a.gate.base + (int64_t) s_ids[s] * a.gate.expert_stride,
-                     sh ? a.sup.base : a.up.base + (int64_t) s_ids[s] * a.up.expert_stride);
-    }
-    if (!grid_barrier(a.bar, 2)) return;
-
-    // ---- phase 2: down dots by output row range, then the combine of each row ----
-    const int hl = lane & 15, half = lane >> 4;
-    const int n_dots = nj * nslot;
-    constexpr int kBatch = 3;  // dots per half-warp with their loads in flight together
-    for (int u2 = warp; 2 * u2 < n_dots; u2 += kDecWarps * kBatch) {  // warp-uniform trip count
-        Dec d[kBatch];
-        ActRegs ar[kBatch];
-        bool act[kBatch];
-        int jl[kBatch], sl[kBatch];
-#pragma unroll
-        for (int i = 0; i < kBatch; i++) {
-            const int u = 2 * (u2 + i * kDecWarps) + half;
-            const bool valid = u < n_dots;
-            jl[i] = valid ? u / nslot : 0;
-            sl[i] = valid ? u % nslot : 0;
-            act[i] = valid && hl < F / 32;  // partial hl of this dot (lanes past the partials hold zero)
-            if (act[i]) {
-                const uint8_t* row = (sl[i] >= K ? a.sdown.base
-                                                 : a.down.base + (int64_t) s_ids[sl[i]] * a.down.expert_stride) +
-                                     (size_t) (j0 + jl[i]) * rbd;
-                decode_q2_global(row, hl, d[i]);
-                ar[i] = load_act(a.ha + ((size_t) sl[i] * nb + hl) * kKaBlock);
+            if (a.has_shared) {
+                const float shv = __fmul_rn(s_parts[jl][K], s_sig);
+                if (a.shared_out) a.shared_out[j] = shv;
+                acc += (double) shv;
             }
+            const float y = (float) acc;
+            if (a.norm) a.vbuf[j] = __fadd_rn(y, s.x[j]);
+            else a.out[j] = y;
         }
+        if (!a.norm) continue;
+        if (!(ok = dec_grid_sync(a.bar, ++nbar))) break;
+        dec_stage(reinterpret_cast<uint8_t*>(s.v), reinterpret_cast<const uint8_t*>(a.vbuf), (uint32_t) H * 4);
+        cp_commit();
+        cp_wait<0>();
+        __syncthreads();
+        // x = rms_norm(v): the RMSNorm kernel's tree (256 threads: column c on thread c % 256, fma in column
+        // order, xor butterfly per warp, the eight warp sums in order), in every CTA
+        if (threadIdx.x < 256) {
+            double ss = 0.0;
+            for (int c = threadIdx.x; c < H; c += 256) {
+                const float v = s.v[c];
+                ss = fma((double) v, (double) v, ss);
+            }
 #pragma unroll
-        for (int i = 0; i < kBatch; i++) {
-            float v = act[i] ? partial_layer<kQ2_0>(d[i], ar[i]) : 0.f;
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-            const int u = 2 * (u2 + i * kDecWarps) + half;
-            if (u < n_dots && hl == 0) s_parts[jl[i]][sl[i]] = v;
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (lane == 0) s_part[warp] = ss;
         }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double t = 0.0;
+            for (int i = 0; i < 8; i++) t += s_part[i];
+            s_den = sqrt(t / (double) H + (double) a.eps);
+        }
+        __syncthreads();
+        const double den = s_den;
+        for (int c = threadIdx.x; c < H; c += kDecThreads) {
+            const double v = (double) s.v[c];
+            const float xn = (float) ((v / den) * (L.norm_w ? (double) L.norm_w[c] : 1.0));
+            s.x[c] = xn;
+            if (l + 1 == a.n_layers && blockIdx.x == 0) a.out[c] = xn;
+        }
+        // the next layer's phase A reads s.x after its first __syncthreads; vbuf is next written in that layer's
+        // phase C, two grid barriers after every CTA has read it here
     }
-    __syncthreads();
-    if ((int) threadIdx.x < nj) {
-        const int jl = threadIdx.x, j = j0 + jl;
-        double acc = 0.0;
-        for (int i = 0; i < K; i++) {
-            acc += (double) s_w[i] * (double) s_parts[jl][i];
-            if (a.parts) a.parts[(size_t) i * H + j] = s_parts[jl][i];
-        }
-        if (a.has_shared) {
-            const float e = (float) exp(-(double) a.sh_logit[0]);
-            const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
-            const float shv = __fmul_rn(s_parts[jl][K], sig);
-            if (a.shared_out) a.shared_out[j] = shv;
-            acc += (double) shv;
-        }
-        a.out[j] = (float) acc;
-    }
+    cp_wait<0>();
+    if (threadIdx.x == 0)  // a CTA that gave up drains its bulk copies in flight (bounded) before it exits
+        for (int b = 0; b < 2; b++)
+            if (pend[b]) mbar_wait_bounded(&s_mb[b], ph[b] & 1u, kWaitLimitNs);
 }
 
-// The fused path needs every matrix in Q2_0, n_embd a multiple of 256 (the router's 8-value lanes), at most 512
-// intermediate values (one half-warp per down dot) and at most 512 experts (one per thread in the routing).
+// Every matrix Q2_0; n_embd a multiple of 512 (gate/up rows of whole 16-byte pieces), n_ff a multiple of 128 (down
+// rows of whole 4-byte words) and at most 1024, at most 1024 experts; the per-CTA work must fit the warps and the
+// shared-memory tables.
 bool decode_qualifies(int H, int F, int E, int k, int gu_type, int d_type, int has_shared, int sg, int su, int sd) {
-    const bool q2 = gu_type == kQ2_0 && d_type == kQ2_0 &&
-                    (!has_shared || (sg == kQ2_0 && su == kQ2_0 && sd == kQ2_0));
-    return q2 && H % 256 == 0 && F % 32 == 0 && F <= 512 && E <= kDecThreads && k <= kMaxK && k <= E;
-}
-
-cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t s) {
-    cudaError_t e = cudaMemsetAsync(a.bar, 0, 2 * sizeof(unsigned), s);
-    if (e != cudaSuccess) return e;
+    const bool q2 = gu_type == kQ2_0 && d_type == kQ2_0 && (!has_shared || (sg == kQ2_0 && su == kQ2_0 && sd == kQ2_0));
     int dev = 0, nsm = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    if ((a.H + nsm - 1) / nsm > kDecMaxRows) return cudaErrorInvalidValue;
+    const DecCounts c = dec_counts(H, F, E, k, nsm);
+    const int xq = (H / 32 + nsm - 1) / nsm;
+    const bool fits = c.rr + xq <= kDecWarps && c.nit <= kDecWarps && c.dr <= kDecMaxDownRows && H <= 4096 &&
+                      F <= 1024 && decode_smem_bytes(H, F, E, k, nsm) <= 220 * 1024;
+    return q2 && fits && H % 512 == 0 && F % 128 == 0 && E <= kDecMaxExperts && k <= kMaxK && k <= E;
+}
+
+size_t decode_scratch_bytes(int H, int F, int E, int k) {
+    auto up = [](size_t n) { return (n + 255) / 256 * 256; };
+    return up((size_t) (E + 1) * 4) + up((size_t) H / 32 * kKaBlock) + up((size_t) (k + 1) * (F / 32) * kKaBlock) +
+           up((size_t) H * 4) + 256;
+}
+
+cudaError_t launch_decode(const DecodeHost& h, cudaStream_t s) {
+    int dev = 0, nsm = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    if (h.n_layers < 1 || h.n_layers > kDecodeMaxLayers || (!h.norm && h.n_layers != 1)) return cudaErrorInvalidValue;
+    DecodeArgs a{};
+    for (int l = 0; l < h.n_layers; l++) {
+        const smoe_layer& L = h.layers[l];
+        auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+        const size_t rbf = (size_t) (L.n_ff / 64) * 18;
+        const int bulk = (a16(L.gate) && a16(L.up) ? 1 : 0) |
+                         (rbf % 16 == 0 && a16(L.down) && (!L.has_shared || a16(L.sdown)) ? 2 : 0);
+        a.layers[l] = DecLayer{L.router, L.has_shared ? L.gate_inp_shexp : nullptr, L.gate, L.up, L.down,
+                               L.sgate, L.sup, L.sdown, h.norm_w ? h.norm_w[l] : nullptr, bulk};
+    }
+    const smoe_layer& L0 = h.layers[0];
+    a.n_layers = h.n_layers;
+    a.H = L0.n_embd;
+    a.F = L0.n_ff;
+    a.E = L0.n_expert;
+    a.k = L0.k;
+    a.has_shared = L0.has_shared ? 1 : 0;
+    a.norm = h.norm;
+    a.eps = h.eps;
+    a.x = h.x;
+    a.out = h.out;
+    auto up = [](size_t n) { return (n + 255) / 256 * 256; };
+    uint8_t* p = static_cast<uint8_t*>(h.scratch);
+    a.logits = reinterpret_cast<float*>(p);
+    p += up((size_t) (a.E + 1) * 4);
+    a.xa = p;
+    p += up((size_t) a.H / 32 * kKaBlock);
+    a.hq = p;
+    p += up((size_t) (a.k + 1) * (a.F / 32) * kKaBlock);
+    a.vbuf = reinterpret_cast<float*>(p);
+    p += up((size_t) a.H * 4);
+    a.bar = reinterpret_cast<unsigned*>(p);
+    a.ids = h.ids;
+    a.w = h.w;
+    a.sh_logit = h.sh_logit;
+    a.xq = h.xq;
+    a.parts = h.parts;
+    a.shared_out = h.shared_out;
+    const size_t smem = decode_smem_bytes(a.H, a.F, a.E, a.k, nsm);
+    cudaError_t e = cudaMemsetAsync(a.bar, 0, sizeof(unsigned), s);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(decode_stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned) nsm);
     cfg.blockDim = dim3(kDecThreads);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, decode_layer_kernel, a);
+    return cudaLaunchKernelEx(&cfg, decode_stack_kernel, a);
 }
 
 }  // namespace smoe

@@ -5,6 +5,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "../../include/smoe.h"
+
 namespace smoe {
 
 constexpr int kRouterTokTile = 16;  // tokens per CTA in the router GEMV (x staged as bf16: 16 x n_embd x 2 bytes)
@@ -206,10 +208,28 @@ cudaError_t launch_s2_hit_add(float* parts, const float* hit_out, const int32_t*
 cudaError_t launch_add_rms_norm(float* x, const float* residual, const float* w, int64_t rows, int64_t cols,
                                 float eps, cudaStream_t s);
 
-// ---- decode.cu ---- (one token through the whole block in one cooperative launch)
-struct DecodeArgs;
+// ---- decode.cu ---- (one token through one layer, or through a stack of layers, in one cooperative launch)
+constexpr int kDecodeMaxLayers = 48;  // layers per launch (the table travels in the launch parameters)
+struct DecodeHost {
+    const smoe_layer* layers;     // n_layers layers of one geometry
+    int n_layers;
+    const float* const* norm_w;   // per-layer RMSNorm weights (null: unit)
+    int norm;                     // 1: x = rms_norm(MoE(x) + x) after every layer; 0: one layer, out = MoE(x)
+    float eps;
+    const float* x;
+    float* out;
+    void* scratch;                // decode_scratch_bytes
+    int32_t* ids;                 // single-layer trace (all may be null)
+    float* w;
+    float* sh_logit;
+    uint8_t* xq;
+    float* parts;
+    float* shared_out;
+};
 bool decode_qualifies(int H, int F, int E, int k, int gu_type, int d_type, int has_shared, int sg, int su, int sd);
-cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t s);
+size_t decode_scratch_bytes(int H, int F, int E, int k);
+// the router logits [E + 1] at the start of the scratch (the last one the shared gate)
+cudaError_t launch_decode(const DecodeHost& h, cudaStream_t s);
 
 // ---- ep.cu ---- (expert parallelism over peer memory)
 size_t ep_arena_bytes(int H, int k, int max_tokens, int world);

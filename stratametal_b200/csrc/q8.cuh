@@ -68,6 +68,53 @@ __device__ __forceinline__ void quant_ka_warp(float xi, uint8_t* __restrict__ bl
     if (lane == 9) reinterpret_cast<int*>(blk48)[9] = 0x4B400000 - qs;
 }
 
+// quant_ka_warp for N blocks at once (blocks whose bit in `valid` is clear are skipped): the same arithmetic per
+// block, with the N dependency chains interleaved so their shuffle and division latencies overlap.
+template <int N>
+__device__ __forceinline__ void quant_ka_warp_n(const float (&xi)[N], uint8_t* const (&blk)[N], unsigned valid, int lane,
+                                                bool q2_layout) {
+    float amax[N], d[N];
+    int q[N], qs[N];
+#pragma unroll
+    for (int i = 0; i < N; i++) amax[i] = fabsf(xi[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < N; i++) amax[i] = fmaxf(amax[i], __shfl_xor_sync(0xffffffffu, amax[i], o));
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+        d[i] = __fdiv_rn(amax[i], 127.f);
+        if (fabsf(d[i]) > 65504.f) d[i] = copysignf(65504.f, d[i]);
+        q[i] = 0;
+        if (amax[i] != 0.f) {
+            float r = roundf(__fdiv_rn(xi[i], d[i]));
+            r = fminf(fmaxf(r, -127.f), 127.f);
+            q[i] = (int) r;
+        }
+        qs[i] = q[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < N; i++) qs[i] += __shfl_xor_sync(0xffffffffu, qs[i], o);
+    const int L = lane & 7;
+    const int src0 = q2_layout ? 16 * (L >> 2) + (L & 3) : 4 * L;
+    const int stride = q2_layout ? 4 : 1;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            const int qb = __shfl_sync(0xffffffffu, q[i], src0 + b * stride);
+            word |= ((uint32_t) qb & 0xFFu) << (8 * b);
+        }
+        if (!((valid >> i) & 1u)) continue;
+        if (lane < 8) reinterpret_cast<uint32_t*>(blk[i])[lane] = word;
+        if (lane == 8) reinterpret_cast<float*>(blk[i])[8] = f16_to_f32(f16_bits(d[i]));
+        if (lane == 9) reinterpret_cast<int*>(blk[i])[9] = 0x4B400000 - qs[i];
+    }
+}
+
 // silu(g) * u (iq.metal:630-663).  exp is taken in fp64 and rounded to f32: that is the correctly rounded
 // expf, which the host reference's libm expf returns on all but a vanishing fraction of inputs.
 __device__ __forceinline__ float silu_mul(float g, float u) {

@@ -155,3 +155,41 @@ def test_fused_single_token_equals_simt(cuda, shared):
     assert np.array_equal(ia, ib) and np.array_equal(bits(wa), bits(wb))
     assert np.array_equal(bits(pa), bits(pb))
     assert np.array_equal(bits(a), bits(b))
+
+
+@pytest.mark.parametrize("router", ["pairs", "zero"])
+def test_fused_single_token_ties(cuda, router):
+    # equal logits: the fused kernel's ranking keeps the lower expert index first, as the router kernel does
+    import ctypes as C
+
+    from stratametal_b200 import _lib
+    spec = synth.LayerSpec(n_embd=512, n_ff=128, n_expert=512, k=10, seed=52)
+    lay = synth.make_layer(spec, 0, cuda)
+    r = lay.tensors["ffn_gate_inp.weight"]
+    if router == "pairs":  # experts 2 i and 2 i + 1 share a router row
+        r.view(256, 2, -1)[:, 1].copy_(r.view(256, 2, -1)[:, 0])
+    else:
+        r.zero_()
+    x = synth.make_x(6, 1, 512, cuda)
+    outs = []
+    try:
+        for path in (3, 1):
+            api.set_expert_path(path)
+            m = api.MoeLayer(lay, 1, cuda)
+            assert _lib.lib().smoe_expert_path_for(C.byref(m.c), 1) == path
+            tr = m.make_trace(1)
+            api.device_status(clear=True)
+            o = m.forward(x, None, tr)
+            torch.cuda.synchronize()
+            assert api.device_status() == 0
+            outs.append((o.cpu().numpy(), tr.ids.cpu().numpy(), tr.weights.cpu().numpy()))
+    finally:
+        api.set_expert_path(0)
+    (a, ia, wa), (b, ib, wb) = outs
+    ids = ia.reshape(-1)
+    if router == "zero":
+        assert list(ids) == list(range(10))
+    else:  # both experts of a tied pair, the even one first
+        assert all(ids[i] % 2 == 0 and ids[i + 1] == ids[i] + 1 for i in range(0, 10, 2))
+    assert np.array_equal(ia, ib) and np.array_equal(bits(wa), bits(wb))
+    assert np.array_equal(bits(a), bits(b))
