@@ -182,31 +182,81 @@ __device__ __forceinline__ void dec_topk_warp(const float* __restrict__ l, int E
     }
 }
 
-// route_warp's softmax terms, by warps 1.. of the CTA while warp 0 ranks: p[e] = exp(l[e] - max) in fp64 and their
-// sum in route_warp's order (lane j adds p[j + 32 i] in i order, then the xor butterfly).  Named barrier 1 joins
-// those warps only.
-__device__ __forceinline__ void dec_softmax_terms(const float* __restrict__ l, int E, double* s_p, float* s_red,
-                                                  double* s_sum) {
-    constexpr int nt = kDecThreads - 32;
-    const int t = (int) threadIdx.x - 32, lane = t & 31, w = t >> 5;
-    float m = -INFINITY;
-    for (int e = t; e < E; e += nt) m = fmaxf(m, l[e]);
+// Routing by the whole CTA in three short steps (then `dec_rank_candidates` and `dec_weights`):
+//   1. thread t packs expert e = 16 (t & 31) + (t >> 5) (warp w holds the experts e = w mod 16, so experts of
+//      similar index, which popularity skews alike, spread over the warps): v = route_key << 32 | ~e; each warp
+//      finds its largest v and its largest logit (fmaxf, route_warp's max).
+//   2. T = the k-th largest of the sixteen warp maxima is at most the k-th largest key overall, so every key of the
+//      top k is >= T; a key is a candidate when fewer than k warp maxima exceed it.  Candidates take slots in
+//      s_cand (up to kDecMaxCand); p[e] = exp(l[e] - max) in fp64.
+//   3. (dec_rank_candidates) one warp ranks the candidates by counting the larger ones; with more than
+//      kDecMaxCand candidates, or k above the number of non-empty warps, dec_topk_warp ranks all keys instead.
+// The result is route_warp's: key descending, lower index first among equal keys.
+constexpr int kDecMaxCand = 64;
+
+__device__ __forceinline__ void dec_route_step1(const float* __restrict__ l, int E, uint64_t& v, uint64_t* s_gmax,
+                                                float* s_fmax) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int e = 16 * lane + w;
+    const float x = e < E ? l[e] : -INFINITY;
+    v = e < E ? ((uint64_t) route_key(x) << 32) | (uint64_t) (~(uint32_t) e) : 0ull;
+    uint64_t g = v;
+    float m = x;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) s_red[w] = m;
-    asm volatile("bar.sync 1, %0;" ::"n"(nt) : "memory");
-    float mx = s_red[0];
-#pragma unroll
-    for (int i = 1; i < kDecWarps - 1; i++) mx = fmaxf(mx, s_red[i]);
-    for (int e = t; e < E; e += nt) s_p[e] = exp((double) l[e] - (double) mx);
-    asm volatile("bar.sync 1, %0;" ::"n"(nt) : "memory");
-    if (w == 0) {
-        double part = 0.0;
-        for (int e = lane; e < E; e += 32) part += s_p[e];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        if (lane == 0) *s_sum = part;
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t y = __shfl_xor_sync(0xffffffffu, g, o);
+        g = y > g ? y : g;
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     }
+    if (lane == 0) {
+        s_gmax[w] = g;
+        s_fmax[w] = m;
+    }
+}
+
+__device__ __forceinline__ void dec_route_step2(const float* __restrict__ l, int E, int k, uint64_t v,
+                                                const uint64_t* s_gmax, const float* s_fmax, uint64_t* s_cand,
+                                                int* s_cnt, double* s_p) {
+    int above = 0;
+#pragma unroll
+    for (int w = 0; w < kDecWarps; w++) above += s_gmax[w] > v ? 1 : 0;
+    if (v != 0ull && above < k) {
+        const int slot = atomicAdd(s_cnt, 1);
+        if (slot < kDecMaxCand) s_cand[slot] = v;
+    }
+    float mx = s_fmax[0];
+#pragma unroll
+    for (int i = 1; i < kDecWarps; i++) mx = fmaxf(mx, s_fmax[i]);
+    const int t = threadIdx.x;
+    if (t < E) s_p[t] = exp((double) l[t] - (double) mx);
+}
+
+// step 3, by one warp: candidate c's rank is the number of larger candidates (values are unique through their
+// index part)
+__device__ __forceinline__ void dec_rank_candidates(const float* __restrict__ l, int E, int k, int n,
+                                                    const uint64_t* s_cand, int32_t* s_ids, int lane) {
+    if (n > kDecMaxCand || k > min(kDecWarps, E)) {
+        dec_topk_warp<kDecMaxExperts / 32>(l, E, k, s_ids, lane);
+        return;
+    }
+    const uint64_t c0 = lane < n ? s_cand[lane] : 0ull, c1 = 32 + lane < n ? s_cand[32 + lane] : 0ull;
+    int r0 = 0, r1 = 0;
+    for (int j = 0; j < n; j++) {
+        const uint64_t c = s_cand[j];
+        r0 += c > c0 ? 1 : 0;
+        r1 += c > c1 ? 1 : 0;
+    }
+    if (lane < n && r0 < k) s_ids[r0] = (int32_t) ~(uint32_t) c0;
+    if (32 + lane < n && r1 < k) s_ids[r1] = (int32_t) ~(uint32_t) c1;
+}
+
+// route_warp's sum of the softmax terms, by one warp: lane j adds p[j + 32 i] in i order, then the xor butterfly
+__device__ __forceinline__ double dec_softmax_sum(const double* s_p, int E, int lane) {
+    double part = 0.0;
+    for (int e = lane; e < E; e += 32) part += s_p[e];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    return part;
 }
 
 // route_warp's weights for the ranked ids, by one warp: w_i = (float)((double)(float)(p_i / sum) / max(sum of the
@@ -329,6 +379,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_stack_kernel(const __gr
     __shared__ double s_den;
     __shared__ float s_sig;
     __shared__ double s_sum;
+    __shared__ uint64_t s_gmax[kDecWarps];
+    __shared__ uint64_t s_cand[kDecMaxCand];
+    __shared__ int s_cnt;
     __shared__ __align__(8) uint64_t s_mb[2];  // bulk copies: [0] this CTA's routed items, [1] its down rows
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int H = a.H, F = a.F, E = a.E, K = a.k;
@@ -393,15 +446,21 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_stack_kernel(const __gr
         cp_commit();
         cp_wait<0>();
         __syncthreads();
-        // warp 0 ranks; the others form the softmax terms and the shared gate meanwhile
+        // routing: candidates by the whole CTA, then warp 0 ranks them while warp 1 sums the softmax terms
+        uint64_t rv;
+        if (threadIdx.x == 0) s_cnt = (K <= min(kDecWarps, E)) ? 0 : kDecMaxCand + 1;
+        dec_route_step1(s.logits, E, rv, s_gmax, s_red);
+        __syncthreads();
+        dec_route_step2(s.logits, E, K, rv, s_gmax, s_red, s_cand, &s_cnt, s.p);
+        __syncthreads();
         if (warp == 0) {
-            dec_topk_warp<kDecMaxExperts / 32>(s.logits, E, K, s_ids, lane);
-        } else {
-            if (threadIdx.x == 32 && a.has_shared) {
-                const float e = (float) exp(-(double) s.logits[E]);
-                s_sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
-            }
-            dec_softmax_terms(s.logits, E, s.p, s_red, &s_sum);
+            dec_rank_candidates(s.logits, E, K, s_cnt, s_cand, s_ids, lane);
+        } else if (warp == 1) {
+            const double sum = dec_softmax_sum(s.p, E, lane);
+            if (lane == 0) s_sum = sum;
+        } else if (threadIdx.x == 64 && a.has_shared) {
+            const float e = (float) exp(-(double) s.logits[E]);
+            s_sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
         }
         __syncthreads();
         // this CTA's routed items and its down rows of every slot: bulk copies issued by warp 0's lanes, completing on

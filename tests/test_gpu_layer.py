@@ -157,20 +157,27 @@ def test_fused_single_token_equals_simt(cuda, shared):
     assert np.array_equal(bits(a), bits(b))
 
 
-@pytest.mark.parametrize("router", ["pairs", "zero"])
-def test_fused_single_token_ties(cuda, router):
-    # equal logits: the fused kernel's ranking keeps the lower expert index first, as the router kernel does
+@pytest.mark.parametrize("router,E,k", [("pairs", 512, 10), ("zero", 512, 10), ("groups", 512, 10),
+                                        ("random", 64, 20), ("random", 12, 12), ("random", 512, 16)])
+def test_fused_single_token_ties(cuda, router, E, k):
+    # the fused kernel's routing equals the router kernel's, ties included (lower expert index first): equal
+    # rows in pairs, an all-zero router, 288 keys above the threshold (experts e mod 16 < 9 far above the rest:
+    # the whole-key fallback), k above sixteen, fewer experts than warps
     import ctypes as C
 
     from stratametal_b200 import _lib
-    spec = synth.LayerSpec(n_embd=512, n_ff=128, n_expert=512, k=10, seed=52)
+    spec = synth.LayerSpec(n_embd=512, n_ff=128, n_expert=E, k=k, seed=52)
     lay = synth.make_layer(spec, 0, cuda)
     r = lay.tensors["ffn_gate_inp.weight"]
+    x = synth.make_x(6, 1, 512, cuda)
     if router == "pairs":  # experts 2 i and 2 i + 1 share a router row
         r.view(256, 2, -1)[:, 1].copy_(r.view(256, 2, -1)[:, 0])
-    else:
+    elif router == "zero":
         r.zero_()
-    x = synth.make_x(6, 1, 512, cuda)
+    elif router == "groups":  # row e = s_e x: logits s_e |x|^2, s_e = 2 + e / 1000 when e mod 16 < 9, else e / 1000
+        e = torch.arange(E, device=cuda, dtype=torch.float32)
+        sc = torch.where(e % 16 < 9, 2 + e / 1000, e / 1000)
+        r.copy_(synth.bf16_bits(sc[:, None] * x.view(1, -1)).view(r.dtype))
     outs = []
     try:
         for path in (3, 1):
@@ -189,7 +196,9 @@ def test_fused_single_token_ties(cuda, router):
     ids = ia.reshape(-1)
     if router == "zero":
         assert list(ids) == list(range(10))
-    else:  # both experts of a tied pair, the even one first
+    elif router == "pairs":  # both experts of a tied pair, the even one first
         assert all(ids[i] % 2 == 0 and ids[i + 1] == ids[i] + 1 for i in range(0, 10, 2))
+    elif router == "groups":
+        assert all(i % 16 < 9 for i in ids)
     assert np.array_equal(ia, ib) and np.array_equal(bits(wa), bits(wb))
     assert np.array_equal(bits(a), bits(b))
