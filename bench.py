@@ -537,7 +537,7 @@ def measure(args, ws, rank, local, clk, cfg, T_req, rot):
         expert_gbs = (D_mean + 1) * E_BYTES / (ms_step * 1e-3) / 1e9
         kos = KERNEL_OF_STAGE_TC if tc else KERNEL_OF_STAGE_TQ if tq else KERNEL_OF_STAGE
         if 2 <= T <= 64:
-            kos = dict(kos, router_gemv="router_gemm_kernel + router_reduce_kernel (split K)")
+            kos = dict(kos, router_gemv="router_gemm_kernel (split K; the top-k launch adds the partials)")
         kname = FUSED_KERNEL if fused else kos[dominant]
         if tc and dominant in ("expert_gate_up", "expert_down"):
             flops = flop_gu if dominant == "expert_gate_up" else flop_dn
@@ -584,9 +584,10 @@ def measure(args, ws, rank, local, clk, cfg, T_req, rot):
                   "D2H of the output"}
     assert api.device_status() == 0
 
-    # router (GEMV, or split-K GEMM + reduce from 2 to 64 tokens), top-k, grouping (3 launches above 256 tokens),
-    # gate/up, SwiGLU (SIMT only), down, combine; the fp16 tensor-core path adds the hi/lo image
-    router_l = 2 if 2 <= T <= 64 else 1
+    # router (GEMV, or split-K GEMM from 2 to 64 tokens, whose partials the top-k launch adds), top-k, grouping
+    # (3 launches above 256 tokens), gate/up, SwiGLU (SIMT only), down, combine; the fp16 tensor-core path adds the
+    # hi/lo image
+    router_l = 1
     group_l = 3 if T > 256 else 1
     if tc:
         per_fwd = router_l + 1 + 1 + group_l + 3

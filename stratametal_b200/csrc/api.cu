@@ -485,14 +485,17 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
         return ok();
     }
 
+    // 2 to 64 tokens: the split-K router GEMM's partials are added by the top-k launch (two launches, not three)
+    int splits = 0;
     cudaError_t e = launch_bf16_gemv(x, true, L->router, sh ? L->gate_inp_shexp : nullptr, logits, sh_logit, T, H,
-                                     E, s, base + lo.rsplit);
+                                     E, s, base + lo.rsplit, &splits);
+    const RouterSplit rsplit{reinterpret_cast<const double*>(base + lo.rsplit), splits, logits, sh ? sh_logit : nullptr};
     if (e == cudaSuccess) e = mark(0, s);
     if (e != cudaSuccess) return cuda_fail(e, "moe_forward: router");
     if (any_format(L)) {
         // any block format (iqx.cu): the q8_1 blocks of x, grouping, gate/up rows, SwiGLU + q8_1 of h, down rows;
         // the shared expert in launches of its own (its types may differ from the routed ones)
-        e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, nullptr, 0);
+        e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, nullptr, 0, &rsplit);
         if (e == cudaSuccess) e = mark(1, s);
         if (e != cudaSuccess) return cuda_fail(e, "moe_forward: top-k");
         e = launch_group(ids, T, K, E, tabs, slot, slot_tok, s, &sc, reinterpret_cast<int32_t*>(base + lo.chunk));
@@ -524,7 +527,7 @@ smoe_status smoe_moe_forward(const smoe_layer* L, const float* x, int n_tokens, 
     // read their own layouts (xa for the SIMT kernels, xh for the tensor-core kernels)
     const bool want_xq = trace && trace->xq;
     e = launch_router_topk(logits, T, E, K, ids, w, x, want_xq ? xq : nullptr, H, s, tc ? nullptr : &xa,
-                           L->gu_type == kQ2_0);
+                           L->gu_type == kQ2_0, &rsplit);
     __half* xh = reinterpret_cast<__half*>(base + lo.xh);
     if (e == cudaSuccess && tc) e = launch_quant_xh(x, T, H, xh, s);
     if (e == cudaSuccess) e = mark(1, s);
@@ -873,10 +876,13 @@ smoe_status smoe_ep_forward(const smoe_layer* L, const smoe_ep* ep, const float*
 
     if (phases & 1) {
         if (T > 0) {
+            int splits = 0;
             e = launch_bf16_gemv(x, true, L->router, sh ? L->gate_inp_shexp : nullptr, logits, sh_logit, T, H, E, s,
-                                 base + lo.rsplit);
+                                 base + lo.rsplit, &splits);
+            const RouterSplit rsplit{reinterpret_cast<const double*>(base + lo.rsplit), splits, logits,
+                                     sh ? sh_logit : nullptr};
             if (e == cudaSuccess) e = mark(0, s);
-            if (e == cudaSuccess) e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, nullptr, 1);
+            if (e == cudaSuccess) e = launch_router_topk(logits, T, E, K, ids, w, x, xq, H, s, nullptr, 1, &rsplit);
             if (e == cudaSuccess) e = mark(1, s);
             if (e != cudaSuccess) return cuda_fail(e, "ep_forward: router");
         }

@@ -32,12 +32,24 @@ inline KAct ka_at(void* base, int64_t rows, int nblk) {
 // ---- router.cu ----
 // split_scratch (router_split_bytes of it, 256-byte aligned): few-token f32 calls take the fp64 tensor-path GEMM
 // split over K instead of the GEMV, to fill the SMs.
+// With defer non-null, a split-K router GEMM leaves the sum of its partials to the top-k launch (*defer = the
+// number of splits, 0 when the GEMM wrote the logits itself).
 cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, const uint16_t* extra, float* y,
-                             float* y_extra, int T, int H, int n_out, cudaStream_t s, void* split_scratch = nullptr);
+                             float* y_extra, int T, int H, int n_out, cudaStream_t s, void* split_scratch = nullptr,
+                             int* defer = nullptr);
 size_t router_split_bytes(int T, int n_rows, int H);
+// The split-K partials of a deferred router GEMM: the top-k kernel adds them (in split order, as the reduce kernel
+// does) into lout [T][E] and y_extra [T] (the shared gate's logit, when the GEMM had that row) before it routes.
+struct RouterSplit {
+    const double* part;
+    int S;
+    float* lout;
+    float* y_extra;
+};
 // xa (optional): the activation in the expert kernels' layout, permuted for Q2_0 gate/up when xa_q2 != 0.
 cudaError_t launch_router_topk(const float* logits, int T, int E, int k, int32_t* ids, float* w, const float* x,
-                               uint8_t* xq, int H, cudaStream_t s, const KAct* xa = nullptr, int xa_q2 = 1);
+                               uint8_t* xq, int H, cudaStream_t s, const KAct* xa = nullptr, int xa_q2 = 1,
+                               const RouterSplit* split = nullptr);
 cudaError_t launch_quant_q8_1(const float* x, int64_t n, uint8_t* y, cudaStream_t s);
 cudaError_t launch_swiglu_q8(const float* g, const float* u, int64_t n, uint8_t* y, cudaStream_t s);
 cudaError_t launch_f32_to_bf16(const float* x, uint16_t* y, int64_t n, cudaStream_t s);

@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const floa
                                                                       float* __restrict__ wout,
                                                                       const float* __restrict__ x,
                                                                       uint8_t* __restrict__ xq, int H, KAct xa,
-                                                                      int xa_q2) {
+                                                                      int xa_q2, RouterSplit rs) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int tpc = topk_tokens_per_cta(T);
     const int route_blocks = (T + tpc - 1) / tpc;
@@ -412,7 +412,37 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const floa
         return;
     }
     const int t = blockIdx.x * tpc + warp;
-    if (warp < tpc && t < T) route_warp<PER_LANE>(logits + (size_t) t * E, E, k, ids + (size_t) t * k, wout + (size_t) t * k, lane);
+    const float* l = logits + (size_t) t * E;
+    if (rs.part) {
+        // the CTA's tokens' logits from the split-K partials, added in split order (router_reduce_kernel's sum), by
+        // all of its threads into shared memory (the routing warps read them there) and out to the logits and gate
+        // buffers
+        extern __shared__ float s_rl[];  // [tokens per CTA][E]
+        const int n_rows = E + (rs.y_extra ? 1 : 0);
+        const int t0 = blockIdx.x * tpc, nt = min(tpc, T - t0);
+        for (int i = threadIdx.x; i < nt * n_rows; i += kTopkWarps * 32) {
+            const int tt = t0 + i / n_rows, o = i % n_rows;
+            double v[32];
+#pragma unroll
+            for (int z = 0; z < 32; z++)
+                if (z < rs.S) v[z] = __ldg(rs.part + ((size_t) z * T + tt) * n_rows + o);
+            double acc = 0.0;
+#pragma unroll
+            for (int z = 0; z < 32; z++)
+                if (z < rs.S) acc += v[z];
+            const float f = (float) acc;
+            if (o < E) {
+                s_rl[(size_t) (i / n_rows) * E + o] = f;
+                rs.lout[(size_t) tt * E + o] = f;
+            } else {
+                rs.y_extra[tt] = f;
+            }
+        }
+        __syncthreads();
+        l = s_rl + (size_t) warp * E;
+    }
+    if (warp >= tpc || t >= T) return;
+    route_warp<PER_LANE>(l, E, k, ids + (size_t) t * k, wout + (size_t) t * k, lane);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -420,9 +450,11 @@ __global__ void __launch_bounds__(kTopkWarps * 32) router_topk_kernel(const floa
 // ------------------------------------------------------------------------------------------------
 
 cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, const uint16_t* extra, float* y,
-                             float* y_extra, int T, int H, int n_out, cudaStream_t s, void* split_scratch) {
+                             float* y_extra, int T, int H, int n_out, cudaStream_t s, void* split_scratch,
+                             int* defer) {
     const int n_rows = n_out + (extra ? 1 : 0);
     const int S = split_scratch ? router_splits(T, n_rows, H) : 1;
+    if (defer) *defer = 0;
     if (f32_in && H % kRgK == 0 && (T > kRouterGemmMinTokens || S > 1)) {
         const dim3 grid((n_rows + kRgRows - 1) / kRgRows, (T + kRgToks - 1) / kRgToks, S);
         cudaError_t err = cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -431,7 +463,8 @@ cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, cons
         double* part = S > 1 ? static_cast<double*>(split_scratch) : nullptr;
         router_gemm_kernel<<<grid, 256, kRgSmem, s>>>(static_cast<const float*>(x), w, extra, y, y_extra, T, H,
                                                       n_out, part);
-        if (S > 1) router_reduce_kernel<<<(T * n_rows + 255) / 256, 256, 0, s>>>(part, S, T, n_rows, n_out, y, y_extra);
+        if (S > 1 && defer) *defer = S;
+        else if (S > 1) router_reduce_kernel<<<(T * n_rows + 255) / 256, 256, 0, s>>>(part, S, T, n_rows, n_out, y, y_extra);
         return cudaGetLastError();
     }
     const size_t smem = (size_t) kRouterTokTile * H * 2;
@@ -459,13 +492,16 @@ cudaError_t launch_bf16_gemv(const void* x, bool f32_in, const uint16_t* w, cons
 }
 
 cudaError_t launch_router_topk(const float* logits, int T, int E, int k, int32_t* ids, float* w, const float* x,
-                               uint8_t* xq, int H, cudaStream_t s, const KAct* xa, int xa_q2) {
+                               uint8_t* xq, int H, cudaStream_t s, const KAct* xa, int xa_q2, const RouterSplit* split) {
     int blocks = (T + topk_tokens_per_cta(T) - 1) / topk_tokens_per_cta(T);
     if (xq || xa) blocks += (int) std::min<int64_t>(((int64_t) T * (H / 32) + kTopkWarps - 1) / kTopkWarps, 148 * 8);
     const KAct a = xa ? *xa : KAct{};
-    if (E <= 256) router_topk_kernel<8><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);
-    else if (E <= 512) router_topk_kernel<16><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);
-    else router_topk_kernel<32><<<blocks, kTopkWarps * 32, 0, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2);
+    const RouterSplit rs = split && split->S > 1 ? *split : RouterSplit{};
+    if (rs.part && rs.S > 32) return cudaErrorInvalidValue;
+    const size_t smem = rs.part ? (size_t) topk_tokens_per_cta(T) * E * sizeof(float) : 0;
+    if (E <= 256) router_topk_kernel<8><<<blocks, kTopkWarps * 32, smem, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2, rs);
+    else if (E <= 512) router_topk_kernel<16><<<blocks, kTopkWarps * 32, smem, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2, rs);
+    else router_topk_kernel<32><<<blocks, kTopkWarps * 32, smem, s>>>(logits, T, E, k, ids, w, x, xq, H, a, xa_q2, rs);
     return cudaGetLastError();
 }
 
