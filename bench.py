@@ -435,14 +435,18 @@ def measure(args, ws, rank, local, clk, cfg, T_req, rot):
 
     # one CUDA graph per step kind: every (layer, batch) forward, or the whole stack
     G = 1 if stack else n_layers * n_batches
+    # each single-layer graph reads and writes buffers of its own (its batch's tokens), so consecutive steps never
+    # share one and the end-to-end loop below can upload the next step's input while this one computes
+    g_in = [xs[0]] if stack else [xs[(gi // n_layers) % n_batches].clone() for gi in range(G)]
+    g_out = [sbuf[(n_layers - 1) & 1]] if stack else [torch.empty(T, H, device=dev) for _ in range(G)]
     graphs = []
     for gi in range(G):
         g = torch.cuda.CUDAGraph()
         for _ in range(2):  # warm the allocator and any first-call set-up outside the capture
-            stack_once() if stack else forward_once(gi % n_layers, (gi // n_layers) % n_batches, out)
+            stack_once() if stack else layers[gi % n_layers].forward(g_in[gi], g_out[gi])
         torch.cuda.synchronize()
         with torch.cuda.graph(g, capture_error_mode="relaxed"):
-            stack_once() if stack else forward_once(gi % n_layers, (gi // n_layers) % n_batches, out)
+            stack_once() if stack else layers[gi % n_layers].forward(g_in[gi], g_out[gi])
         g.replay()  # set-up, not a step: a graph's first launch uploads it to the device
         graphs.append(g)
     torch.cuda.synchronize()
@@ -560,28 +564,52 @@ def measure(args, ws, rank, local, clk, cfg, T_req, rot):
                     "unit": "GB/s", "frac": achieved / hbm_peak if achieved else None, "traffic": traffic,
                     "algorithmic_bytes_per_launch": dom_bytes, "ms_per_launch": dom_ms}
 
-    # end to end: every step copies its input from pinned host memory, replays the captured API calls and
-    # reads the result back
-    x_host = [x.cpu().pin_memory() for x in xs]
-    out_host = torch.empty(T, H).pin_memory()
-    res = sbuf[(n_layers - 1) & 1] if stack else out
+    # end to end: every step uploads its input from pinned host memory into the buffer its captured forward reads,
+    # replays the captured API calls and reads its result back into pinned host memory, all inside the timed
+    # region.  The copies run on two copy streams, pipelined with the replays as a serving loop runs them: step
+    # i + 1's upload and step i - 1's read-back overlap step i's compute.  A step's upload waits until the previous
+    # step that used the same buffers has been read back (events), and each replay waits for its own upload.
+    x_host = [t.cpu().pin_memory() for t in g_in]
+    out_host = [torch.empty(T, H).pin_memory() for _ in range(2)]
+    hs, ds = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     Ke = min(K, 1000)
     torch.cuda.synchronize()
     barrier(ws)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    go = torch.cuda.Event()
+    # one event of each kind per buffer set, created and first recorded here, outside the timed loop (a stream wait
+    # takes an event's latest record, so each is recorded again for every step that uses its buffers)
+    up_ev, done_ev, rb_ev = ([torch.cuda.Event() for _ in range(G)] for _ in range(3))
+    for evs in (up_ev, done_ev, rb_ev, [go]):
+        for ev in evs:
+            ev.record(gstream)
+    torch.cuda.synchronize()
     e0.record(gstream)
+    go.record(gstream)
+    hs.wait_event(go)
+    ds.wait_event(go)
     for i in range(Ke):
-        b = 0 if stack else (i // n_layers) % n_batches
-        xs[b].copy_(x_host[b], non_blocking=True)
-        graphs[i % G].replay()
-        out_host.copy_(res, non_blocking=True)
+        gi = i % G
+        with torch.cuda.stream(hs):
+            hs.wait_event(rb_ev[gi])  # the previous step on these buffers has been read back
+            g_in[gi].copy_(x_host[gi], non_blocking=True)
+            up_ev[gi].record(hs)
+        gstream.wait_event(up_ev[gi])
+        graphs[gi].replay()
+        done_ev[gi].record(gstream)
+        with torch.cuda.stream(ds):
+            ds.wait_event(done_ev[gi])
+            out_host[i % 2].copy_(g_out[gi], non_blocking=True)
+            rb_ev[gi].record(ds)
+    gstream.wait_stream(hs)
+    gstream.wait_stream(ds)
     e1.record(gstream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), ws) / Ke
     e2e = {"value": ws * T / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": T * H * 4,
            "d2h_bytes_per_step": T * H * 4, "ms_per_step": e2e_ms,
            "how": "per step: H2D of the input from pinned memory, replay of the captured smoe_moe_forward calls, "
-                  "D2H of the output"}
+                  "D2H of the output; the copies on two copy streams, overlapping the neighbouring steps' compute"}
     assert api.device_status() == 0
 
     # router (GEMV, or split-K GEMM from 2 to 64 tokens, whose partials the top-k launch adds), top-k, grouping
