@@ -310,7 +310,8 @@ void smoe_gguf_free_layer(void* owner);
  * x = rms_norm_weighted(MoE_l(x) + x, norm_w[l]) for l = 0 .. n_layers - 1 (eps; norm_w NULL or any entry NULL: unit
  * weight), out = the last x.  Equals n_layers calls of smoe_moe_forward each followed by smoe_add_rms_norm, bit for
  * bit, in one persistent cooperative launch per 48 layers.  Every layer: one geometry, every matrix Q2_0, n_embd a
- * multiple of 512, n_ff a multiple of 128 (SMOE_UNSUPPORTED otherwise).  x and out may be the same buffer. */
+ * multiple of 512 up to 4096, n_ff a multiple of 128 up to 1024, n_expert at most 512 (the rule of path 3;
+ * SMOE_UNSUPPORTED otherwise).  x and out may be the same buffer. */
 size_t smoe_stack_decode_scratch_bytes(const smoe_layer* L);
 smoe_status smoe_stack_decode(const smoe_layer* layers, int n_layers, const float* const* norm_w, float eps,
                               const float* x, float* out, void* scratch, size_t scratch_bytes, void* stream);
