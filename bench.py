@@ -588,7 +588,29 @@ def measure(args, ws, rank, local, clk, cfg, T_req, rot):
     go.record(gstream)
     hs.wait_event(go)
     ds.wait_event(go)
-    for i in range(Ke):
+    drv = _driver_calls(graphs)
+    if drv is not None:  # the same operations through the driver API, so the Python loop stays off the critical path
+        d, execs = drv
+        gs_h, hs_h, ds_h = gstream.cuda_stream, hs.cuda_stream, ds.cuda_stream
+        up_h, done_h, rb_h = ([e.cuda_event for e in evs] for evs in (up_ev, done_ev, rb_ev))
+        nbytes = T * H * 4
+        in_p, out_p = [t.data_ptr() for t in g_in], [t.data_ptr() for t in g_out]
+        xh_p, oh_p = [t.data_ptr() for t in x_host], [t.data_ptr() for t in out_host]
+        bad = 0
+        for i in range(Ke):
+            gi = i % G
+            bad |= d.cuStreamWaitEvent(hs_h, rb_h[gi], 0)
+            bad |= d.cuMemcpyHtoDAsync_v2(in_p[gi], xh_p[gi], nbytes, hs_h)
+            bad |= d.cuEventRecord(up_h[gi], hs_h)
+            bad |= d.cuStreamWaitEvent(gs_h, up_h[gi], 0)
+            bad |= d.cuGraphLaunch(execs[gi], gs_h)
+            bad |= d.cuEventRecord(done_h[gi], gs_h)
+            bad |= d.cuStreamWaitEvent(ds_h, done_h[gi], 0)
+            bad |= d.cuMemcpyDtoHAsync_v2(oh_p[i % 2], out_p[gi], nbytes, ds_h)
+            bad |= d.cuEventRecord(rb_h[gi], ds_h)
+        if bad:
+            raise RuntimeError("end-to-end loop: a CUDA driver call failed")
+    for i in range(Ke if drv is None else 0):
         gi = i % G
         with torch.cuda.stream(hs):
             hs.wait_event(rb_ev[gi])  # the previous step on these buffers has been read back
@@ -709,6 +731,29 @@ def run_ours(args, ws, rank, local):
         if subs:
             line["configs"] = {name: public(r) for name, r in subs.items()}
         print(json.dumps(line), flush=True)
+
+
+def _driver_calls(graphs):
+    """The CUDA driver entry points the end-to-end loop issues (through ctypes) and the graphs' executable handles,
+    or None when either is unavailable (the loop then goes through torch)."""
+    import ctypes as C
+    try:
+        d = C.CDLL("libcuda.so.1")
+        execs = [g.raw_cuda_graph_exec() for g in graphs]
+    except (OSError, AttributeError, RuntimeError):
+        return None
+    if any(not isinstance(e, int) or not e for e in execs):
+        return None
+    sig = {"cuStreamWaitEvent": [C.c_void_p, C.c_void_p, C.c_uint],
+           "cuMemcpyHtoDAsync_v2": [C.c_uint64, C.c_void_p, C.c_size_t, C.c_void_p],
+           "cuMemcpyDtoHAsync_v2": [C.c_void_p, C.c_uint64, C.c_size_t, C.c_void_p],
+           "cuEventRecord": [C.c_void_p, C.c_void_p],
+           "cuGraphLaunch": [C.c_void_p, C.c_void_p]}
+    for name, args in sig.items():
+        f = getattr(d, name)
+        f.argtypes = args
+        f.restype = C.c_int
+    return d, execs
 
 
 def main():
